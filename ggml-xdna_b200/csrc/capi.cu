@@ -1,0 +1,446 @@
+// The C ABI of libzest_b200.so (include/zest_b200.h): the stream-level
+// kernel entry points and the matmul service zest_npu, the counterpart of
+// the reference's xdna_npu (src/xdna-npu.{h,cpp}).
+#include "zest_b200.h"
+#include "zest_device.cuh"
+#include "zest_internal.h"
+
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+namespace zest {
+
+static thread_local std::string g_err;
+
+int set_error(const char *msg) {
+    g_err = msg;
+    return -1;
+}
+
+int check_launch(const char *what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return 0;
+    g_err = std::string(what) + ": " + cudaGetErrorString(e);
+    return -1;
+}
+
+// The IQ3_S codebook, kept on the host so every device that converts IQ3_S
+// weights gets a copy (a __device__ symbol exists once per device).
+static std::mutex g_grid_mu;
+static std::vector<uint32_t> g_grid_host;
+static uint64_t g_grid_devices = 0;  // bit d: loaded on device d
+
+bool iq3s_grid_loaded() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lk(g_grid_mu);
+    if (dev < 64 && (g_grid_devices >> dev) & 1) return true;
+    if (g_grid_host.empty()) return false;
+    if (set_iq3s_grid(g_grid_host.data())) return false;
+    if (dev < 64) g_grid_devices |= 1ull << dev;
+    return true;
+}
+
+// Environment knobs read once; empty means unset (src/xdna-env.h:9-17).
+static long long env_ll(const char *name, long long def) {
+    const char *s = getenv(name);
+    return s && *s ? atoll(s) : def;
+}
+
+// Flags every result non-finite: the fault-injection counterpart of the
+// NPU's damaged results (GGML_XDNA_NAN_AFTER, src/xdna-npu.cpp:102-112).
+__global__ void check_finite_kernel(const float *y, int64_t n, unsigned *err) {
+    uint32_t bad = 0;
+    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x)
+        bad |= (__float_as_uint(y[i]) & 0x7f800000u) == 0x7f800000u;
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x % 32) == 0) atomicOr(err, ERR_NOT_FINITE);
+}
+
+}  // namespace zest
+
+using namespace zest;
+
+extern "C" {
+
+int zest_version(void) { return ZEST_B200_VERSION; }
+
+const char *zest_last_error(void) { return g_err.c_str(); }
+
+int zest_load_iq3s_grid(const uint32_t *grid512) {
+    if (!grid512) return set_error("zest_load_iq3s_grid: no table");
+    std::lock_guard<std::mutex> lk(g_grid_mu);
+    g_grid_host.assign(grid512, grid512 + 512);
+    g_grid_devices = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return set_error("zest_load_iq3s_grid: no CUDA device");
+    if (set_iq3s_grid(grid512)) return -1;
+    if (dev < 64) g_grid_devices |= 1ull << dev;
+    return 0;
+}
+
+int zest_pack_activations(const float *x, int64_t T, int64_t K, int64_t ldx, int64_t m_pad, uint8_t *a_bfp16,
+                          uint16_t *a_bf16, int64_t ld_bf16, void *stream) {
+    return launch_pack_activations(x, T, K, ldx, m_pad, a_bfp16, a_bf16, ld_bf16, (cudaStream_t) stream);
+}
+
+int zest_convert_weight(int type, const void *raw, int64_t rows_total, int64_t row0, int64_t N, int64_t K,
+                        int64_t n_pad, uint8_t *b_bfp16, uint16_t *b_bf16, void *stream) {
+    if (row0 < 0 || N < 0 || row0 + N > rows_total) return set_error("zest_convert_weight: rows out of range");
+    return launch_convert_weight(type, raw, raw, 0, N, row0, rows_total, K, n_pad, b_bfp16, b_bf16,
+                                 (cudaStream_t) stream);
+}
+
+int zest_convert_gate_up(int type, const void *gate, const void *up, int64_t rows_total, int64_t row0, int64_t F,
+                         int64_t K, int64_t f_pad, uint8_t *b_bfp16, uint16_t *b_bf16, void *stream) {
+    if (row0 < 0 || F < 0 || row0 + F > rows_total || f_pad % 256 || f_pad < F)
+        return set_error("zest_convert_gate_up: rows out of range or f_pad not a multiple of 256");
+    return launch_convert_weight(type, gate, up, 1, F, row0, rows_total, K, 2 * f_pad, b_bfp16, b_bf16,
+                                 (cudaStream_t) stream);
+}
+
+int zest_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
+              int64_t K, int mode, float *c, int64_t ldc, unsigned *err, void *stream) {
+    return launch_gemm(a_bf16, lda, b_bf16, ldb, M, N, K, mode, c, ldc, err, (cudaStream_t) stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// the matmul service
+// ---------------------------------------------------------------------------
+
+struct zest_npu {
+    struct weight {
+        uint8_t *bytes = nullptr;   // bfp16 B operand, reference layout
+        uint16_t *bf16 = nullptr;   // [n_pad][K]
+        int64_t K = 0, N = 0, n_pad = 0, n_out = 0;
+        int mode = 0;
+    };
+    using key_t = std::tuple<const void *, const void *, int, int64_t, int64_t, int>;
+
+    int device = 0;
+    cudaStream_t st = nullptr;
+    bool out16 = true;
+    std::map<key_t, weight> weights;
+    // per-call workspace; grows only
+    float *x_dev = nullptr, *y_dev = nullptr;
+    uint16_t *a_bf16 = nullptr;
+    size_t x_cap = 0, y_cap = 0, a_cap = 0;
+    unsigned *err_dev = nullptr, *err_host = nullptr;
+    cudaEvent_t ev[5] = {};
+    zest_times times = {};
+    long long submissions = 0;
+
+    ~zest_npu() {
+        cudaSetDevice(device);
+        if (st) cudaStreamSynchronize(st);
+        for (auto &kv : weights) {
+            cudaFree(kv.second.bytes);
+            cudaFree(kv.second.bf16);
+        }
+        cudaFree(x_dev);
+        cudaFree(y_dev);
+        cudaFree(a_bf16);
+        cudaFree(err_dev);
+        if (err_host) cudaFreeHost(err_host);
+        for (cudaEvent_t e : ev)
+            if (e) cudaEventDestroy(e);
+        if (st) cudaStreamDestroy(st);
+    }
+
+    static key_t key_of(const zest_wkey *k, int fused) { return key_t(k->buffer, k->data, k->type, k->K, k->N, fused); }
+
+    const weight *find(const zest_wkey *k, int fused) const {
+        auto it = weights.find(key_of(k, fused));
+        return it == weights.end() ? nullptr : &it->second;
+    }
+};
+
+namespace zest {
+
+static bool grow(void **p, size_t *cap, size_t need) {
+    if (need <= *cap) return true;
+    cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    if (cudaMalloc(p, need) != cudaSuccess) return false;
+    *cap = need;
+    return true;
+}
+
+// GGML_XDNA_FAIL_AFTER=n: every submission after the n-th fails, to test the
+// caller's failure path (src/xdna-npu.cpp:89-100).
+static bool injected_failure() {
+    static const long long after = env_ll("GGML_XDNA_FAIL_AFTER", -1);
+    static std::atomic<long long> n{ 0 };
+    return after >= 0 && ++n > after;
+}
+
+// GGML_XDNA_NAN_AFTER=n: every result after the n-th submission comes back
+// NaN, to test that such results are caught (src/xdna-npu.cpp:102-112).
+static bool injected_nan() {
+    static const long long after = env_ll("GGML_XDNA_NAN_AFTER", -1);
+    static std::atomic<long long> n{ 0 };
+    return after >= 0 && ++n > after;
+}
+
+static int cuda_fail(const char *what, cudaError_t e) {
+    g_err = std::string(what) + ": " + cudaGetErrorString(e);
+    return -1;
+}
+
+static int add_copy(zest_npu *npu, const zest_wkey *key, const void *raw0, const void *raw1, int raw_on_device,
+                    int fused) {
+    if (!npu || !key) return set_error("zest_add_weight: no service or key");
+    if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_add_weight: cannot select the device");
+    const int64_t K = key->K, N = key->N;
+    int64_t row_bytes = 0;
+    switch (key->type) {
+        case TYPE_F32: row_bytes = K * 4; break;
+        case TYPE_F16: row_bytes = K * 2; break;
+        case TYPE_Q8_0: row_bytes = K / 32 * 34; break;
+        case TYPE_Q4_K: row_bytes = K / 256 * 144; break;
+        case TYPE_Q6_K: row_bytes = K / 256 * 210; break;
+        case TYPE_IQ3_S: row_bytes = K / 256 * 110; break;
+        default: return set_error("zest_add_weight: unsupported weight type");
+    }
+    zest_npu::weight w;
+    w.K = K;
+    w.N = N;
+    w.n_out = N;
+    w.n_pad = fused ? 2 * ((N + 255) / 256 * 256) : (N + 511) / 512 * 512;  // pad_f / pad_n (xdna-npu.cpp:46-47)
+    w.mode = fused ? MODE_SWIGLU : (npu->out16 ? MODE_BF16 : MODE_F32);
+    const size_t raw_bytes = (size_t) (row_bytes * N);
+    const void *src0 = raw0, *src1 = raw1;
+    void *staged[2] = { nullptr, nullptr };
+    cudaEvent_t t0 = npu->ev[0], t1 = npu->ev[1];
+    cudaEventRecord(t0, npu->st);
+    if (!raw_on_device) {
+        for (int i = 0; i < (fused ? 2 : 1); i++) {
+            cudaError_t e = cudaMalloc(&staged[i], raw_bytes ? raw_bytes : 16);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(staged[i], i ? raw1 : raw0, raw_bytes, cudaMemcpyHostToDevice, npu->st);
+            if (e != cudaSuccess) {
+                cudaFree(staged[0]);
+                cudaFree(staged[1]);
+                return cuda_fail("zest_add_weight: staging the raw weight", e);
+            }
+        }
+        src0 = staged[0];
+        src1 = staged[1];
+    }
+    cudaError_t e = cudaMalloc(&w.bytes, (size_t) (w.n_pad * K / 8 * BLOCK_BYTES));
+    if (e == cudaSuccess) e = cudaMalloc(&w.bf16, (size_t) (w.n_pad * K) * 2);
+    int rc = e == cudaSuccess ? 0 : cuda_fail("zest_add_weight: allocating the weight copy", e);
+    if (!rc)
+        rc = fused ? launch_convert_weight(key->type, src0, src1, 1, N, 0, N, K, w.n_pad, w.bytes, w.bf16, npu->st)
+                   : launch_convert_weight(key->type, src0, src0, 0, N, 0, N, K, w.n_pad, w.bytes, w.bf16, npu->st);
+    cudaEventRecord(t1, npu->st);
+    e = cudaStreamSynchronize(npu->st);
+    if (!rc && e != cudaSuccess) rc = cuda_fail("zest_add_weight", e);
+    cudaFree(staged[0]);
+    cudaFree(staged[1]);
+    if (rc) {
+        cudaFree(w.bytes);
+        cudaFree(w.bf16);
+        return rc;
+    }
+    float ms = 0;
+    cudaEventElapsedTime(&ms, t0, t1);
+    npu->times.pack_ms += ms;
+    auto k = zest_npu::key_of(key, fused);
+    auto old = npu->weights.find(k);
+    if (old != npu->weights.end()) {
+        cudaFree(old->second.bytes);
+        cudaFree(old->second.bf16);
+    }
+    npu->weights[k] = w;
+    return 0;
+}
+
+// One exact integer multiply through all three kernels, checked against the
+// host (npu_self_test, src/xdna-npu.cpp:136-184): small whole numbers that
+// bfp16 holds exactly and fp32 sums add exactly, so every answer must match.
+static std::string self_test(int device) {
+    constexpr int64_t M = 512, K = 128, N = 512;
+    std::vector<int8_t> ai((size_t) (M * K)), wi((size_t) (N * K));
+    uint32_t seed = 1;
+    auto next = [&](int span) {
+        seed = seed * 1664525u + 1013904223u;
+        return (int8_t) ((int) (seed >> 24) % span - span / 2);
+    };
+    for (int8_t &v : ai) v = next(5);
+    for (int8_t &v : wi) v = next(7);
+    std::vector<float> a(ai.begin(), ai.end()), w(wi.begin(), wi.end()), c((size_t) (M * N));
+    zest_npu *npu = zest_open(device);
+    if (!npu) return std::string("cannot open the GPU (") + g_err + ")";
+    zest_set_out16(npu, 0);
+    const zest_wkey key = { nullptr, w.data(), TYPE_F32, K, N };
+    std::string why;
+    if (zest_add_weight(npu, &key, w.data(), 0) || zest_mul_mat(npu, &key, 0, a.data(), M, c.data(), 0)) {
+        why = "a test multiply failed (" + g_err + ")";
+    } else {
+        for (int64_t r = 0; r < M && why.empty(); r++)
+            for (int64_t n = 0; n < N; n++) {
+                int want = 0;
+                for (int64_t k = 0; k < K; k++) want += ai[r * K + k] * wi[n * K + k];
+                if (c[r * N + n] != (float) want) {
+                    char where[128];
+                    snprintf(where, sizeof(where), "a test multiply came out wrong (row %lld, column %lld: %g, not %d)",
+                             (long long) r, (long long) n, c[r * N + n], want);
+                    why = where;
+                    break;
+                }
+            }
+    }
+    zest_close(npu);
+    return why;
+}
+
+}  // namespace zest
+
+extern "C" {
+
+zest_npu *zest_open(int device) {
+    if (cudaSetDevice(device) != cudaSuccess) {
+        set_error("zest_open: no such CUDA device");
+        return nullptr;
+    }
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (major != 10 || minor != 0) {
+        set_error("zest_open: this build runs on sm_100 (B200) only");
+        return nullptr;
+    }
+    auto *npu = new zest_npu;
+    npu->device = device;
+    npu->out16 = env_ll("GGML_XDNA_OUT16", 1) != 0;
+    cudaError_t e = cudaStreamCreateWithFlags(&npu->st, cudaStreamNonBlocking);
+    for (cudaEvent_t &ev : npu->ev)
+        if (e == cudaSuccess) e = cudaEventCreate(&ev);
+    if (e == cudaSuccess) e = cudaMalloc(&npu->err_dev, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMallocHost(&npu->err_host, sizeof(unsigned));
+    if (e != cudaSuccess) {
+        cuda_fail("zest_open", e);
+        delete npu;
+        return nullptr;
+    }
+    return npu;
+}
+
+void zest_close(zest_npu *npu) { delete npu; }
+
+void zest_set_out16(zest_npu *npu, int on) {
+    if (npu) npu->out16 = on != 0;
+}
+
+int zest_usable(int device, char *why, size_t why_len) {
+    static std::mutex mu;
+    static std::map<int, std::string> verdict;  // "" = usable
+    std::string v;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = verdict.find(device);
+        if (it == verdict.end()) it = verdict.emplace(device, self_test(device)).first;
+        v = it->second;
+    }
+    const std::string said = v.empty() ? "B200 self-test multiply right" : v;
+    if (why && why_len) snprintf(why, why_len, "%s", said.c_str());
+    if (!v.empty()) return set_error(v.c_str());
+    return 0;
+}
+
+int zest_has_weight(const zest_npu *npu, const zest_wkey *key) {
+    return npu && key && (npu->find(key, 0) || npu->find(key, 1)) ? 1 : 0;
+}
+
+int zest_add_weight(zest_npu *npu, const zest_wkey *key, const void *raw, int raw_on_device) {
+    return add_copy(npu, key, raw, raw, raw_on_device, 0);
+}
+
+int zest_add_fused(zest_npu *npu, const zest_wkey *gate, const void *gate_raw, const void *up_raw, int raw_on_device) {
+    return add_copy(npu, gate, gate_raw, up_raw, raw_on_device, 1);
+}
+
+int64_t zest_out_width(const zest_npu *npu, const zest_wkey *key, int fused) {
+    const zest_npu::weight *w = npu && key ? npu->find(key, fused) : nullptr;
+    return w ? w->n_out : -1;
+}
+
+const uint8_t *zest_weight_bfp16(const zest_npu *npu, const zest_wkey *key, int fused) {
+    const zest_npu::weight *w = npu && key ? npu->find(key, fused) : nullptr;
+    return w ? w->bytes : nullptr;
+}
+
+const uint16_t *zest_weight_bf16(const zest_npu *npu, const zest_wkey *key, int fused, int64_t *n_pad) {
+    const zest_npu::weight *w = npu && key ? npu->find(key, fused) : nullptr;
+    if (w && n_pad) *n_pad = w->n_pad;
+    return w ? w->bf16 : nullptr;
+}
+
+void *zest_stream(zest_npu *npu) { return npu ? (void *) npu->st : nullptr; }
+
+int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x, int64_t T, float *y, int on_device) {
+    if (!npu || !key) return set_error("zest_mul_mat: no service or key");
+    const zest_npu::weight *w = npu->find(key, fused);
+    if (!w) return set_error("zest_mul_mat: weight not added");
+    if (T <= 0) return 0;
+    if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_mul_mat: cannot select the device");
+    if (injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
+    const int64_t K = w->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
+    const size_t x_bytes = (size_t) (T * K) * 4, y_bytes = (size_t) (T * w->n_out) * 4;
+    if (!grow((void **) &npu->a_bf16, &npu->a_cap, (size_t) (m_pad * K) * 2) ||
+        (!on_device && (!grow((void **) &npu->x_dev, &npu->x_cap, x_bytes) ||
+                        !grow((void **) &npu->y_dev, &npu->y_cap, y_bytes))))
+        return set_error("zest_mul_mat: out of GPU memory for the call's buffers");
+    cudaStream_t st = npu->st;
+    const float *xd = on_device ? x : npu->x_dev;
+    float *yd = on_device ? y : npu->y_dev;
+    cudaEventRecord(npu->ev[0], st);
+    if (!on_device) cudaMemcpyAsync(npu->x_dev, x, x_bytes, cudaMemcpyHostToDevice, st);
+    cudaMemsetAsync(npu->err_dev, 0, sizeof(unsigned), st);
+    cudaEventRecord(npu->ev[1], st);
+    int rc = launch_pack_activations(xd, T, K, K, m_pad, nullptr, npu->a_bf16, K, st);
+    cudaEventRecord(npu->ev[2], st);
+    if (!rc) rc = launch_gemm(npu->a_bf16, K, w->bf16, K, T, w->n_pad, K, w->mode, yd, w->n_out, npu->err_dev, st);
+    if (!rc && injected_nan()) {
+        cudaMemsetAsync(yd, 0xff, y_bytes, st);
+        check_finite_kernel<<<148, 256, 0, st>>>(yd, T * w->n_out, npu->err_dev);
+    }
+    cudaEventRecord(npu->ev[3], st);
+    if (!on_device) cudaMemcpyAsync(y, npu->y_dev, y_bytes, cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(npu->err_host, npu->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
+    cudaEventRecord(npu->ev[4], st);
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail("zest_mul_mat", e);
+    float a = 0, b = 0, c = 0, d = 0;
+    cudaEventElapsedTime(&a, npu->ev[0], npu->ev[1]);
+    cudaEventElapsedTime(&b, npu->ev[1], npu->ev[2]);
+    cudaEventElapsedTime(&c, npu->ev[2], npu->ev[3]);
+    cudaEventElapsedTime(&d, npu->ev[3], npu->ev[4]);
+    npu->times.copy_ms += a + d;
+    npu->times.encode_ms += b;
+    npu->times.gemm_ms += c;
+    npu->times.calls++;
+    if (*npu->err_host & ERR_TIMEOUT) return set_error("a GPU kernel's bounded wait ran out");
+    if (*npu->err_host & ERR_NOT_FINITE) return set_error("the GPU's results held NaN or infinity");
+    return 0;
+}
+
+int zest_take_times(zest_npu *npu, zest_times *out) {
+    if (!npu || !out) return set_error("zest_take_times: no service");
+    *out = npu->times;
+    npu->times = {};
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,391 @@
+// K3: the bfp16 GEMM on the 5th-generation tensor cores.
+//
+// C[M x N] = A[M x K] * B[N x K]^T, where A and B hold bfp16-decoded values
+// (every bfp16 value is exact in bf16), so a bf16 x bf16 -> fp32 tcgen05 MMA
+// computes the reference's products exactly and only the fp32 summation
+// order differs (mm_paired, kernels/bfp16_gemm/aie_kernels/aie2p/
+// mm_bfp_acc.cc:44-100). The epilogue applies the reference's output modes
+// (out_epilogue, :258-278), un-tiles to ggml's row-major [M][N] as
+// bfp16_c_row / bfp16_c16_row do (src/npu/bfp16_pack.cpp:188-229), and
+// raises a device flag on any NaN/Inf result (all_finite,
+// src/xdna-npu.cpp:59-67).
+//
+// Shape: a persistent kernel, one CTA per SM, 192 threads:
+//   warp 0      TMA producer: 128x64 A and 256x64 B bf16 tiles, 128-byte
+//               swizzle, into a 4-stage shared-memory ring
+//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
+//               (M=128, N=256, K=16 per instruction, fp32 in TMEM)
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, mode, store
+// Two 256-column accumulators (all 512 TMEM columns) let the epilogue of
+// one tile overlap the MMAs of the next. Every wait is bounded; on timeout
+// the kernel raises ERR_TIMEOUT, drains its own copies and MMAs, frees TMEM
+// and returns.
+#include "zest_device.cuh"
+#include "zest_internal.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+namespace zest {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int ACC_COLS = BN;
+constexpr int TMEM_COLS = 2 * ACC_COLS;
+constexpr int NUM_THREADS = 192;
+constexpr int NUM_BARRIERS = 2 * STAGES + 5;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARRIERS * 8 + 16;
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // 1 s
+constexpr int GROUP_M = 8;
+
+// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both
+// K-major, N=256, M=128.
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (BN >> 3) << 17) |
+                           ((uint32_t) (BM >> 4) << 24);
+
+struct gemm_params {
+    int64_t M, N, K, ldc;
+    int64_t n_out;  // output columns (N, or the real F for SwiGLU)
+    float *c;
+    unsigned *err;
+    int mode, num_m, num_n, num_k;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
+    const int per_group = GROUP_M * num_n;
+    const int g = t / per_group, first_m = g * GROUP_M;
+    const int gsz = min(num_m - first_m, GROUP_M);
+    const int r = t % per_group;
+    mb = first_m + r % gsz;
+    nb = r / gsz;
+}
+
+__device__ __forceinline__ float bf16_round(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(u | 0x00400000u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return __uint_as_float(u & 0xffff0000u);
+}
+
+__device__ __forceinline__ uint32_t not_finite(float v) {
+    return (__float_as_uint(v) & 0x7f800000u) == 0x7f800000u;
+}
+
+// Writes one thread's 32 accumulator columns [col0, col0+32) of row `row`.
+__device__ __forceinline__ uint32_t store_chunk(const gemm_params &p, const uint32_t (&r)[32], int64_t row,
+                                                int64_t col0) {
+    uint32_t bad = 0;
+    if (row >= p.M) return 0;
+    if (p.mode == MODE_SWIGLU) {
+        // columns: 8 gate, 8 up, 8 gate, 8 up -> 16 outputs
+        float o[16];
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float g = __uint_as_float(r[h * 16 + i]), u = __uint_as_float(r[h * 16 + 8 + i]);
+                const float s = 1.0f / (1.0f + expf(-g));
+                o[h * 8 + i] = bf16_round((g * u) * s);
+            }
+        const int64_t oc0 = col0 / 2;
+        float *dst = p.c + row * p.ldc + oc0;
+        if (oc0 + 16 <= p.n_out && (p.ldc % 4) == 0) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+                *reinterpret_cast<float4 *>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+                bad |= not_finite(o[i]) | not_finite(o[i + 1]) | not_finite(o[i + 2]) | not_finite(o[i + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                if (oc0 + i < p.n_out) {
+                    dst[i] = o[i];
+                    bad |= not_finite(o[i]);
+                }
+        }
+        return bad;
+    }
+    float o[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        const float v = __uint_as_float(r[i]);
+        o[i] = p.mode == MODE_BF16 ? bf16_round(v) : v;
+    }
+    float *dst = p.c + row * p.ldc + col0;
+    if (col0 + 32 <= p.n_out && (p.ldc % 4) == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            *reinterpret_cast<float4 *>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+            bad |= not_finite(o[i]) | not_finite(o[i + 1]) | not_finite(o[i + 2]) | not_finite(o[i + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (col0 + i < p.n_out) {
+                dst[i] = o[i];
+                bad |= not_finite(o[i]);
+            }
+    }
+    return bad;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const gemm_params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = tfull + 2,
+             *drain = tempty + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + NUM_BARRIERS);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, TMEM_COLS);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    const int total = p.num_m * p.num_n;
+
+    auto fail = [&]() {
+        *abort_flag = 1;
+        atomicOr(p.err, ERR_TIMEOUT);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0, armed_phase = 0;  // per-stage bits: loads issued, and their phase
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int mb, nb;
+                tile_coords(t, p.num_m, p.num_n, mb, nb);
+                for (int kb = 0; kb < p.num_k; kb++) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, WAIT_LIMIT_NS)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                    uint8_t *sa = smem + stage * STAGE_BYTES;
+                    tma_load_2d(sa, &tmA, &full[stage], kb * BK, mb * BM);
+                    tma_load_2d(sa + A_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+                    armed |= 1u << stage;
+                    armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // no copy of ours may land after the block exits
+            for (int s = 0; s < STAGES; s++)
+                if ((armed & (1u << s)) && !mbar_wait_bounded(&full[s], (armed_phase >> s) & 1u, nullptr, WAIT_LIMIT_NS))
+                    fail();
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag, WAIT_LIMIT_NS)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t) (acc * ACC_COLS);
+                for (int kb = 0; kb < p.num_k; kb++) {
+                    if (!mbar_wait_bounded(&full[stage], phase, abort_flag, WAIT_LIMIT_NS)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t *sa = smem + stage * STAGE_BYTES;
+                    const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++)
+                        tc_mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+                    tc_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+            // every MMA we issued is complete before TMEM is freed
+            tc_commit(drain);
+            if (!mbar_wait_bounded(drain, 0, nullptr, WAIT_LIMIT_NS)) fail();
+        }
+    } else {
+        const int q = warp % 4;  // TMEM lane quarter this warp may read
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        uint32_t bad = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            int mb, nb;
+            tile_coords(t, p.num_m, p.num_n, mb, nb);
+            if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, WAIT_LIMIT_NS)) {
+                fail();
+                break;
+            }
+            tc_fence_after();
+            const int64_t row = (int64_t) mb * BM + q * 32 + lane;
+            const uint32_t tbase = tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * ACC_COLS);
+            uint32_t r[32];
+            for (int ch = 0; ch < BN / 32; ch++) {
+                tmem_ld_32x32b_x32(tbase + (uint32_t) (ch * 32), r);
+                tmem_ld_wait();
+                if (ch == BN / 32 - 1) {
+                    tc_fence_before();
+                    mbar_arrive(&tempty[acc]);
+                }
+                const int64_t col0 = (int64_t) nb * BN + ch * 32;
+                if (col0 < p.N) bad |= store_chunk(p, r, row, col0);
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.err, ERR_NOT_FINITE);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// Plain CUDA-core GEMM: one thread per output, fp32 accumulation.
+__global__ void gemm_simt_kernel(const uint16_t *a, int64_t lda, const uint16_t *b, int64_t ldb, int64_t M, int64_t N,
+                                 int64_t K, float *c, int64_t ldc) {
+    const int64_t n = blockIdx.x * (int64_t) blockDim.x + threadIdx.x, m = blockIdx.y;
+    if (n >= N || m >= M) return;
+    float acc = 0.0f;
+    for (int64_t k = 0; k < K; k++)
+        acc = fmaf(__uint_as_float((uint32_t) a[m * lda + k] << 16), __uint_as_float((uint32_t) b[n * ldb + k] << 16),
+                   acc);
+    c[m * ldc + n] = acc;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// A row-major bf16 matrix [rows][ld] as 64 x box_rows tiles, 128-byte swizzle.
+bool make_tmap(CUtensorMap *m, const void *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = { (cuuint64_t) cols, (cuuint64_t) rows };
+    cuuint64_t strides[1] = { (cuuint64_t) ld * 2 };
+    cuuint32_t box[2] = { (cuuint32_t) BK, (cuuint32_t) box_rows };
+    cuuint32_t estr[2] = { 1, 1 };
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
+}  // namespace
+
+int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
+                int64_t K, int mode, float *c, int64_t ldc, unsigned *err_flag, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return 0;
+    if (K <= 0 || K % 8 || lda < K || ldb < K || lda % 8 || ldb % 8 || ((uintptr_t) a_bf16 & 15) ||
+        ((uintptr_t) b_bf16 & 15) || !err_flag)
+        return set_error("gemm: K and the row strides must be multiples of 8 and the operands 16-byte aligned");
+    if (mode < MODE_F32 || mode > MODE_SWIGLU || (mode == MODE_SWIGLU && N % 16))
+        return set_error("gemm: bad output mode");
+    const int64_t n_out = mode == MODE_SWIGLU ? N / 2 : N;
+    if (ldc < n_out) return set_error("gemm: ldc smaller than the output width");
+    CUtensorMap ta, tb;
+    if (!make_tmap(&ta, a_bf16, M, K, lda, BM) || !make_tmap(&tb, b_bf16, N, K, ldb, BN))
+        return set_error("gemm: cannot build the TMA descriptors");
+    gemm_params p;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.ldc = ldc;
+    p.n_out = n_out;
+    p.c = c;
+    p.err = err_flag;
+    p.mode = mode;
+    p.num_m = (int) ((M + BM - 1) / BM);
+    p.num_n = (int) ((N + BN - 1) / BN);
+    p.num_k = (int) ((K + BK - 1) / BK);
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+            cudaSuccess)
+            return check_launch("gemm (shared memory size)");
+        attr = true;
+    }
+    const int64_t tiles = (int64_t) p.num_m * p.num_n;
+    const int grid = (int) (tiles < num_sms() ? tiles : num_sms());
+    gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, p);
+    return check_launch("gemm");
+}
+
+int launch_gemm_simt(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
+                     int64_t K, float *c, int64_t ldc, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return 0;
+    dim3 grid((unsigned) ((N + 127) / 128), (unsigned) M);
+    gemm_simt_kernel<<<grid, 128, 0, st>>>(a_bf16, lda, b_bf16, ldb, M, N, K, c, ldc);
+    return check_launch("gemm_simt");
+}
+
+}  // namespace zest

@@ -1,0 +1,48 @@
+// Internal declarations shared by the CUDA sources of libzest_b200.so.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace zest {
+
+// ggml_type ids (GGUF file-format values) of the weight types converted
+enum {
+    TYPE_F32 = 0,
+    TYPE_F16 = 1,
+    TYPE_Q8_0 = 8,
+    TYPE_Q4_K = 12,
+    TYPE_Q6_K = 14,
+    TYPE_IQ3_S = 21,
+};
+
+// GEMM output modes (kernels/bfp16_gemm/aie_kernels/aie2p/mm_bfp_acc.cc:138-148)
+enum {
+    MODE_F32 = 0,     // fp32 as accumulated
+    MODE_BF16 = 1,    // every value rounded to bf16, nearest even
+    MODE_SWIGLU = 2,  // SiLU(gate) * up, rounded to bf16 (weights interleaved 8 gate + 8 up rows)
+};
+
+// Records `msg` as the thread's last error and returns -1.
+int set_error(const char *msg);
+// After a launch: -1 with the CUDA error recorded, or 0.
+int check_launch(const char *what);
+bool iq3s_grid_loaded();
+int set_iq3s_grid(const uint32_t *grid512);
+
+int launch_pack_activations(const float *x, int64_t T, int64_t K, int64_t ldx, int64_t m_pad, uint8_t *a_bytes,
+                            uint16_t *a_bf16, int64_t ldb, cudaStream_t st);
+
+int launch_convert_weight(int type, const void *src0, const void *src1, int fused, int64_t n_rows, int64_t src_row0,
+                          int64_t src_rows_total, int64_t K, int64_t n_pad, uint8_t *b_bytes, uint16_t *b_bf16,
+                          cudaStream_t st);
+
+int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
+                int64_t K, int mode, float *c, int64_t ldc, unsigned *err_flag, cudaStream_t st);
+
+// The plain CUDA-core GEMM used by the start-up self-test as a second
+// opinion on the tensor-core kernel.
+int launch_gemm_simt(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
+                     int64_t K, float *c, int64_t ldc, cudaStream_t st);
+
+}  // namespace zest

@@ -1,0 +1,254 @@
+"""ctypes binding of libzest_b200.so (include/zest_b200.h) for tests and bench.
+
+Torch is used only for device memory and streams: every call passes plain
+device pointers and the current CUDA stream through the C ABI. There is no
+CPU fallback: if the library or a GPU is missing, the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+PKG_DIR = Path(__file__).resolve().parent.parent
+LIB_PATH = PKG_DIR / "libzest_b200.so"
+BACKEND_PATH = PKG_DIR / "libggml-zest.so"
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_IQ3_S = 0, 1, 8, 12, 14, 21
+MODE_F32, MODE_BF16, MODE_SWIGLU = 0, 1, 2
+ERR_NOT_FINITE, ERR_TIMEOUT = 1, 2
+BLOCK_BYTES = 9
+# (values per quant block, bytes per quant block)
+QUANT = {TYPE_F32: (1, 4), TYPE_F16: (1, 2), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144),
+         TYPE_Q6_K: (256, 210), TYPE_IQ3_S: (256, 110)}
+
+_i64, _vp, _int, _u32p = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)
+
+
+class ZestError(RuntimeError):
+    pass
+
+
+class WKey(ctypes.Structure):
+    """zest_wkey: a weight's identity (xdna_npu::wkey, src/xdna-npu.h:46-52)."""
+    _fields_ = [("buffer", _vp), ("data", _vp), ("type", _int), ("K", _i64), ("N", _i64)]
+
+
+class Times(ctypes.Structure):
+    _fields_ = [("encode_ms", ctypes.c_double), ("gemm_ms", ctypes.c_double), ("copy_ms", ctypes.c_double),
+                ("pack_ms", ctypes.c_double), ("calls", _int)]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it was never built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ZestError(f"{LIB_PATH} is missing: run __graft_entry__.build() (make -C ggml-xdna_b200)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    sig = {
+        "zest_version": (_int, []),
+        "zest_last_error": (ctypes.c_char_p, []),
+        "zest_load_iq3s_grid": (_int, [_u32p]),
+        "zest_pack_activations": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
+        "zest_convert_weight": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
+        "zest_convert_gate_up": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
+        "zest_gemm": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
+        "zest_usable": (_int, [_int, ctypes.c_char_p, ctypes.c_size_t]),
+        "zest_open": (_vp, [_int]),
+        "zest_close": (None, [_vp]),
+        "zest_set_out16": (None, [_vp, _int]),
+        "zest_has_weight": (_int, [_vp, ctypes.POINTER(WKey)]),
+        "zest_add_weight": (_int, [_vp, ctypes.POINTER(WKey), _vp, _int]),
+        "zest_add_fused": (_int, [_vp, ctypes.POINTER(WKey), _vp, _vp, _int]),
+        "zest_out_width": (_i64, [_vp, ctypes.POINTER(WKey), _int]),
+        "zest_weight_bfp16": (_vp, [_vp, ctypes.POINTER(WKey), _int]),
+        "zest_weight_bf16": (_vp, [_vp, ctypes.POINTER(WKey), _int, ctypes.POINTER(_i64)]),
+        "zest_mul_mat": (_int, [_vp, ctypes.POINTER(WKey), _int, _vp, _i64, _vp, _int]),
+        "zest_stream": (_vp, [_vp]),
+        "zest_take_times": (_int, [_vp, ctypes.POINTER(Times)]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype, f.argtypes = res, args
+    _lib = L
+    return L
+
+
+def exported_symbols() -> list[str]:
+    return [n for n in ("zest_version", "zest_last_error", "zest_load_iq3s_grid", "zest_pack_activations",
+                        "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_usable", "zest_open",
+                        "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
+                        "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_mul_mat", "zest_stream",
+                        "zest_take_times")]
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise ZestError(f"{what}: {lib().zest_last_error().decode()}")
+
+
+def iq3s_grid() -> np.ndarray:
+    """ggml's IQ3_S codebook (512 x 4 magnitudes) packed as uint32, read
+    from the installed gguf package at run time."""
+    from gguf.quants import IQ3_S
+    IQ3_S.init_grid()
+    g = np.asarray(IQ3_S.grid, dtype=np.float32).reshape(512, 4).astype(np.uint32)
+    return (g[:, 0] | (g[:, 1] << 8) | (g[:, 2] << 16) | (g[:, 3] << 24)).astype(np.uint32)
+
+
+def load_iq3s_grid() -> None:
+    g = np.ascontiguousarray(iq3s_grid())
+    _check(lib().zest_load_iq3s_grid(g.ctypes.data_as(_u32p)), "zest_load_iq3s_grid")
+
+
+def row_bytes(qtype: int, k: int) -> int:
+    qk, bb = QUANT[qtype]
+    return k // qk * bb
+
+
+def pad_to(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+# --- stream-level kernels on torch tensors -----------------------------------
+
+def _stream():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def pack_activations(x, m_pad: int | None = None, want_bytes: bool = True, want_bf16: bool = True):
+    """K2: f32 [T][K] cuda tensor -> (bfp16 bytes uint8 [m_pad*K/8*9], bf16 int16 [m_pad][K])."""
+    import torch
+    T, K = x.shape
+    m_pad = m_pad or pad_to(max(T, 1), 128)
+    ab = torch.empty(m_pad * K // 8 * 9, dtype=torch.uint8, device=x.device) if want_bytes else None
+    ah = torch.empty((m_pad, K), dtype=torch.int16, device=x.device) if want_bf16 else None
+    _check(lib().zest_pack_activations(_ptr(x), T, K, x.stride(0), m_pad, _ptr(ab), _ptr(ah), K, _stream()),
+           "zest_pack_activations")
+    return ab, ah
+
+
+def convert_weight(qtype: int, raw, N: int, K: int, row0: int = 0, n_rows: int | None = None,
+                   n_pad: int | None = None, want_bytes: bool = True, want_bf16: bool = True):
+    """K1: raw GGUF rows (uint8 cuda tensor of N rows) -> (bfp16 B operand, bf16 [n_pad][K])."""
+    import torch
+    n_rows = N - row0 if n_rows is None else n_rows
+    n_pad = n_pad or pad_to(max(n_rows, 1), 512)
+    bb = torch.empty(n_pad * K // 8 * 9, dtype=torch.uint8, device=raw.device) if want_bytes else None
+    bh = torch.empty((n_pad, K), dtype=torch.int16, device=raw.device) if want_bf16 else None
+    _check(lib().zest_convert_weight(qtype, _ptr(raw), N, row0, n_rows, K, n_pad, _ptr(bb), _ptr(bh), _stream()),
+           "zest_convert_weight")
+    return bb, bh
+
+
+def convert_gate_up(qtype: int, gate, up, F: int, K: int, row0: int = 0, n_rows: int | None = None,
+                    f_pad: int | None = None, want_bytes: bool = True, want_bf16: bool = True):
+    import torch
+    n_rows = F - row0 if n_rows is None else n_rows
+    f_pad = f_pad or pad_to(max(n_rows, 1), 256)
+    bb = torch.empty(2 * f_pad * K // 8 * 9, dtype=torch.uint8, device=gate.device) if want_bytes else None
+    bh = torch.empty((2 * f_pad, K), dtype=torch.int16, device=gate.device) if want_bf16 else None
+    _check(lib().zest_convert_gate_up(qtype, _ptr(gate), _ptr(up), F, row0, n_rows, K, f_pad, _ptr(bb), _ptr(bh),
+                                      _stream()), "zest_convert_gate_up")
+    return bb, bh
+
+
+def gemm(a_bf16, b_bf16, M: int, N: int, mode: int = MODE_F32, out=None, err=None):
+    """K3: out[M][N or N/2] f32 = A * B^T; err: int32 cuda word (cleared by the caller)."""
+    import torch
+    K = a_bf16.shape[1]
+    n_out = N // 2 if mode == MODE_SWIGLU else N
+    if out is None:
+        out = torch.empty((M, n_out), dtype=torch.float32, device=a_bf16.device)
+    own_err = err is None
+    if own_err:
+        err = torch.zeros(1, dtype=torch.int32, device=a_bf16.device)
+    _check(lib().zest_gemm(_ptr(a_bf16), a_bf16.stride(0), _ptr(b_bf16), b_bf16.stride(0), M, N, K, mode, _ptr(out),
+                           out.stride(0), _ptr(err), _stream()), "zest_gemm")
+    if own_err:
+        e = int(err.item())
+        if e:
+            raise ZestError(f"zest_gemm raised device error bits {e:#x}")
+    return out
+
+
+# --- the matmul service -------------------------------------------------------
+
+class Npu:
+    """zest_npu: per-GPU weight cache + y = x * W^T (xdna_npu, src/xdna-npu.h:40-136)."""
+
+    def __init__(self, device: int = 0):
+        self.h = lib().zest_open(device)
+        if not self.h:
+            raise ZestError(f"zest_open: {lib().zest_last_error().decode()}")
+
+    def close(self):
+        if self.h:
+            lib().zest_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_out16(self, on: bool):
+        lib().zest_set_out16(self.h, int(on))
+
+    @staticmethod
+    def key(data_addr: int, qtype: int, K: int, N: int, buffer: int = 0) -> WKey:
+        return WKey(buffer, data_addr, qtype, K, N)
+
+    def add_weight(self, key: WKey, raw_ptr: int, on_device: bool):
+        _check(lib().zest_add_weight(self.h, ctypes.byref(key), ctypes.c_void_p(raw_ptr), int(on_device)),
+               "zest_add_weight")
+
+    def add_fused(self, key: WKey, gate_ptr: int, up_ptr: int, on_device: bool):
+        _check(lib().zest_add_fused(self.h, ctypes.byref(key), ctypes.c_void_p(gate_ptr), ctypes.c_void_p(up_ptr),
+                                    int(on_device)), "zest_add_fused")
+
+    def has_weight(self, key: WKey) -> bool:
+        return bool(lib().zest_has_weight(self.h, ctypes.byref(key)))
+
+    def out_width(self, key: WKey, fused: bool = False) -> int:
+        return int(lib().zest_out_width(self.h, ctypes.byref(key), int(fused)))
+
+    def weight_bf16(self, key: WKey, fused: bool = False):
+        n_pad = _i64(0)
+        p = lib().zest_weight_bf16(self.h, ctypes.byref(key), int(fused), ctypes.byref(n_pad))
+        return p, n_pad.value
+
+    def mul_mat(self, key: WKey, x_ptr: int, T: int, y_ptr: int, on_device: bool, fused: bool = False):
+        _check(lib().zest_mul_mat(self.h, ctypes.byref(key), int(fused), ctypes.c_void_p(x_ptr), T,
+                                  ctypes.c_void_p(y_ptr), int(on_device)), "zest_mul_mat")
+
+    def stream(self) -> int:
+        return int(lib().zest_stream(self.h) or 0)
+
+    def take_times(self) -> Times:
+        t = Times()
+        _check(lib().zest_take_times(self.h, ctypes.byref(t)), "zest_take_times")
+        return t
+
+
+def usable(device: int = 0) -> tuple[bool, str]:
+    buf = ctypes.create_string_buffer(512)
+    rc = lib().zest_usable(device, buf, len(buf))
+    return rc == 0, buf.value.decode()
+
+
+def env_threads() -> int:
+    return os.cpu_count() or 1

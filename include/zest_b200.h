@@ -1,0 +1,177 @@
+/*
+ * zest_b200: the B200 (sm_100a) implementation of the Zest add-on's prefill
+ * MUL_MAT path, as a C ABI (libzest_b200.so). Plain pointers and sizes only.
+ *
+ * Two layers:
+ *   1. stream-level kernels on device memory, on the caller's CUDA stream
+ *      (cudaStream_t passed as void *; NULL = the legacy default stream);
+ *   2. the matmul service `zest_npu`, the counterpart of the reference's
+ *      class xdna_npu (src/xdna-npu.h:40-136): a per-GPU weight-copy cache
+ *      keyed like xdna_npu::wkey and y = x * W^T on host or device buffers.
+ *
+ * Every function returns 0 on success and -1 on failure, with the reason in
+ * zest_last_error() (the reference returns bool and fills std::string &err).
+ * No function aborts or throws.
+ *
+ * Data layouts (the reference's, src/npu/bfp16_pack.h:1-60):
+ *   bfp16 block   9 bytes: the largest biased float exponent e of 8 values,
+ *                 then 8 int8 mantissas q; value = q * 2^(e - 133)
+ *   A operand     activations, rows of K values, in 128-row x 64-column tiles
+ *   B operand     weights (N rows of K), per array column c of 8, its 64-row
+ *                 groups (c + 8t), each in 64 x 64 tiles
+ *   bf16 copies   the same decoded values, row-major [rows][ld], which the
+ *                 tensor-core GEMM reads (every bfp16 value is exact in bf16)
+ */
+#ifndef ZEST_B200_H
+#define ZEST_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZEST_B200_VERSION 1
+
+/* weight types (ggml_type ids, as GGUF stores them) */
+#define ZEST_TYPE_F32 0
+#define ZEST_TYPE_F16 1
+#define ZEST_TYPE_Q8_0 8
+#define ZEST_TYPE_Q4_K 12
+#define ZEST_TYPE_Q6_K 14
+#define ZEST_TYPE_IQ3_S 21
+
+/* GEMM output modes (kernels/bfp16_gemm/aie_kernels/aie2p/mm_bfp_acc.cc:138-148) */
+#define ZEST_MODE_F32 0    /* fp32 as accumulated */
+#define ZEST_MODE_BF16 1   /* each value rounded to bf16 (nearest even), returned as f32 */
+#define ZEST_MODE_SWIGLU 2 /* SiLU(gate) * up rounded to bf16; N/2 outputs a row */
+
+/* bits of the device error word the GEMM raises */
+#define ZEST_ERR_NOT_FINITE 1u /* a result was NaN or infinite */
+#define ZEST_ERR_TIMEOUT 2u    /* a bounded wait inside a kernel ran out */
+
+int zest_version(void);
+/* Why the last call on this thread failed. */
+const char *zest_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * 1. Stream-level kernels (device pointers)
+ * ------------------------------------------------------------------------- */
+
+/* The IQ3_S codebook: ggml's iq3s_grid, 512 entries of four magnitudes packed
+ * in a uint32 (host pointer). Needed before converting IQ3_S weights.
+ * Replaces: nothing in the reference itself; ggml's to_float for IQ3_S reads
+ * the table (called at src/xdna-npu.cpp:345). */
+int zest_load_iq3s_grid(const uint32_t *grid512);
+
+/* K2, the activation pack. x: f32 rows [T][ldx]; writes rows [0, m_pad) of
+ * the A operand (m_pad a multiple of 128, >= T; rows past T are zeros):
+ * a_bfp16 (m_pad*K/8*9 bytes, the reference layout; may be NULL) and/or
+ * a_bf16 ([m_pad][ld_bf16] decoded values; may be NULL). K % 64 == 0.
+ * Replaces: bfp16_pack_a_into (src/npu/bfp16_pack.h:56-58) and the encode
+ * loop of xdna_npu::mul_mat / begin / encode_row (src/xdna-npu.cpp:406-420,
+ * 476-515). */
+int zest_pack_activations(const float *x, int64_t T, int64_t K, int64_t ldx, int64_t m_pad, uint8_t *a_bfp16,
+                          uint16_t *a_bf16, int64_t ld_bf16, void *stream);
+
+/* K1, the weight conversion. raw: GGUF rows of `type` (rows_total rows of K
+ * values); converts rows [row0, row0 + N) into a B operand of n_pad rows
+ * (n_pad % 512 == 0, rows past N zeros): b_bfp16 (n_pad*K/8*9 bytes, the
+ * reference layout; may be NULL) and/or b_bf16 ([n_pad][K]; may be NULL).
+ * Replaces: xdna_npu::unpack (ggml to_float) + bfp16_pack_b inside
+ * xdna_npu::add_weight (src/xdna-npu.cpp:339-378). */
+int zest_convert_weight(int type, const void *raw, int64_t rows_total, int64_t row0, int64_t N, int64_t K,
+                        int64_t n_pad, uint8_t *b_bfp16, uint16_t *b_bf16, void *stream);
+
+/* K1 for a fused gate/up pair: 8 gate rows, then the 8 up rows that pair
+ * with them, F padded to f_pad (a multiple of 256) -> a B operand of 2*f_pad
+ * rows. Rows [row0, row0 + F) of gate and up (rows_total rows each).
+ * Replaces: xdna_npu::add_fused (src/xdna-npu.cpp:380-390) with
+ * bfp16_interleave_gate_up (src/npu/bfp16_pack.cpp:231-237). */
+int zest_convert_gate_up(int type, const void *gate, const void *up, int64_t rows_total, int64_t row0, int64_t F,
+                         int64_t K, int64_t f_pad, uint8_t *b_bfp16, uint16_t *b_bf16, void *stream);
+
+/* K3, the GEMM: c[M][ldc] = A[M][K] * B[N][K]^T in fp32 on the tensor cores,
+ * then `mode`. In ZEST_MODE_SWIGLU, B comes from zest_convert_gate_up and c
+ * gets N/2 values a row. err: a device word the kernel ORs ZEST_ERR_* bits
+ * into (the caller clears it).
+ * Replaces: the NPU kernel's mm_paired + out_epilogue
+ * (kernels/bfp16_gemm/aie_kernels/aie2p/mm_bfp_acc.cc:44-100,258-278) and the
+ * host read-back read_row / bfp16_c_row / bfp16_c16_row / all_finite
+ * (src/xdna-npu.cpp:59-85, src/npu/bfp16_pack.cpp:188-229). */
+int zest_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
+              int64_t K, int mode, float *c, int64_t ldc, unsigned *err, void *stream);
+
+/* ---------------------------------------------------------------------------
+ * 2. The matmul service (xdna_npu)
+ * ------------------------------------------------------------------------- */
+
+typedef struct zest_npu zest_npu;
+
+/* A weight's identity across calls: where it lives and what it is
+ * (xdna_npu::wkey, src/xdna-npu.h:46-52). */
+typedef struct {
+    const void *buffer, *data;
+    int type;
+    int64_t K, N;
+} zest_wkey;
+
+/* Time spent since the last zest_take_times (xdna_npu::times,
+ * src/xdna-npu.h:104-107), measured with CUDA events. */
+typedef struct {
+    double encode_ms, gemm_ms, copy_ms, pack_ms;
+    int calls;
+} zest_times;
+
+/* Whether GPU `device` can run the path: it opens, and a small exact integer
+ * multiply through all three kernels comes back right. Checked once per
+ * device; `why` (may be NULL) says what passed or failed.
+ * Replaces: xdna_npu_usable + npu_self_test (src/xdna-npu.cpp:142-184,255-291). */
+int zest_usable(int device, char *why, size_t why_len);
+
+/* A service on GPU `device` with its own stream. NULL on failure.
+ * Replaces: xdna_npu::xdna_npu + init (src/xdna-npu.cpp:304-317). */
+zest_npu *zest_open(int device);
+void zest_close(zest_npu *npu);
+
+/* Output mode for weights added from now on: 1 = bf16 (the default, as the
+ * reference's GGML_XDNA_OUT16), 0 = fp32 (src/xdna-npu.cpp:49-55,374). */
+void zest_set_out16(zest_npu *npu, int on);
+
+int zest_has_weight(const zest_npu *npu, const zest_wkey *key);
+
+/* Builds a weight's copy from its raw GGUF bytes (host memory, or device
+ * memory when raw_on_device): bfp16 bytes + bf16 expansion, kept on the GPU.
+ * Replaces: xdna_npu::add_weight (src/xdna-npu.cpp:369-378). */
+int zest_add_weight(zest_npu *npu, const zest_wkey *key, const void *raw, int raw_on_device);
+
+/* A gate and an up weight fused for SiLU(gate) * up, keyed by gate's key.
+ * Replaces: xdna_npu::add_fused (src/xdna-npu.cpp:380-390). */
+int zest_add_fused(zest_npu *npu, const zest_wkey *gate, const void *gate_raw, const void *up_raw, int raw_on_device);
+
+/* Output values a row of a weight added above: N, or F for a fused pair
+ * (xdna_npu::out_width, src/xdna-npu.h:74). -1 if unknown. */
+int64_t zest_out_width(const zest_npu *npu, const zest_wkey *key, int fused);
+
+/* The weight copy's device buffers, for callers that run the kernels
+ * themselves (NULL if unknown). */
+const uint8_t *zest_weight_bfp16(const zest_npu *npu, const zest_wkey *key, int fused);
+const uint16_t *zest_weight_bf16(const zest_npu *npu, const zest_wkey *key, int fused, int64_t *n_pad);
+
+/* y[T][out_width] = x[T][K] * W^T, f32 row-major, for a weight added above
+ * (fused: the SwiGLU of the pair). x and y are host memory, or device memory
+ * when on_device. Checks every result for NaN/Inf.
+ * Replaces: xdna_npu::mul_mat (src/xdna-npu.cpp:392-444). */
+int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x, int64_t T, float *y, int on_device);
+
+/* The service's CUDA stream (a cudaStream_t). */
+void *zest_stream(zest_npu *npu);
+
+/* Replaces: xdna_npu::take_times (src/xdna-npu.cpp:555-559). */
+int zest_take_times(zest_npu *npu, zest_times *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

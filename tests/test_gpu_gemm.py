@@ -1,0 +1,123 @@
+"""K3, the tensor-core GEMM, through the C ABI.
+
+Parity bar (the north star's): max|C_gpu - C_ref| / max|C_ref| <= 1e-3, where
+C_ref is the reference's CPU matmul (xdna-ref) on the bfp16-decoded operands.
+The products are exact in bf16 x bf16 -> fp32, so only the summation order
+differs; the measured error is ~1e-6. Integer operands must match exactly.
+"""
+import numpy as np
+import pytest
+import torch
+
+import zest_b200 as Z
+from oracle import oracle as O
+from gpu_util import dev, host, bf16_to_f32
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def operands(M, N, K, qt=O.Q8_0, seed=0, outliers=False):
+    raw = O.quantize(qt, O.weights_f32(N, K, seed + 1))
+    x = O.activations(M, K, seed + 2, outliers=outliers)
+    _, bh = Z.convert_weight(qt, dev(raw), N, K)
+    _, ah = Z.pack_activations(dev(x))
+    a_dec = bf16_to_f32(host(ah)[:M].view(np.uint16))
+    b_dec = bf16_to_f32(host(bh)[:N].view(np.uint16))
+    return ah, bh, a_dec, b_dec, raw, x
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (1000, 1000, 320), (96, 4096, 2560),
+                                   (513, 777, 1024)])
+def test_gemm_f32_vs_oracle(M, N, K):
+    ah, bh, a_dec, b_dec, _, _ = operands(M, N, K, seed=M + N)
+    c = host(Z.gemm(ah, bh, M, N))
+    want = O.mul_mat(b_dec, a_dec)
+    assert O.nmax_err(c, want) <= TOL
+
+
+def test_gemm_exact_integers():
+    a, w = O.selftest_operands(512, 128, 512)
+    ah = dev(O.decode_blocks(O.encode_blocks(a.astype(np.float32))).reshape(512, 128))
+    _, ah = Z.pack_activations(ah)
+    _, bh = Z.convert_weight(O.F32, dev(w.astype(np.float32).view(np.uint8)), 512, 128)
+    c = host(Z.gemm(ah, bh, 512, 512))
+    want = a.astype(np.int64) @ w.astype(np.int64).T
+    assert np.array_equal(c, want.astype(np.float32))
+
+
+def test_gemm_matches_reference_golden():
+    g = np.load(Z.PKG_DIR.parent / "tests" / "golden" / "mul_mat_q8_0.npz")
+    N, K, M = int(g["N"]), int(g["K"]), int(g["M"])
+    _, bh = Z.convert_weight(O.Q8_0, dev(g["raw"]), N, K)
+    _, ah = Z.pack_activations(dev(g["x"]))
+    c = host(Z.gemm(ah, bh, M, N))
+    assert O.nmax_err(c, g["y_decoded"]) <= TOL
+    # against the reference on the unrounded operands: the bfp16 rounding's own error
+    assert O.nmax_err(c, g["y"]) < 5e-2
+
+
+def test_gemm_config1_rows():
+    # config 1: 1024 x 2560 activations, Q8_0 9728 x 2560 weight; 64 rows checked in full
+    M, N, K = 1024, 9728, 2560
+    ah, bh, a_dec, b_dec, _, _ = operands(M, N, K, seed=1)
+    c = host(Z.gemm(ah, bh, M, N))
+    rows = np.r_[0:32, 992:1024]
+    assert O.nmax_err(c[rows], O.mul_mat(b_dec, a_dec[rows])) <= TOL
+
+
+def test_gemm_bf16_mode_is_rounded_f32():
+    M, N, K = 384, 768, 512
+    ah, bh, _, _, _, _ = operands(M, N, K, seed=3)
+    c0 = host(Z.gemm(ah, bh, M, N, Z.MODE_F32))
+    c1 = host(Z.gemm(ah, bh, M, N, Z.MODE_BF16))
+    assert np.array_equal(c1, O.round_bf16(c0))
+
+
+def test_gemm_swiglu_mode():
+    M, F, K = 256, 300, 512
+    gr = O.quantize(O.Q4_K, O.weights_f32(F, K, 1))
+    ur = O.quantize(O.Q4_K, O.weights_f32(F, K, 2))
+    _, bh = Z.convert_gate_up(O.Q4_K, dev(gr), dev(ur), F, K)
+    _, ah = Z.pack_activations(dev(O.activations(M, K, 3)))
+    n = bh.shape[0]  # 2 * f_pad
+    acc = host(Z.gemm(ah, bh, M, n, Z.MODE_F32))
+    got = host(Z.gemm(ah, bh, M, n, Z.MODE_SWIGLU))
+    idx = np.arange(F)
+    at = (idx // 8) * 16 + idx % 8
+    want = O.swiglu_bf16(acc[:, at], acc[:, at + 8])
+    assert got.shape == (M, n // 2)
+    g = got[:, :F]
+    # one bf16 ulp at most (SiLU's exp differs in its last fp32 bits)
+    ulp = np.abs(g.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64)) >> 16
+    assert ulp.max() <= 1
+    assert not got[:, F:].any()
+
+
+def test_gemm_flags_non_finite():
+    M, N, K = 128, 512, 64
+    w = O.weights_f32(N, K, 1)
+    w[7, 3] = np.inf
+    _, bh = Z.convert_weight(O.F32, dev(w.view(np.uint8)), N, K)
+    _, ah = Z.pack_activations(dev(O.activations(M, K, 2)))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    Z.gemm(ah, bh, M, N, err=err)
+    assert int(err.item()) & Z.ERR_NOT_FINITE
+
+
+def test_gemm_full_size_vs_torch_fp32():
+    # config 2's largest projection shape at M=8192 against cuBLAS fp32 on the same decoded operands
+    torch.backends.cuda.matmul.allow_tf32 = False
+    M, N, K = 8192, 9728, 2560
+    g = torch.Generator("cuda").manual_seed(5)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+    _, ah = Z.pack_activations(x)
+    _, bh = Z.convert_weight(O.F32, w.contiguous().view(torch.uint8), N, K)
+    c = Z.gemm(ah, bh, M, N)
+    a32 = (ah.to(torch.int32) << 16).view(torch.float32)
+    b32 = (bh[:N].to(torch.int32) << 16).view(torch.float32)
+    ref = a32 @ b32.T
+    err = ((c - ref).abs().max() / ref.abs().max()).item()
+    assert err <= TOL, err

@@ -1,0 +1,123 @@
+"""The matmul service zest_npu (xdna_npu's counterpart) through the C ABI:
+self-test, weight cache, y = x * W^T on host and device buffers, output
+modes, and the failure paths the reference tests with its injection
+variables (GGML_XDNA_FAIL_AFTER / GGML_XDNA_NAN_AFTER), on the host side."""
+import os
+import subprocess
+import sys
+import textwrap
+
+import numpy as np
+import pytest
+import torch
+
+import zest_b200 as Z
+from oracle import oracle as O
+from gpu_util import dev, host, bf16_to_f32
+
+pytestmark = pytest.mark.gpu
+ROOT = Z.PKG_DIR.parent
+
+
+def test_usable():
+    ok, why = Z.usable(0)
+    assert ok, why
+
+
+@pytest.mark.parametrize("qt", [O.Q8_0, O.Q4_K, O.Q6_K, O.IQ3_S])
+def test_mul_mat_host_buffers(qt):
+    Z.load_iq3s_grid()
+    npu = Z.Npu(0)
+    npu.set_out16(False)
+    N, K, T = 1024, 512, 300
+    raw = O.quantize(qt, O.weights_f32(N, K, qt))
+    x = O.activations(T, K, 1)
+    key = Z.Npu.key(raw.ctypes.data, qt, K, N)
+    npu.add_weight(key, raw.ctypes.data, on_device=False)
+    assert npu.has_weight(key) and npu.out_width(key) == N
+    y = np.empty((T, N), np.float32)
+    npu.mul_mat(key, x.ctypes.data, T, y.ctypes.data, on_device=False)
+    a_dec = O.decode_blocks(O.encode_blocks(x)).reshape(T, K)
+    w_dec = O.decode_blocks(O.encode_blocks(O.dequant(qt, raw, N, K))).reshape(N, K)
+    assert O.nmax_err(y, O.mul_mat(w_dec, a_dec)) <= 1e-3
+    t = npu.take_times()
+    assert t.calls == 1 and t.gemm_ms > 0
+    npu.close()
+
+
+def test_mul_mat_out16_and_device_buffers():
+    npu = Z.Npu(0)  # GGML_XDNA_OUT16 unset: bf16 output, as the reference's default
+    N, K, T = 512, 256, 1024
+    raw = O.quantize(O.Q8_0, O.weights_f32(N, K, 4))
+    key = Z.Npu.key(raw.ctypes.data, O.Q8_0, K, N)
+    npu.add_weight(key, raw.ctypes.data, on_device=False)
+    xd = dev(O.activations(T, K, 2))
+    yd = torch.empty((T, N), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    npu.mul_mat(key, xd.data_ptr(), T, yd.data_ptr(), on_device=True)
+    y = host(yd)
+    assert np.array_equal(y, O.round_bf16(y))  # every value a bf16
+    a_dec = O.decode_blocks(O.encode_blocks(host(xd))).reshape(T, K)
+    w_dec = O.decode_blocks(O.encode_blocks(O.dequant(O.Q8_0, raw, N, K))).reshape(N, K)
+    assert O.nmax_err(y, O.mul_mat(w_dec, a_dec)) <= 4e-3  # bf16 output rounding (2^-9) included
+    npu.close()
+
+
+def test_fused_gate_up():
+    npu = Z.Npu(0)
+    F, K, T = 1000, 512, 200
+    g = O.quantize(O.Q4_K, O.weights_f32(F, K, 1))
+    u = O.quantize(O.Q4_K, O.weights_f32(F, K, 2))
+    key = Z.Npu.key(g.ctypes.data, O.Q4_K, K, F)
+    npu.add_fused(key, g.ctypes.data, u.ctypes.data, on_device=False)
+    assert npu.out_width(key, fused=True) == F
+    x = O.activations(T, K, 3)
+    y = np.empty((T, F), np.float32)
+    npu.mul_mat(key, x.ctypes.data, T, y.ctypes.data, on_device=False, fused=True)
+    a_dec = O.decode_blocks(O.encode_blocks(x)).reshape(T, K)
+    gd = O.decode_blocks(O.encode_blocks(O.dequant(O.Q4_K, g, F, K))).reshape(F, K)
+    ud = O.decode_blocks(O.encode_blocks(O.dequant(O.Q4_K, u, F, K))).reshape(F, K)
+    want = O.swiglu_bf16(O.mul_mat(gd, a_dec), O.mul_mat(ud, a_dec))
+    assert O.nmax_err(y, want) <= 4e-3
+    npu.close()
+
+
+def _child(env_extra: dict, body: str) -> subprocess.CompletedProcess:
+    env = dict(os.environ, **env_extra)
+    code = textwrap.dedent(f"""
+        import sys
+        sys.path[:0] = [{str(ROOT)!r}, {str(ROOT / 'ggml-xdna_b200')!r}]
+        import numpy as np, zest_b200 as Z
+        from oracle import oracle as O
+        npu = Z.Npu(0)
+        N, K, T = 512, 256, 128
+        raw = O.quantize(O.Q8_0, O.weights_f32(N, K, 1))
+        key = Z.Npu.key(raw.ctypes.data, O.Q8_0, K, N)
+        npu.add_weight(key, raw.ctypes.data, on_device=False)
+        x = O.activations(T, K, 2)
+        y = np.empty((T, N), np.float32)
+    """) + textwrap.dedent(body)
+    return subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
+
+
+def test_injected_failure():
+    r = _child({"GGML_XDNA_FAIL_AFTER": "1"}, """
+        npu.mul_mat(key, x.ctypes.data, T, y.ctypes.data, on_device=False)
+        try:
+            npu.mul_mat(key, x.ctypes.data, T, y.ctypes.data, on_device=False)
+        except Z.ZestError as e:
+            print("FAILED:", e)
+    """)
+    assert r.returncode == 0, r.stderr
+    assert "FAILED:" in r.stdout and "GGML_XDNA_FAIL_AFTER" in r.stdout
+
+
+def test_injected_nan_is_caught():
+    r = _child({"GGML_XDNA_NAN_AFTER": "0"}, """
+        try:
+            npu.mul_mat(key, x.ctypes.data, T, y.ctypes.data, on_device=False)
+        except Z.ZestError as e:
+            print("FAILED:", e)
+    """)
+    assert r.returncode == 0, r.stderr
+    assert "NaN or infinity" in r.stdout
