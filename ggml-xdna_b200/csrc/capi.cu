@@ -107,7 +107,7 @@ int zest_convert_gate_up(int type, const void *gate, const void *up, int64_t row
 
 int zest_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
               int64_t K, int mode, float *c, int64_t ldc, unsigned *err, void *stream) {
-    return launch_gemm(a_bf16, lda, b_bf16, ldb, M, N, K, mode, c, ldc, err, (cudaStream_t) stream);
+    return launch_gemm(a_bf16, lda, b_bf16, ldb, M, N, K, mode, c, ldc, 0, err, (cudaStream_t) stream);
 }
 
 }  // extern "C"
@@ -410,7 +410,8 @@ int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x,
     cudaEventRecord(npu->ev[1], st);
     int rc = launch_pack_activations(xd, T, K, K, m_pad, nullptr, npu->a_bf16, K, st);
     cudaEventRecord(npu->ev[2], st);
-    if (!rc) rc = launch_gemm(npu->a_bf16, K, w->bf16, K, T, w->n_pad, K, w->mode, yd, w->n_out, npu->err_dev, st);
+    if (!rc) rc = launch_gemm(npu->a_bf16, K, w->bf16, K, T, w->n_pad, K, w->mode, yd, w->n_out, w->n_out,
+                                  npu->err_dev, st);
     if (!rc && injected_nan()) {
         cudaMemsetAsync(yd, 0xff, y_bytes, st);
         check_finite_kernel<<<148, 256, 0, st>>>(yd, T * w->n_out, npu->err_dev);

@@ -343,14 +343,15 @@ int num_sms() {
 }  // namespace
 
 int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
-                int64_t K, int mode, float *c, int64_t ldc, unsigned *err_flag, cudaStream_t st) {
+                int64_t K, int mode, float *c, int64_t ldc, int64_t n_out, unsigned *err_flag, cudaStream_t st) {
     if (M <= 0 || N <= 0) return 0;
     if (K <= 0 || K % 8 || lda < K || ldb < K || lda % 8 || ldb % 8 || ((uintptr_t) a_bf16 & 15) ||
         ((uintptr_t) b_bf16 & 15) || !err_flag)
         return set_error("gemm: K and the row strides must be multiples of 8 and the operands 16-byte aligned");
     if (mode < MODE_F32 || mode > MODE_SWIGLU || (mode == MODE_SWIGLU && N % 16))
         return set_error("gemm: bad output mode");
-    const int64_t n_out = mode == MODE_SWIGLU ? N / 2 : N;
+    const int64_t width = mode == MODE_SWIGLU ? N / 2 : N;
+    if (n_out <= 0 || n_out > width) n_out = width;
     if (ldc < n_out) return set_error("gemm: ldc smaller than the output width");
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, a_bf16, M, K, lda, BM) || !make_tmap(&tb, b_bf16, N, K, ldb, BN))

@@ -37,8 +37,10 @@ int launch_convert_weight(int type, const void *src0, const void *src1, int fuse
                           int64_t src_rows_total, int64_t K, int64_t n_pad, uint8_t *b_bytes, uint16_t *b_bf16,
                           cudaStream_t st);
 
+// n_out: output columns to write (<= 0: all, N or N/2 for SwiGLU); a fused
+// gate/up copy padded to f_pad writes only the real F.
 int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
-                int64_t K, int mode, float *c, int64_t ldc, unsigned *err_flag, cudaStream_t st);
+                int64_t K, int mode, float *c, int64_t ldc, int64_t n_out, unsigned *err_flag, cudaStream_t st);
 
 // The plain CUDA-core GEMM used by the start-up self-test as a second
 // opinion on the tensor-core kernel.
