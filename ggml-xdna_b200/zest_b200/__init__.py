@@ -60,6 +60,7 @@ def lib() -> ctypes.CDLL:
         "zest_convert_weight": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
         "zest_convert_gate_up": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
         "zest_gemm": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
+        "zest_mul_mat_noalloc": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
         "zest_usable": (_int, [_int, ctypes.c_char_p, ctypes.c_size_t]),
         "zest_open": (_vp, [_int]),
         "zest_close": (None, [_vp]),
@@ -83,7 +84,8 @@ def lib() -> ctypes.CDLL:
 
 def exported_symbols() -> list[str]:
     return [n for n in ("zest_version", "zest_last_error", "zest_load_iq3s_grid", "zest_pack_activations",
-                        "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_usable", "zest_open",
+                        "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_mul_mat_noalloc",
+                        "zest_usable", "zest_open",
                         "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
                         "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_mul_mat", "zest_stream",
                         "zest_take_times")]

@@ -103,6 +103,26 @@ int zest_convert_gate_up(int type, const void *gate, const void *up, int64_t row
 int zest_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
               int64_t K, int mode, float *c, int64_t ldc, unsigned *err, void *stream);
 
+/* K2 + K3 without allocating anything: y[T][ldy] = x[T][K] * W^T, where w_bf16
+ * is a weight's bf16 B operand (zest_convert_weight / zest_weight_bf16) of N
+ * rows and the same mode and err word as zest_gemm. No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc on this path,
+ * such as a host program whose GPU memory is planned and owned by its own
+ * allocator, or a latency-sensitive caller that cannot afford cudaMalloc /
+ * cudaFree synchronising the device mid-prompt.
+ * The bf16 copy of the activations goes to a fixed device array of
+ * ZEST_NOALLOC_MAX_VALUES values (32 MiB), held on every GPU that loads the
+ * library until the process exits; calls with roundup(T, 128) * K above that
+ * fail with a clear error. The first call on each device looks up the array's
+ * device address (with that device current); make that first call before any
+ * stream capture. Every call shares the one array, so calls that overlap on
+ * the GPU (other streams, other threads) race: serialise them. Nothing in
+ * the array needs clearing between calls: each call writes every row it
+ * reads. */
+#define ZEST_NOALLOC_MAX_VALUES (16 * 1024 * 1024)
+int zest_mul_mat_noalloc(const float *x, int64_t T, int64_t K, int64_t ldx, const uint16_t *w_bf16, int64_t ldw,
+                         int64_t N, int mode, float *y, int64_t ldy, unsigned *err, void *stream);
+
 /* ---------------------------------------------------------------------------
  * 2. The matmul service (xdna_npu)
  * ------------------------------------------------------------------------- */
