@@ -40,6 +40,7 @@ QNAME = {Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", IQ3_S: "IQ3_S"}
 # (name, N, K, input) per projection; projections sharing an input share one pack
 WORKLOADS = {
     "qwen3-4b-layer": dict(config="BASELINE configs[1]: Qwen3-4B-shaped layer, 7 projections", M=8192, qtype=Q4_K,
+                           profiled="down",
                            proj=[("q", 4096, 2560, "attn"), ("k", 1024, 2560, "attn"), ("v", 1024, 2560, "attn"),
                                  ("o", 2560, 4096, "o"), ("gate", 9728, 2560, "ffn"), ("up", 9728, 2560, "ffn"),
                                  ("down", 2560, 9728, "down")]),
@@ -108,7 +109,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
         except OSError:
@@ -214,7 +215,9 @@ def run_reference(args, w: dict) -> None:
     from oracle import oracle as O
     threads = os.cpu_count() or 1
     raws = {name: weight_raw(w["qtype"], name, N, K, threads) for name, N, K, _ in w["proj"]}
-    rows = 128
+    # rows per step: a bounded sample sized so all steps take about a minute
+    _, t16 = cpu_reference_run(w, 16, threads, raws)
+    rows = int(max(8, min(128, 16 * 60.0 / (args.steps + args.warmup) / max(t16, 1e-3))))
     for _ in range(args.warmup):
         cpu_reference_run(w, rows, threads, raws)
     fl, t = 0.0, 0.0
@@ -346,8 +349,15 @@ def run_ours(args, w: dict) -> None:
     local_gemm_flops = sum(2.0 * M * slabs[name][1] * K for name, N, K, _ in w["proj"])
     peaks = measured_peaks()
     gemm_total_ms = sum(gemm_ms)
-    achieved = local_gemm_flops / (gemm_total_ms * 1e-3) / 1e12
-    traffic = profiled_traffic("k3_gemm", args.workload)
+    # the roofline's launch: the projection with the most work (the one the
+    # committed ncu capture profiles), per launch
+    names = [p[0] for p in w["proj"]]
+    top = names.index(w["profiled"]) if w.get("profiled") in names else \
+        max(range(len(w["proj"])), key=lambda i: slabs[w["proj"][i][0]][1] * w["proj"][i][2])
+    top_name, _, top_k, _ = w["proj"][top]
+    top_flops = 2.0 * M * slabs[top_name][1] * top_k
+    achieved = top_flops / (gemm_ms[top] * 1e-3) / 1e12
+    traffic = profiled_traffic("k3_gemm", args.workload) if world == 1 else None
 
     # --- end to end through the C ABI, host buffers (N=1) ---------------------
     e2e = None
@@ -376,8 +386,11 @@ def run_ours(args, w: dict) -> None:
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["tflops_sustained"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["tflops_sustained"],
                          "traffic": traffic, "kernel": "k3 gemm_bf16_tc_kernel",
+                         "launch": f"{top_name}: {M}x{slabs[top_name][1]}x{top_k}, {top_flops / 1e9:.1f} GFLOP, "
+                                   f"{gemm_ms[top] * 1e3:.1f} us avg",
                          "peak_kind": f"bf16 sustained ({peaks['source']})", "peak_burst": peaks["tflops_burst"],
-                         "gemm_ms_per_step": gemm_total_ms},
+                         "all_gemms": {"ms_per_step": gemm_total_ms,
+                                       "tflops": local_gemm_flops / (gemm_total_ms * 1e-3) / 1e12}},
             "gpu_launches": args.steps * (len(kinds) + len(w["proj"])),
             "clocks": clocks.summary(),
         }
@@ -432,7 +445,7 @@ def e2e_run(args, w: dict, raws: dict, Z, torch) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT)

@@ -136,7 +136,9 @@ struct zest_npu {
     unsigned *err_dev = nullptr, *err_host = nullptr;
     cudaEvent_t ev[5] = {};
     zest_times times = {};
-    long long submissions = 0;
+    // whether GGML_XDNA_FAIL_AFTER / _NAN_AFTER apply: not to the start-up
+    // self-test, which the reference runs outside its injection points too
+    bool inject = true;
 
     ~zest_npu() {
         cudaSetDevice(device);
@@ -196,13 +198,15 @@ static int cuda_fail(const char *what, cudaError_t e) {
     return -1;
 }
 
+// A weight copy from raw rows of type `ctype` (the key's own type, or F32
+// for values the caller dequantised), keyed by `key`.
 static int add_copy(zest_npu *npu, const zest_wkey *key, const void *raw0, const void *raw1, int raw_on_device,
-                    int fused) {
+                    int fused, int ctype) {
     if (!npu || !key) return set_error("zest_add_weight: no service or key");
     if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_add_weight: cannot select the device");
     const int64_t K = key->K, N = key->N;
     int64_t row_bytes = 0;
-    switch (key->type) {
+    switch (ctype) {
         case TYPE_F32: row_bytes = K * 4; break;
         case TYPE_F16: row_bytes = K * 2; break;
         case TYPE_Q8_0: row_bytes = K / 32 * 34; break;
@@ -240,8 +244,8 @@ static int add_copy(zest_npu *npu, const zest_wkey *key, const void *raw0, const
     if (e == cudaSuccess) e = cudaMalloc(&w.bf16, (size_t) (w.n_pad * K) * 2);
     int rc = e == cudaSuccess ? 0 : cuda_fail("zest_add_weight: allocating the weight copy", e);
     if (!rc)
-        rc = fused ? launch_convert_weight(key->type, src0, src1, 1, N, 0, N, K, w.n_pad, w.bytes, w.bf16, npu->st)
-                   : launch_convert_weight(key->type, src0, src0, 0, N, 0, N, K, w.n_pad, w.bytes, w.bf16, npu->st);
+        rc = fused ? launch_convert_weight(ctype, src0, src1, 1, N, 0, N, K, w.n_pad, w.bytes, w.bf16, npu->st)
+                   : launch_convert_weight(ctype, src0, src0, 0, N, 0, N, K, w.n_pad, w.bytes, w.bf16, npu->st);
     cudaEventRecord(t1, npu->st);
     e = cudaStreamSynchronize(npu->st);
     if (!rc && e != cudaSuccess) rc = cuda_fail("zest_add_weight", e);
@@ -282,6 +286,7 @@ static std::string self_test(int device) {
     zest_npu *npu = zest_open(device);
     if (!npu) return std::string("cannot open the GPU (") + g_err + ")";
     zest_set_out16(npu, 0);
+    npu->inject = false;
     const zest_wkey key = { nullptr, w.data(), TYPE_F32, K, N };
     std::string why;
     if (zest_add_weight(npu, &key, w.data(), 0) || zest_mul_mat(npu, &key, 0, a.data(), M, c.data(), 0)) {
@@ -363,11 +368,15 @@ int zest_has_weight(const zest_npu *npu, const zest_wkey *key) {
 }
 
 int zest_add_weight(zest_npu *npu, const zest_wkey *key, const void *raw, int raw_on_device) {
-    return add_copy(npu, key, raw, raw, raw_on_device, 0);
+    return add_copy(npu, key, raw, raw, raw_on_device, 0, key ? key->type : -1);
+}
+
+int zest_add_weight_values(zest_npu *npu, const zest_wkey *key, const float *values, int on_device) {
+    return add_copy(npu, key, values, values, on_device, 0, TYPE_F32);
 }
 
 int zest_add_fused(zest_npu *npu, const zest_wkey *gate, const void *gate_raw, const void *up_raw, int raw_on_device) {
-    return add_copy(npu, gate, gate_raw, up_raw, raw_on_device, 1);
+    return add_copy(npu, gate, gate_raw, up_raw, raw_on_device, 1, gate ? gate->type : -1);
 }
 
 int64_t zest_out_width(const zest_npu *npu, const zest_wkey *key, int fused) {
@@ -394,7 +403,7 @@ int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x,
     if (!w) return set_error("zest_mul_mat: weight not added");
     if (T <= 0) return 0;
     if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_mul_mat: cannot select the device");
-    if (injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
+    if (npu->inject && injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
     const int64_t K = w->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
     const size_t x_bytes = (size_t) (T * K) * 4, y_bytes = (size_t) (T * w->n_out) * 4;
     if (!grow((void **) &npu->a_bf16, &npu->a_cap, (size_t) (m_pad * K) * 2) ||
@@ -412,7 +421,7 @@ int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x,
     cudaEventRecord(npu->ev[2], st);
     if (!rc) rc = launch_gemm(npu->a_bf16, K, w->bf16, K, T, w->n_pad, K, w->mode, yd, w->n_out, w->n_out,
                                   npu->err_dev, st);
-    if (!rc && injected_nan()) {
+    if (!rc && npu->inject && injected_nan()) {
         cudaMemsetAsync(yd, 0xff, y_bytes, st);
         check_finite_kernel<<<148, 256, 0, st>>>(yd, T * w->n_out, npu->err_dev);
     }

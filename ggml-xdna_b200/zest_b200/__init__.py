@@ -68,6 +68,7 @@ def lib() -> ctypes.CDLL:
         "zest_has_weight": (_int, [_vp, ctypes.POINTER(WKey)]),
         "zest_add_weight": (_int, [_vp, ctypes.POINTER(WKey), _vp, _int]),
         "zest_add_fused": (_int, [_vp, ctypes.POINTER(WKey), _vp, _vp, _int]),
+        "zest_add_weight_values": (_int, [_vp, ctypes.POINTER(WKey), _vp, _int]),
         "zest_out_width": (_i64, [_vp, ctypes.POINTER(WKey), _int]),
         "zest_weight_bfp16": (_vp, [_vp, ctypes.POINTER(WKey), _int]),
         "zest_weight_bf16": (_vp, [_vp, ctypes.POINTER(WKey), _int, ctypes.POINTER(_i64)]),
@@ -87,6 +88,7 @@ def exported_symbols() -> list[str]:
                         "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_mul_mat_noalloc",
                         "zest_usable", "zest_open",
                         "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
+                        "zest_add_weight_values",
                         "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_mul_mat", "zest_stream",
                         "zest_take_times")]
 

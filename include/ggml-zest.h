@@ -1,0 +1,38 @@
+/*
+ * The ggml backend plugin libggml-zest.so, B200 build: a drop-in for the
+ * reference's plugin of the same name (include/ggml-zest.h:1-17 there). It
+ * registers the device XDNA0, which llama.cpp selects with
+ * `-dev XDNA0,CUDA0`. XDNA0 claims large-batch weight MUL_MATs
+ * (supports_op, src/ggml-zest.cpp:1160-1226) and runs them on the B200's
+ * tensor cores in place, on the CUDA backend's device buffers.
+ *
+ * Loaded with GGML_BACKEND_PATH=libggml-zest.so, whose exports are
+ * ggml_backend_init and ggml_backend_score (GGML_BACKEND_DL_IMPL /
+ * GGML_BACKEND_DL_SCORE_IMPL, src/ggml-zest.cpp:1318-1319), or linked and
+ * registered through ggml_backend_xdna_reg.
+ */
+#ifndef GGML_ZEST_H
+#define GGML_ZEST_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GGML_XDNA_NAME "XDNA"         /* the backend (registry) name */
+#define GGML_XDNA_DEVICE_NAME "XDNA0" /* the device, as -dev names it */
+
+typedef struct ggml_backend_reg *ggml_backend_reg_t;
+struct ggml_tensor;
+
+/* Replaces: ggml_backend_xdna_reg (include/ggml-zest.h:9, src/ggml-zest.cpp:1294-1301). */
+__attribute__((visibility("default"))) ggml_backend_reg_t ggml_backend_xdna_reg(void);
+
+/* The dispatch policy alone, without the device checks: whether supports_op
+ * would claim `op` on a usable GPU (src/ggml-zest.cpp:1167-1226). For tests
+ * and for hosts that plan placement themselves; no GPU is touched. */
+__attribute__((visibility("default"))) int ggml_zest_policy_supports(const struct ggml_tensor *op);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

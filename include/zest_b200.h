@@ -166,6 +166,13 @@ int zest_has_weight(const zest_npu *npu, const zest_wkey *key);
  * Replaces: xdna_npu::add_weight (src/xdna-npu.cpp:369-378). */
 int zest_add_weight(zest_npu *npu, const zest_wkey *key, const void *raw, int raw_on_device);
 
+/* The same from the weight already dequantised to f32 rows (N x K, host
+ * memory or device memory when on_device), for GGUF types without a GPU
+ * converter here: the caller runs ggml's to_float once, as the reference
+ * does for every type (xdna_npu::unpack, src/xdna-npu.cpp:339-350). The copy
+ * is keyed by `key` (its type stays the GGUF one). */
+int zest_add_weight_values(zest_npu *npu, const zest_wkey *key, const float *values, int on_device);
+
 /* A gate and an up weight fused for SiLU(gate) * up, keyed by gate's key.
  * Replaces: xdna_npu::add_fused (src/xdna-npu.cpp:380-390). */
 int zest_add_fused(zest_npu *npu, const zest_wkey *gate, const void *gate_raw, const void *up_raw, int raw_on_device);

@@ -1,0 +1,180 @@
+"""Drives libggml-zest.so through its ggml vtables, with the stand-in
+ggml-base (libfake_ggml.so) underneath. TEST INFRASTRUCTURE ONLY.
+
+The ctypes structures mirror ggml_abi.h: ggml_tensor, the reg / device /
+backend interfaces in the slot order of the reference's initialisers.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent.parent
+FAKE = HERE / "libfake_ggml.so"
+PLUGIN = ROOT / "ggml-xdna_b200" / "libggml-zest.so"
+
+_vp, _i64, _int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+
+F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, IQ3_S, I32 = 0, 1, 2, 8, 12, 14, 21, 26
+USAGE_ANY, USAGE_WEIGHTS, USAGE_COMPUTE = 0, 1, 2
+FLAG_INPUT, FLAG_OUTPUT = 1, 2
+DEV_CPU, DEV_GPU, DEV_IGPU, DEV_ACCEL = 0, 1, 2, 3
+STATUS_FAILED, STATUS_SUCCESS = -1, 0
+BLCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210),
+        IQ3_S: (256, 110), I32: (1, 4)}
+
+
+class Tensor(ctypes.Structure):
+    _fields_ = [("type", _int), ("buffer", _vp), ("ne", _i64 * 4), ("nb", ctypes.c_size_t * 4), ("op", _int),
+                ("op_params", ctypes.c_int32 * 16), ("flags", ctypes.c_int32), ("src", _vp * 10), ("view_src", _vp),
+                ("view_offs", ctypes.c_size_t), ("data", _vp), ("name", ctypes.c_char * 64), ("extra", _vp),
+                ("padding", ctypes.c_char * 8)]
+
+
+class RegI(ctypes.Structure):
+    _fields_ = [("get_name", _vp), ("get_device_count", _vp), ("get_device", _vp), ("get_proc_address", _vp)]
+
+
+class Reg(ctypes.Structure):
+    _fields_ = [("api_version", _int), ("iface", RegI), ("context", _vp)]
+
+
+class DeviceI(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("get_name", "get_description", "get_memory", "get_type", "get_props",
+                                   "init_backend", "get_buffer_type", "get_host_buffer_type", "buffer_from_host_ptr",
+                                   "supports_op", "supports_buft", "offload_op", "event_new", "event_free",
+                                   "event_synchronize")]
+
+
+class Device(ctypes.Structure):
+    _fields_ = [("iface", DeviceI), ("reg", _vp), ("context", _vp)]
+
+
+class BackendI(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("get_name", "free", "set_tensor_async", "get_tensor_async", "set_tensor_2d_async",
+                                   "get_tensor_2d_async", "cpy_tensor_async", "synchronize", "graph_plan_create",
+                                   "graph_plan_free", "graph_plan_update", "graph_plan_compute", "graph_compute",
+                                   "event_record", "event_wait", "graph_optimize")]
+
+
+class Backend(ctypes.Structure):
+    _fields_ = [("guid", _vp), ("iface", BackendI), ("device", _vp), ("context", _vp)]
+
+
+class Caps(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_bool) for n in ("async_", "host_buffer", "buffer_from_host_ptr", "events",
+                                             "mmap_support")]
+
+
+class Props(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("description", ctypes.c_char_p), ("memory_free", ctypes.c_size_t),
+                ("memory_total", ctypes.c_size_t), ("type", _int), ("device_id", ctypes.c_char_p), ("caps", Caps)]
+
+
+def fn(ptr, restype, *argtypes):
+    return ctypes.CFUNCTYPE(restype, *argtypes)(ptr)
+
+
+class Harness:
+    """The fake ggml-base and the plugin, loaded into this process."""
+
+    def __init__(self):
+        self.fake = ctypes.CDLL(str(FAKE), mode=ctypes.RTLD_GLOBAL)
+        self.fake.fake_buffer_new.restype = _vp
+        self.fake.fake_buffer_new.argtypes = [_int, _int]
+        self.fake.fake_graph_new.restype = _vp
+        self.fake.fake_graph_new.argtypes = [_int, _vp]
+        self.fake.fake_cuda_buft.restype = _vp
+        self.fake.fake_cpu_buft.restype = _vp
+        self.fake.fake_op_id.argtypes = [ctypes.c_char_p]
+        self.plugin = ctypes.CDLL(str(PLUGIN))
+        self.plugin.ggml_backend_xdna_reg.restype = ctypes.POINTER(Reg)
+        self.plugin.ggml_backend_init.restype = ctypes.POINTER(Reg)
+        self.plugin.ggml_backend_score.restype = _int
+        self.plugin.ggml_zest_policy_supports.argtypes = [ctypes.POINTER(Tensor)]
+        self.keep = []  # ctypes objects the C side points at
+
+    # --- registry / device / backend ------------------------------------------
+    def reg(self):
+        return self.plugin.ggml_backend_xdna_reg().contents
+
+    def reg_name(self) -> str:
+        r = self.plugin.ggml_backend_xdna_reg()
+        return fn(r.contents.iface.get_name, ctypes.c_char_p, _vp)(ctypes.cast(r, _vp)).decode()
+
+    def device_count(self) -> int:
+        r = self.plugin.ggml_backend_xdna_reg()
+        return fn(r.contents.iface.get_device_count, ctypes.c_size_t, _vp)(ctypes.cast(r, _vp))
+
+    def device(self):
+        r = self.plugin.ggml_backend_xdna_reg()
+        p = fn(r.contents.iface.get_device, _vp, _vp, ctypes.c_size_t)(ctypes.cast(r, _vp), 0)
+        return p, ctypes.cast(p, ctypes.POINTER(Device)).contents
+
+    def dev_call(self, name, restype, *args, argtypes=()):
+        p, d = self.device()
+        return fn(getattr(d.iface, name), restype, _vp, *argtypes)(p, *args)
+
+    def supports_op(self, t: Tensor) -> bool:
+        return bool(self.dev_call("supports_op", ctypes.c_bool, ctypes.byref(t), argtypes=(ctypes.POINTER(Tensor),)))
+
+    def policy(self, t: Tensor) -> bool:
+        return bool(self.plugin.ggml_zest_policy_supports(ctypes.byref(t)))
+
+    def init_backend(self):
+        p = self.dev_call("init_backend", _vp, None, argtypes=(ctypes.c_char_p,))
+        return p, (ctypes.cast(p, ctypes.POINTER(Backend)).contents if p else None)
+
+    def graph_compute(self, backend_ptr, nodes: list[Tensor]) -> int:
+        arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])
+        self.keep.append(arr)
+        g = self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp))
+        b = ctypes.cast(backend_ptr, ctypes.POINTER(Backend)).contents
+        return fn(b.iface.graph_compute, _int, _vp, _vp)(backend_ptr, g)
+
+    def graph_optimize(self, backend_ptr, nodes: list[Tensor]) -> None:
+        arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])
+        self.keep.append(arr)
+        g = self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp))
+        b = ctypes.cast(backend_ptr, ctypes.POINTER(Backend)).contents
+        fn(b.iface.graph_optimize, None, _vp, _vp, _vp)(backend_ptr, g, None)
+
+    def backend_free(self, backend_ptr) -> None:
+        b = ctypes.cast(backend_ptr, ctypes.POINTER(Backend)).contents
+        fn(b.iface.free, None, _vp)(backend_ptr)
+
+    # --- tensors ---------------------------------------------------------------
+    def buffer(self, usage=USAGE_COMPUTE, host=False):
+        return self.fake.fake_buffer_new(usage, int(host))
+
+    def op(self, name: str) -> int:
+        return self.fake.fake_op_id(name.encode())
+
+    def tensor(self, type_: int, ne, name="t", buffer=None, data=None, op="NONE", src=(), view_src=None,
+               flags=0) -> Tensor:
+        t = Tensor()
+        t.type = type_
+        t.buffer = buffer
+        ne = list(ne) + [1] * (4 - len(ne))
+        blck, size = BLCK[type_]
+        t.ne[:] = ne
+        t.nb[0] = size
+        t.nb[1] = size * (ne[0] // blck)
+        t.nb[2] = t.nb[1] * ne[1]
+        t.nb[3] = t.nb[2] * ne[2]
+        t.op = self.op(op)
+        for i, s in enumerate(src):
+            t.src[i] = ctypes.cast(ctypes.pointer(s), _vp)
+        if view_src is not None:
+            t.view_src = ctypes.cast(ctypes.pointer(view_src), _vp)
+        t.data = data
+        t.name = name.encode()[:63]
+        t.flags = flags
+        self.keep.append(t)
+        return t
+
+    def mul_mat(self, w: Tensor, x: Tensor, name="mm", buffer=None, data=None) -> Tensor:
+        # ggml_mul_mat: dst ne = [w.ne1, x.ne1, x.ne2, x.ne3], f32
+        return self.tensor(F32, [w.ne[1], x.ne[1], x.ne[2], x.ne[3]], name=name, buffer=buffer, data=data,
+                           op="MUL_MAT", src=(w, x))

@@ -1,0 +1,130 @@
+"""The ggml plugin's boundary on the host (no GPU needed): registration,
+the device vtable, and the dispatch gate's truth table, mirroring the
+reference's tests/test-dispatch-gate.cpp:50-153 (with block claiming off,
+as this build claims matmuls only). The plugin is the real
+libggml-zest.so, driven through the stand-in ggml-base."""
+import ctypes
+import os
+import subprocess
+import sys
+
+import pytest
+
+sys.path.insert(0, os.path.join(os.path.dirname(__file__), "ggml_harness"))
+from harness import (DEV_IGPU, F16, F32, FLAG_INPUT, Harness, Props, Q4_0, Q4_K, Q8_0, Tensor,  # noqa: E402
+                     USAGE_COMPUTE, USAGE_WEIGHTS, fn)
+
+
+@pytest.fixture(scope="module")
+def h():
+    return Harness()
+
+
+def mm(h, wtype, k, n, batch, weight_op="NONE"):
+    w = h.tensor(wtype, [k, n], name="blk.0.attn_q.weight", buffer=h.buffer(USAGE_WEIGHTS), op=weight_op)
+    x = h.tensor(F32, [k, batch], buffer=h.buffer(USAGE_COMPUTE))
+    return h.mul_mat(w, x)
+
+
+def test_abi_sizes():
+    assert ctypes.sizeof(Tensor) == 336  # ggml_tensor on LP64
+    assert ctypes.sizeof(Props) == 56
+
+
+def test_registration(h):
+    assert h.reg_name() == "XDNA"
+    assert h.reg().api_version >= 1
+    assert h.plugin.ggml_backend_score() == 1
+    assert ctypes.addressof(h.plugin.ggml_backend_init().contents) == ctypes.addressof(h.reg())
+
+
+def test_device_vtable(h):
+    p, d = h.device()
+    assert fn(d.iface.get_name, ctypes.c_char_p, ctypes.c_void_p)(p) == b"XDNA0"
+    assert fn(d.iface.get_type, ctypes.c_int, ctypes.c_void_p)(p) == DEV_IGPU
+    free, total = ctypes.c_size_t(1), ctypes.c_size_t(0)
+    fn(d.iface.get_memory, None, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p)(p, ctypes.byref(free),
+                                                                                  ctypes.byref(total))
+    assert free.value == 0 and total.value > 0, "no free memory: llama.cpp gives it no layers"
+    props = Props()
+    fn(d.iface.get_props, None, ctypes.c_void_p, ctypes.c_void_p)(p, ctypes.byref(props))
+    assert props.name == b"XDNA0" and props.type == DEV_IGPU and not props.caps.async_ and not props.caps.events
+    buft = fn(d.iface.get_buffer_type, ctypes.c_void_p, ctypes.c_void_p)(p)
+    assert buft == h.fake.fake_cuda_buft(), "its buffer type is the CUDA backend's (no copies between them)"
+    sb = fn(d.iface.supports_buft, ctypes.c_bool, ctypes.c_void_p, ctypes.c_void_p)
+    assert sb(p, h.fake.fake_cuda_buft()) and sb(p, h.fake.fake_cpu_buft())
+    assert not d.iface.offload_op, "no offload_op: that path copies the weights per op"
+    assert not d.iface.get_host_buffer_type and not d.iface.event_new
+
+
+def test_batch_gate(h):
+    k = n = 2048
+    assert not h.policy(mm(h, Q4_K, k, n, 1)), "batch 1 (reply generation) is not claimed"
+    assert not h.policy(mm(h, Q4_K, k, n, 512)), "batch 512 is not claimed"
+    assert not h.policy(mm(h, Q4_K, k, n, 1023)), "batch 1023 is not claimed"
+    assert h.policy(mm(h, Q4_K, k, n, 1024)), "batch 1024, q4_K 2048x2048 is claimed"
+    assert h.policy(mm(h, Q4_0, k, n, 2048)), "batch 2048, q4_0 (dequantised with ggml's to_float) is claimed"
+    assert h.policy(mm(h, Q8_0, k, n, 4096))
+
+
+def test_work_floor(h):
+    # 2*1024*64*1024 = 134 MFLOP, under the 256 MFLOP floor
+    assert not h.policy(mm(h, Q4_K, 1024, 64, 1024))
+
+
+def test_weight_must_be_a_plain_leaf(h):
+    k, n = 2048, 2048
+    cache = h.tensor(F16, [k, 4 * n], buffer=h.buffer(USAGE_COMPUTE))
+    view = h.tensor(F16, [k, n], buffer=h.buffer(USAGE_COMPUTE), op="VIEW", view_src=cache)
+    x = h.tensor(F32, [k, 1024], buffer=h.buffer(USAGE_COMPUTE))
+    assert not h.policy(h.mul_mat(view, x)), "a view (a cache read) is not claimed"
+    a = h.tensor(F32, [k, n])
+    computed = h.tensor(F32, [k, n], op="ADD", src=(a, a))
+    assert not h.policy(h.mul_mat(computed, x)), "a computed left side is not claimed"
+    assert not h.policy(computed), "other ops (ADD) are not claimed"
+
+
+def test_operand_types_and_shapes(h):
+    k, n = 2048, 2048
+    w = h.tensor(Q4_K, [k, n], buffer=h.buffer(USAGE_WEIGHTS))
+    assert not h.policy(h.mul_mat(w, h.tensor(F16, [k, 1024]))), "f16 activations are not claimed"
+    assert not h.policy(h.mul_mat(w, h.tensor(F32, [k // 2, 1024]))), "mismatched K is not claimed"
+    x3 = h.tensor(F32, [k, 1024, 2])
+    assert not h.policy(h.mul_mat(w, x3)), "batched activations are not claimed"
+    # K must be a multiple of the bfp16 tile's 64 (the reference's kernel needs K % 64 too)
+    w_odd = h.tensor(Q8_0, [65 * 32, 4096], buffer=h.buffer(USAGE_WEIGHTS))
+    assert not h.policy(h.mul_mat(w_odd, h.tensor(F32, [65 * 32, 2048])))
+
+
+def test_mul_mat_id_not_claimed(h):
+    experts = h.tensor(Q4_0, [2048, 2048, 8], buffer=h.buffer(USAGE_WEIGHTS))
+    rows = h.tensor(F32, [2048, 1, 2048])
+    t = h.tensor(F32, [2048, 1, 2048], op="MUL_MAT_ID", src=(experts, rows))
+    assert not h.policy(t)
+    assert h.policy(mm(h, Q4_0, 2048, 2048, 2048)), "ordinary matmuls are still claimed afterwards"
+
+
+def test_supports_op_needs_a_usable_gpu(h):
+    # supports_op = a usable GPU (start-up self-test) and the policy; without
+    # a GPU no device is offered and nothing is claimed
+    try:
+        import torch
+        gpu = torch.cuda.is_available()
+    except ImportError:
+        gpu = False
+    t = mm(h, Q4_K, 2048, 2048, 1024)
+    assert h.device_count() == (1 if gpu else 0)
+    assert h.supports_op(t) == gpu
+
+
+def test_min_batch_env():
+    code = ("import sys; sys.path.insert(0, %r); from harness import *; h = Harness(); "
+            "w = h.tensor(Q4_K, [2048, 2048], buffer=h.buffer(USAGE_WEIGHTS)); "
+            "x = h.tensor(F32, [2048, 512]); print('CLAIMED' if h.policy(h.mul_mat(w, x)) else 'NOT')"
+            % os.path.join(os.path.dirname(__file__), "ggml_harness"))
+    env = dict(os.environ, GGML_XDNA_MIN_BATCH="512")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
+    assert "CLAIMED" in out.stdout, out.stderr
+    env = dict(os.environ, GGML_XDNA_MIN_BATCH="")  # empty means unset: the default 1024
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
+    assert "NOT" in out.stdout, out.stderr
