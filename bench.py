@@ -87,13 +87,6 @@ def weight_raw(qtype: int, name: str, N: int, K: int, threads: int) -> np.ndarra
     return quantize_threaded(qtype, O.weights_f32(N, K, seed_of(name, 1)), threads)
 
 
-def shard(N: int, world: int, rank: int) -> tuple[int, int]:
-    """This rank's N-slab [row0, row0 + n): 256-row granules spread evenly."""
-    g = (N + 255) // 256
-    lo, hi = g * rank // world * 256, min(N, g * (rank + 1) // world * 256)
-    return lo, max(0, hi - lo)
-
-
 # ---------------------------------------------------------------------------
 # clocks during the timed region
 # ---------------------------------------------------------------------------
@@ -262,11 +255,18 @@ def run_ours(args, w: dict) -> None:
         Z.load_iq3s_grid()
     M, qt = w["M"], w["qtype"]
 
-    # --- load: every projection's slab converted once (K1) -----------------
+    # tokens: every rank its own prompt chunk through whole weights (no
+    # collective); nshard: every rank an N-slab of each weight, outputs
+    # all-gathered into ggml's row-major [M][N]
+    from zest_b200.shard import gather_slabs, shard_rows, slab_width
+    nshard = world > 1 and args.mode != "tokens"
+    gather = nshard and args.mode == "nshard"
+
+    # --- load: every projection's (slab of) weight converted once (K1) ---------
     raws, bh, slabs = {}, {}, {}
     for name, N, K, _ in w["proj"]:
         raws[name] = weight_raw(qt, name, N, K, threads)
-        row0, n = shard(N, world, rank)
+        row0, n = shard_rows(N, world, rank) if nshard else (0, N)
         slabs[name] = (row0, n)
         raw_dev = torch.from_numpy(raws[name]).cuda()
         _, bh[name] = Z.convert_weight(qt, raw_dev, N, K, row0=row0, n_rows=n, want_bytes=False)
@@ -278,18 +278,19 @@ def run_ours(args, w: dict) -> None:
     for name, N, K, kind in w["proj"]:
         kinds.setdefault(kind, K)
     x, ah = {}, {}
-    gen = torch.Generator("cuda").manual_seed(1234)
+    gen = torch.Generator("cuda").manual_seed(1234 + (0 if nshard else rank))  # tokens: each rank its own chunk
     for kind, K in kinds.items():
         x[kind] = torch.randn(M, K, device="cuda", generator=gen)
         if w.get("outliers"):
             mask = torch.rand(M, K, device="cuda", generator=gen) < 0.01
             x[kind] = torch.where(mask, x[kind] * 50, x[kind])
         ah[kind] = torch.empty((Z.pad_to(M, 128), K), dtype=torch.int16, device="cuda")
-    out = {name: torch.empty((M, max(1, slabs[name][1])), dtype=torch.float32, device="cuda") for name, *_ in w["proj"]}
-    gathered = {}
-    if world > 1:
+    width = {name: (slab_width(N, world) if nshard else N) for name, N, *_ in w["proj"]}
+    out = {name: torch.zeros((M, max(1, width[name])), dtype=torch.float32, device="cuda") for name, *_ in w["proj"]}
+    full = {}
+    if gather:
         for name, N, K, _ in w["proj"]:
-            gathered[name] = torch.empty((world, M, out[name].shape[1]), dtype=torch.float32, device="cuda")
+            full[name] = torch.empty((M, N), dtype=torch.float32, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
     L = Z.lib()
@@ -312,8 +313,8 @@ def run_ours(args, w: dict) -> None:
                 events[i][1].record(stream)
             if rc:
                 raise Z.ZestError(L.zest_last_error().decode())
-            if world > 1:
-                dist.all_gather_into_tensor(gathered[name], out[name])
+            if gather:
+                gather_slabs(out[name], full[name], world, N)
 
     # --- warm-up, then K timed steps ---------------------------------------
     for _ in range(args.warmup):
@@ -345,7 +346,7 @@ def run_ours(args, w: dict) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
 
-    total_flops = flops(w)
+    total_flops = flops(w) * (1 if nshard else world)  # the whole job: all ranks' tokens
     local_gemm_flops = sum(2.0 * M * slabs[name][1] * K for name, N, K, _ in w["proj"])
     peaks = measured_peaks()
     gemm_total_ms = sum(gemm_ms)
@@ -359,10 +360,20 @@ def run_ours(args, w: dict) -> None:
     achieved = top_flops / (gemm_ms[top] * 1e-3) / 1e12
     traffic = profiled_traffic("k3_gemm", args.workload) if world == 1 else None
 
-    # --- end to end through the C ABI, host buffers (N=1) ---------------------
+    # --- end to end through the C ABI, host buffers: each rank its own chunk ----
     e2e = None
-    if world == 1:
+    if not nshard:
+        if world > 1:
+            dist.barrier()
         e2e = e2e_run(args, w, raws, Z, torch)
+        if world > 1:
+            t = torch.tensor([e2e["ms_per_step"]], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e["ms_per_step"] = float(t.item())
+            e2e["value"] = world * flops(w) / (e2e["ms_per_step"] * 1e-3) / 1e12
+            e2e["tokens_per_s"] = world * M / (e2e["ms_per_step"] * 1e-3)
+            e2e["h2d_bytes_per_step"] *= world
+            e2e["d2h_bytes_per_step"] *= world
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -373,15 +384,18 @@ def run_ours(args, w: dict) -> None:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": ("strong" if nshard else "weak") if world > 1 else "none", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
             "config": {"workload": args.workload, "desc": w["config"], "M": M, "weights": QNAME[qt],
                        "projections": {name: [N, K] for name, N, K, _ in w["proj"]},
-                       "parallelism": f"n-shard{world}" + ("+allgather" if world > 1 else ""),
+                       "parallelism": (f"n-shard{world}" + ("+allgather" if gather else "")) if nshard else
+                                      f"tokens{world} (each GPU its own {M}-token chunk, no collective)",
+                       "global_tokens_per_step": M * (1 if nshard else world),
                        "output": "f32 holding bf16-rounded values (reference default GGML_XDNA_OUT16=1)",
                        "l2": "no flush: each step reads %.0f MB of inputs and weights (> 126 MB L2)" %
                              (sum(M * K * 4 for K in kinds.values()) / 1e6 +
                               sum(slabs[n][1] * K * 2 for n, N, K, _ in w["proj"]) / 1e6)},
-            "tokens_per_s": M / (ms_max * 1e-3),
+            "tokens_per_s": M * (1 if nshard else world) / (ms_max * 1e-3),
             "pct_of_bf16_peak": 100.0 * value / peaks["tflops_sustained"],
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["tflops_sustained"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["tflops_sustained"],
@@ -450,6 +464,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--mode", choices=["tokens", "nshard", "nshard-nogather"], default="tokens",
+                    help="N>1: each GPU its own token chunk (default, no collective), or N-slabs of every weight "
+                         "with (nshard) or without the NCCL all-gather of the output slabs")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
     w = WORKLOADS[args.workload]

@@ -1,0 +1,42 @@
+"""N-sharding of a MUL_MAT across GPUs: each rank converts and multiplies
+its slab of weight rows (output columns); an all-gather of the slab outputs
+over NCCL (gloo on CPU) rebuilds ggml's row-major [M][N] on every rank.
+
+The reference runs on one NPU and has no counterpart; this is the
+partitioning its GEMM admits (output columns are independent).
+"""
+from __future__ import annotations
+
+GRANULE = 128  # rows per shard granule: whole GEMM tile rows, and 16-row pack units
+
+
+def shard_rows(N: int, world: int, rank: int, granule: int = GRANULE) -> tuple[int, int]:
+    """This rank's slab [row0, row0 + n) of N weight rows, in whole granules
+    spread as evenly as they go (the last slab takes the ragged end)."""
+    g = (N + granule - 1) // granule
+    lo = g * rank // world * granule
+    hi = min(N, g * (rank + 1) // world * granule)
+    return lo, max(0, hi - lo)
+
+
+def slab_width(N: int, world: int, granule: int = GRANULE) -> int:
+    """The widest slab: every rank's output is padded to it for the gather."""
+    return max(shard_rows(N, world, r, granule)[1] for r in range(world))
+
+
+def gather_slabs(slab_out, full_out, world: int, N: int, group=None, granule: int = GRANULE):
+    """slab_out: this rank's [M][slab_width] output (columns past its slab
+    unused); full_out: [M][N]. All-gathers the slabs and writes them into
+    their columns of full_out. Collective: every rank calls it, in order."""
+    import torch
+    import torch.distributed as dist
+
+    M, w = slab_out.shape
+    flat = torch.empty((world * M, w), dtype=slab_out.dtype, device=slab_out.device)
+    dist.all_gather_into_tensor(flat, slab_out.contiguous(), group=group)
+    gathered = flat.view(world, M, w)
+    for r in range(world):
+        lo, n = shard_rows(N, world, r, granule)
+        if n:
+            full_out[:, lo:lo + n].copy_(gathered[r, :, :n])
+    return full_out

@@ -1,0 +1,77 @@
+"""The N>1 host logic on CPU: world_size-2 gloo ranks, each multiplying its
+slab of weight rows (the oracle stands in for the GPU kernels), then the
+all-gather of slab outputs rebuilds the full row-major product on every rank."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from zest_b200.shard import shard_rows, slab_width
+
+
+def test_shards_cover_rows_exactly():
+    for N in (1, 127, 128, 1024, 2560, 9728, 17408):
+        for world in (1, 2, 4, 8):
+            spans = [shard_rows(N, world, r) for r in range(world)]
+            covered = []
+            for lo, n in spans:
+                covered.extend(range(lo, lo + n))
+            assert covered == list(range(N)), (N, world)
+            assert all(lo % 128 == 0 for lo, n in spans if n)
+            assert slab_width(N, world) == max(n for _, n in spans)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank: int, world: int, port: int, q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root), str(root / "ggml-xdna_b200")]
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+    from zest_b200.shard import gather_slabs, shard_rows, slab_width
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        M, N, K = 64, 1000, 256
+        raw = O.quantize(O.Q8_0, O.weights_f32(N, K, 1))
+        W = O.dequant(O.Q8_0, raw, N, K)
+        X = O.activations(M, K, 2)
+        lo, n = shard_rows(N, world, rank)
+        w = slab_width(N, world)
+        slab = torch.zeros((M, w), dtype=torch.float32)
+        if n:
+            slab[:, :n] = torch.from_numpy(O.mul_mat(W[lo:lo + n], X))
+        full = torch.full((M, N), float("nan"))
+        gather_slabs(slab, full, world, N)
+        want = O.mul_mat(W, X)
+        q.put((rank, bool(np.array_equal(full.numpy(), want))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_rebuilds_row_major_product_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    results = dict(q.get(timeout=10) for _ in range(world))
+    assert all(p.exitcode == 0 for p in procs)
+    assert results == {0: True, 1: True}
