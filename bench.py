@@ -396,7 +396,7 @@ def run_ours(args, w: dict) -> None:
                              (sum(M * K * 4 for K in kinds.values()) / 1e6 +
                               sum(slabs[n][1] * K * 2 for n, N, K, _ in w["proj"]) / 1e6)},
             "tokens_per_s": M * (1 if nshard else world) / (ms_max * 1e-3),
-            "pct_of_bf16_peak": 100.0 * value / peaks["tflops_sustained"],
+            "pct_of_bf16_peak": 100.0 * value / (world * peaks["tflops_sustained"]),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["tflops_sustained"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["tflops_sustained"],
                          "traffic": traffic, "kernel": "k3 gemm_bf16_tc_kernel",
