@@ -291,10 +291,150 @@ bool claim_mul_mat(const ggml_tensor *op) {
     return mflop >= min_mflop() && budget_takes(src0);
 }
 
-// The whole policy. Block claiming of the small ops around our matmuls is
-// not built yet, so this claims matmuls only (the reference with
-// GGML_XDNA_BLOCKS=0).
-bool policy(const ggml_tensor *op) { return op_is(op, "MUL_MAT") && claim_mul_mat(op); }
+// --- block claiming: the small ops next to our matmuls
+// (src/xdna-exec.cpp:85-131, src/ggml-zest.cpp:1131-1226) ------------------
+
+int32_t param_i32(const ggml_tensor *t, int i) { return t->op_params[i]; }
+float param_f32(const ggml_tensor *t, int i) {
+    float v;
+    memcpy(&v, &t->op_params[i], sizeof v);
+    return v;
+}
+
+bool same_shape(const ggml_tensor *a, const ggml_tensor *b) {
+    return a->ne[0] == b->ne[0] && a->ne[1] == b->ne[1] && a->ne[2] == b->ne[2] && a->ne[3] == b->ne[3];
+}
+
+bool f32_contig(const ggml_tensor *t) { return t && t->type == GGML_TYPE_F32 && ggml_is_contiguous(t); }
+
+// a single row as wide as a's rows (a norm's scale, a bias), broadcast over every row of a
+bool is_row_of(const ggml_tensor *r, const ggml_tensor *a) {
+    return f32_contig(r) && r->ne[0] == a->ne[0] && r->ne[1] == 1 && r->ne[2] == 1 && r->ne[3] == 1;
+}
+
+// Rows are prompt tokens, along a tensor's last dimension in use.
+int64_t tokens_of(const ggml_tensor *t) { return t->ne[3] > 1 ? t->ne[3] : t->ne[2] > 1 ? t->ne[2] : t->ne[1]; }
+
+bool glu_kind(int g) {
+    return g == ZEST_GLU_SWIGLU || g == ZEST_GLU_GEGLU || g == ZEST_GLU_GEGLU_ERF || g == ZEST_GLU_GEGLU_QUICK ||
+           g == ZEST_GLU_REGLU;
+}
+
+// The input an op keeps as a parameter (a scale or bias row, rope's
+// frequency factors); null for none (src/xdna-exec.cpp:85-95).
+const ggml_tensor *exec_param(const ggml_tensor *op) {
+    if (op_is(op, "MUL")) return op->src[1];
+    if (op_is(op, "ADD"))
+        return op->src[1] && op->src[0] && is_row_of(op->src[1], op->src[0]) && !same_shape(op->src[0], op->src[1])
+                   ? op->src[1]
+                   : nullptr;
+    if (op_is(op, "ROPE")) return op->src[2];
+    return nullptr;
+}
+
+// Whether the GPU runs this op in this variant (src/xdna-exec.cpp:97-131).
+bool exec_supports(const ggml_tensor *op) {
+    const ggml_tensor *a = op->src[0], *b = op->src[1];
+    if (op_is(op, "MUL_MAT")) return true;
+    if (op_is(op, "RESHAPE")) return a && ggml_is_contiguous(a);
+    if (op_is(op, "RMS_NORM")) return f32_contig(a) && f32_contig(op);
+    if (op_is(op, "MUL")) return f32_contig(a) && f32_contig(op) && is_row_of(b, a) && same_shape(a, op);
+    if (op_is(op, "ADD"))
+        return f32_contig(a) && f32_contig(b) && f32_contig(op) && same_shape(a, op) &&
+               (same_shape(a, b) || is_row_of(b, a));
+    if (op_is(op, "SCALE")) return f32_contig(a) && f32_contig(op) && same_shape(a, op);
+    if (op_is(op, "GLU")) {
+        if (!glu_kind(param_i32(op, 0)) || !f32_contig(a) || !f32_contig(op)) return false;
+        if (b) return param_i32(op, 1) == 0 && f32_contig(b) && same_shape(a, b) && same_shape(a, op);
+        return a->ne[0] == 2 * op->ne[0] && ggml_nrows(a) == ggml_nrows(op);
+    }
+    if (op_is(op, "ROPE")) {
+        if (!f32_contig(a) || !f32_contig(op) || !b || b->type != GGML_TYPE_I32) return false;
+        const int n_dims = param_i32(op, 1), mode = param_i32(op, 2), n_offs = param_i32(op, 15);
+        const ggml_tensor *ff = op->src[2];
+        if (ff && (!f32_contig(ff) || ff->ne[0] < n_dims / 2)) return false;
+        return (mode == ZEST_ROPE_NEOX || mode == ZEST_ROPE_NORMAL) && n_dims > 0 && n_dims % 2 == 0 &&
+               n_dims <= a->ne[0] && n_offs == 0 && a->ne[3] == 1 && b->ne[0] == a->ne[2];
+    }
+    return false;
+}
+
+// Block claiming on, unless GGML_XDNA_BLOCKS=0 (src/ggml-zest.cpp:1131-1140).
+bool blocks() {
+    static const bool v = env_int("GGML_XDNA_BLOCKS", 1) != 0;
+    return v;
+}
+
+// Whether a tensor may live in host memory once allocated: a graph input, an
+// embedding lookup, or one in a host buffer (src/ggml-zest.cpp:1149-1158).
+bool maybe_host(const ggml_tensor *t) {
+    for (; t; t = t->view_src) {
+        if ((t->flags & GGML_TENSOR_FLAG_INPUT) || op_is(t, "GET_ROWS")) return true;
+        if (t->buffer && ggml_backend_buffer_is_host(t->buffer)) return true;
+    }
+    return false;
+}
+
+// Who reads what, as the scheduler shows us (src/ggml-zest.cpp:1074-1109):
+// every supports_op question carries the op's inputs. A fused matmul skips
+// writing its own result only when nothing outside its piece reads it.
+std::mutex g_read_mu;
+std::unordered_map<const ggml_tensor *, std::vector<const ggml_tensor *>> g_readers;
+
+void note_readers(const ggml_tensor *op) {
+    std::lock_guard<std::mutex> lk(g_read_mu);
+    for (int j = 0; j < GGML_MAX_SRC; j++)
+        if (const ggml_tensor *s = op->src[j]) {
+            auto &r = g_readers[s];
+            if (std::find(r.begin(), r.end(), op) == r.end()) r.push_back(op);
+            for (const ggml_tensor *v = s->view_src; v; v = v->view_src) {
+                auto &rv = g_readers[v];
+                if (std::find(rv.begin(), rv.end(), op) == rv.end()) rv.push_back(op);
+            }
+        }
+}
+
+template <typename Set>
+bool read_outside(const ggml_tensor *t, const Set &in_piece) {
+    static const bool all = env_int("GGML_XDNA_WRITE_ALL", 0) != 0;
+    if (all || (t->flags & GGML_TENSOR_FLAG_OUTPUT)) return true;
+    std::lock_guard<std::mutex> lk(g_read_mu);
+    auto it = g_readers.find(t);
+    if (it == g_readers.end()) return true;
+    for (const ggml_tensor *r : it->second)
+        if (!in_piece.count(r)) return true;
+    return false;
+}
+
+// The whole policy (src/ggml-zest.cpp:1182-1226): a matmul we can take, or a
+// small op the GPU runs that covers a prompt-sized batch, keeps its
+// parameters in plain leaves, cannot have its result placed in host memory,
+// and is fed by an op we claim.
+bool policy(const ggml_tensor *op, int depth = 0) {
+    if (op_is(op, "MUL_MAT")) return claim_mul_mat(op);
+    if (!blocks() || depth > 8) return false;
+    if (!op_is(op, "RESHAPE") && tokens_of(op) < min_batch()) return false;
+    if (!exec_supports(op)) return false;
+    {
+        // GGML_XDNA_BLOCK_OPS: a comma list of the small ops block claiming may take
+        static const std::string allow = [] {
+            const char *s = zenv("GGML_XDNA_BLOCK_OPS");
+            return s ? "," + std::string(s) + "," : std::string();
+        }();
+        if (!allow.empty() && allow.find("," + std::string(ggml_op_name(op->op)) + ",") == std::string::npos)
+            return false;
+    }
+    if (const ggml_tensor *w = exec_param(op))
+        if (w->op != GGML_OP_NONE || w->view_src) return false;
+    for (int j = 0; j < GGML_MAX_SRC; j++)
+        if (const ggml_tensor *s = op->src[j])
+            if (maybe_host(s) && same_shape(op, s)) return false;
+    for (int j = 0; j < GGML_MAX_SRC; j++) {
+        const ggml_tensor *s = op->src[j];
+        if (s && s->op != GGML_OP_NONE && policy(s, depth + 1)) return true;
+    }
+    return false;
+}
 
 // ---------------------------------------------------------------------------
 // the backend context (src/ggml-zest.cpp:184-423)
@@ -306,14 +446,36 @@ struct context {
     std::vector<uint8_t> host_raw;
     float *stage_x = nullptr, *stage_y = nullptr;
     size_t stage_x_cap = 0, stage_y_cap = 0;
+    // device copies of a piece's host-memory tensors (rotary positions),
+    // slot by slot, reused from piece to piece
+    std::vector<std::pair<void *, size_t>> stage;
+    size_t stage_next = 0;
+    float *rope_table = nullptr;
+    size_t rope_cap = 0;
     // where the time goes, printed with GGML_XDNA_TRACE=1
     double compute_ms = 0, copy_ms = 0;
-    int64_t matmuls = 0, pieces = 0, late_copies = 0;
+    int64_t matmuls = 0, pieces = 0, late_copies = 0, small_ops = 0, fused = 0;
+
+    void *stage_slot(size_t n) {
+        if (stage_next == stage.size()) stage.emplace_back(nullptr, 0);
+        auto &s = stage[stage_next];
+        if (s.second < n) {
+            cudaFree(s.first);
+            s.first = nullptr;
+            s.second = 0;
+            if (cudaMalloc(&s.first, n) != cudaSuccess) return nullptr;
+            s.second = n;
+        }
+        stage_next++;
+        return s.first;
+    }
 
     ~context() {
         if (npu) zest_close(npu);
         cudaFree(stage_x);
         cudaFree(stage_y);
+        cudaFree(rope_table);
+        for (auto &s : stage) cudaFree(s.first);
     }
 };
 
@@ -425,6 +587,132 @@ void backend_free(ggml_backend_t backend) {
     if (--g_budget.contexts == 0) g_budget.reset();
 }
 
+const ggml_tensor *owner(const ggml_tensor *t) {
+    while (t->view_src) t = t->view_src;
+    return t;
+}
+
+// SiLU(gate) * up as one GEMM (output mode 2): a SwiGLU whose gate and up are
+// matmuls of this piece on the same input, read by nothing else, or one
+// matmul whose weight holds the gate's rows and then the up's
+// (find_fusions, src/xdna-exec.cpp:392-431).
+struct fusion {
+    ggml_tensor *gate, *up, *glu;  // up: null for one weight holding both
+};
+
+template <typename Set>
+std::vector<fusion> find_fusions(const std::vector<ggml_tensor *> &nodes, const Set &in_piece) {
+    std::vector<fusion> out;
+    for (ggml_tensor *n : nodes) {
+        if (!op_is(n, "GLU") || param_i32(n, 0) != ZEST_GLU_SWIGLU || param_i32(n, 1) != 0) continue;
+        ggml_tensor *gm = n->src[0], *um = n->src[1];
+        if (!op_is(gm, "MUL_MAT") || !in_piece.count(gm) || read_outside(gm, in_piece)) continue;
+        if (!native_type(gm->src[0]->type)) continue;
+        if (um) {
+            if (!op_is(um, "MUL_MAT") || !in_piece.count(um) || read_outside(um, in_piece)) continue;
+            if (owner(gm->src[1]) != owner(um->src[1]) || gm->src[0]->type != um->src[0]->type ||
+                !same_shape(gm->src[0], um->src[0]))
+                continue;
+        } else if (gm->src[0]->ne[1] % 2 != 0) {
+            continue;
+        }
+        bool other = false;  // another reader in the piece
+        for (ggml_tensor *m : nodes)
+            for (int j = 0; j < GGML_MAX_SRC && m != n; j++)
+                if (m->src[j] && (owner(m->src[j]) == gm || (um && owner(m->src[j]) == um))) other = true;
+        if (!other) out.push_back({ gm, um, n });
+    }
+    return out;
+}
+
+bool ensure_fused(context &ctx, const fusion &f, zest_wkey &key, std::string &err) {
+    const ggml_tensor *g = f.gate->src[0];
+    key = { g->buffer, g->data, (int) g->type, g->ne[0], f.up ? g->ne[1] : g->ne[1] / 2 };
+    if (zest_out_width(ctx.npu, &key, 1) >= 0) return true;
+    const char *up_raw = f.up ? (const char *) f.up->src[0]->data : (const char *) g->data + key.N * g->nb[1];
+    const auto t0 = std::chrono::steady_clock::now();
+    const int rc = zest_add_fused(ctx.npu, &key, g->data, up_raw, is_host(g) ? 0 : 1);
+    ctx.copy_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (rc) err = std::string(g->name) + ": " + zest_last_error();
+    return rc == 0;
+}
+
+// A tensor's bytes on the device: in place, or a staged copy of a
+// host-memory tensor (a graph input such as the rotary positions).
+const void *device_in(context &ctx, const ggml_tensor *t, cudaStream_t st) {
+    if (!t || !is_host(t)) return t ? t->data : nullptr;
+    const size_t n = ggml_nbytes(t);
+    void *d = ctx.stage_slot(n);
+    if (!d || cudaMemcpyAsync(d, t->data, n, cudaMemcpyHostToDevice, st) != cudaSuccess) return nullptr;
+    return d;
+}
+
+// One small op on the GPU, on the service's stream (run_rows,
+// src/xdna-exec.cpp:253-346).
+bool small_op(context &ctx, ggml_tensor *n, std::string &err) {
+    cudaStream_t st = (cudaStream_t) zest_stream(ctx.npu);
+    const ggml_tensor *a = n->src[0], *b = n->src[1];
+    const float *x = (const float *) device_in(ctx, a, st);
+    float *y = is_host(n) ? (float *) ctx.stage_slot(ggml_nbytes(n)) : (float *) n->data;
+    if (!x || !y) {
+        err = std::string(n->name) + ": cannot stage a host tensor";
+        return false;
+    }
+    int rc = -1;
+    const int64_t d = a->ne[0], rows = ggml_nrows(a);
+    if (op_is(n, "RMS_NORM")) {
+        rc = zest_rms_norm(x, rows, d, param_f32(n, 0), y, st);
+    } else if (op_is(n, "MUL")) {
+        rc = zest_mul_row(x, (const float *) device_in(ctx, b, st), rows, d, y, st);
+    } else if (op_is(n, "ADD")) {
+        rc = zest_add(x, (const float *) device_in(ctx, b, st), same_shape(a, b) ? 0 : 1, rows, d, y, st);
+    } else if (op_is(n, "SCALE")) {
+        rc = zest_scale(x, rows * d, param_f32(n, 0), param_f32(n, 1), y, st);
+    } else if (op_is(n, "GLU")) {
+        const int kind = param_i32(n, 0);
+        const int64_t f = n->ne[0], out_rows = ggml_nrows(n);
+        if (b) {
+            rc = zest_glu(kind, x, f, (const float *) device_in(ctx, b, st), f, out_rows, f, y, st);
+        } else {
+            const bool swapped = param_i32(n, 1) != 0;
+            rc = zest_glu(kind, x + (swapped ? f : 0), 2 * f, x + (swapped ? 0 : f), 2 * f, out_rows, f, y, st);
+        }
+    } else if (op_is(n, "ROPE")) {
+        const int n_dims = param_i32(n, 1), mode = param_i32(n, 2), n_ctx_orig = param_i32(n, 4);
+        const int64_t T = a->ne[2];
+        const float par[6] = { param_f32(n, 5), param_f32(n, 6), param_f32(n, 7),
+                               param_f32(n, 8), param_f32(n, 9), param_f32(n, 10) };
+        const size_t tb = (size_t) (T * n_dims) * sizeof(float);
+        if (tb > ctx.rope_cap) {
+            cudaFree(ctx.rope_table);
+            ctx.rope_table = nullptr;
+            ctx.rope_cap = 0;
+            if (cudaMalloc(&ctx.rope_table, tb) != cudaSuccess) {
+                err = "cannot allocate the rope table";
+                return false;
+            }
+            ctx.rope_cap = tb;
+        }
+        const int32_t *pos = (const int32_t *) device_in(ctx, b, st);
+        const float *ff = (const float *) device_in(ctx, n->src[2], st);
+        rc = zest_rope_table(pos, T, n_dims, n_ctx_orig, par, ff, ctx.rope_table, st);
+        if (!rc) rc = zest_rope(x, T, a->ne[1], a->ne[0], n_dims, mode, ctx.rope_table, y, st);
+    } else {
+        err = std::string("unsupported op ") + ggml_op_name(n->op);
+        return false;
+    }
+    if (rc) {
+        err = std::string(n->name) + ": " + zest_last_error();
+        return false;
+    }
+    if (is_host(n) && cudaMemcpyAsync(n->data, y, ggml_nbytes(n), cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+        err = std::string(n->name) + ": cannot write the result back";
+        return false;
+    }
+    ctx.small_ops++;
+    return true;
+}
+
 enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgraph) {
     context &ctx = *(context *) backend->context;
     {
@@ -435,23 +723,64 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(cuda_device());
+    ctx.stage_next = 0;
     enum ggml_status status = GGML_STATUS_SUCCESS;
+    std::vector<ggml_tensor *> nodes;
     const int n = ggml_graph_n_nodes(cgraph);
-    for (int i = 0; i < n && status == GGML_STATUS_SUCCESS; i++) {
+    for (int i = 0; i < n; i++) {
         ggml_tensor *node = ggml_graph_node(cgraph, i);
-        if (op_is(node, "NONE") || op_is(node, "RESHAPE") || op_is(node, "VIEW") || op_is(node, "PERMUTE") ||
-            op_is(node, "TRANSPOSE"))
-            continue;
+        if (!(op_is(node, "NONE") || op_is(node, "RESHAPE") || op_is(node, "VIEW") || op_is(node, "PERMUTE") ||
+              op_is(node, "TRANSPOSE")))
+            nodes.push_back(node);
+    }
+    std::unordered_map<const ggml_tensor *, int> in_piece_map;
+    for (int i = 0; i < n; i++) in_piece_map[ggml_graph_node(cgraph, i)] = i;
+    struct piece_set {
+        const std::unordered_map<const ggml_tensor *, int> &m;
+        size_t count(const ggml_tensor *t) const { return m.count(t); }
+    } in_piece{ in_piece_map };
+    const std::vector<fusion> fusions = blocks() ? find_fusions(nodes, in_piece) : std::vector<fusion>();
+    std::unordered_map<const ggml_tensor *, const fusion *> fused_gate;
+    std::unordered_map<const ggml_tensor *, bool> fused_skip;
+    for (const fusion &f : fusions) {
+        fused_gate[f.gate] = &f;
+        if (f.up) fused_skip[f.up] = true;
+        fused_skip[f.glu] = true;
+    }
+    cudaStream_t st = (cudaStream_t) zest_stream(ctx.npu);
+    for (ggml_tensor *node : nodes) {
+        if (status != GGML_STATUS_SUCCESS) break;
         std::string err;
-        if (op_is(node, "MUL_MAT")) {
-            if (!mul_mat(ctx, node, err)) {
-                failed(err);
-                status = GGML_STATUS_FAILED;
+        bool ok;
+        if (fused_skip.count(node)) continue;
+        if (auto it = fused_gate.find(node); it != fused_gate.end()) {
+            const fusion &f = *it->second;
+            zest_wkey key;
+            const ggml_tensor *x = f.gate->src[1];
+            ok = ensure_fused(ctx, f, key, err);
+            if (ok && (is_host(x) || is_host(f.glu))) {
+                err = "a fused SwiGLU with host-memory operands";
+                ok = false;
             }
+            if (ok && zest_mul_mat(ctx.npu, &key, 1, (const float *) x->data, x->ne[1], (float *) f.glu->data, 1)) {
+                err = std::string(f.glu->name) + ": " + zest_last_error();
+                ok = false;
+            }
+            ctx.matmuls += f.up ? 2 : 1;
+            ctx.fused++;
+        } else if (op_is(node, "MUL_MAT")) {
+            ok = mul_mat(ctx, node, err);
         } else {
-            log_line("", std::string("unsupported op ") + ggml_op_name(node->op));
+            ok = small_op(ctx, node, err);
+        }
+        if (!ok) {
+            failed(err);
             status = GGML_STATUS_FAILED;
         }
+    }
+    if (cudaStreamSynchronize(st) != cudaSuccess && status == GGML_STATUS_SUCCESS) {
+        failed(std::string("a kernel failed: ") + cudaGetErrorString(cudaGetLastError()));
+        status = GGML_STATUS_FAILED;
     }
     cudaSetDevice(prev);
     ctx.compute_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -481,15 +810,41 @@ void backend_graph_optimize(ggml_backend_t backend, ggml_cgraph *cgraph, ggml_ba
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(cuda_device());
+    // the copies the piece will use, as running it would make them
+    // (xdna_exec_weights, src/xdna-exec.cpp:435-448): fused gate/up pairs once
+    std::vector<ggml_tensor *> nodes;
+    std::unordered_map<const ggml_tensor *, int> in_piece_map;
     for (int i = 0; i < n; i++) {
-        const ggml_tensor *node = ggml_graph_node(cgraph, i);
+        ggml_tensor *node = ggml_graph_node(cgraph, i);
+        in_piece_map[node] = i;
+        if (!op_is(node, "NONE")) nodes.push_back(node);
+    }
+    struct piece_set {
+        const std::unordered_map<const ggml_tensor *, int> &m;
+        size_t count(const ggml_tensor *t) const { return m.count(t); }
+    } in_piece{ in_piece_map };
+    std::unordered_map<const ggml_tensor *, const fusion *> fused;
+    const std::vector<fusion> fusions = blocks() ? find_fusions(nodes, in_piece) : std::vector<fusion>();
+    for (const fusion &f : fusions) {
+        fused[f.gate] = &f;
+        if (f.up) fused[f.up] = nullptr;
+    }
+    for (const ggml_tensor *node : nodes) {
         if (!op_is(node, "MUL_MAT")) continue;
         const ggml_tensor *w = node->src[0];
         // llama.cpp's memory-fitting trial loads no weight data: nothing to build
         if (!w || !w->data || !w->buffer || ggml_backend_buffer_get_usage(w->buffer) != GGML_BACKEND_BUFFER_USAGE_WEIGHTS)
             continue;
         std::string err;
-        if (!ensure_weight(ctx, w, err)) {
+        bool ok = true;
+        auto it = fused.find(node);
+        if (it == fused.end()) {
+            ok = ensure_weight(ctx, w, err);
+        } else if (it->second) {
+            zest_wkey key;
+            ok = ensure_fused(ctx, *it->second, key, err);
+        }
+        if (!ok) {
             failed("building a weight copy at load: " + err);
             break;
         }
@@ -566,6 +921,7 @@ ggml_backend_t dev_init_backend(ggml_backend_dev_t dev, const char *) {
 ggml_backend_buffer_type_t dev_get_buffer_type(ggml_backend_dev_t) { return sibling().buft; }
 
 bool dev_supports_op(ggml_backend_dev_t, const ggml_tensor *op) {
+    if (blocks()) note_readers(op);
     if (!sibling().dev || g_broken || !gpu_usable()) return false;
     return policy(op);
 }

@@ -61,6 +61,13 @@ def lib() -> ctypes.CDLL:
         "zest_convert_gate_up": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
         "zest_gemm": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
         "zest_mul_mat_noalloc": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
+        "zest_rms_norm": (_int, [_vp, _i64, _i64, ctypes.c_float, _vp, _vp]),
+        "zest_mul_row": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
+        "zest_add": (_int, [_vp, _vp, _int, _i64, _i64, _vp, _vp]),
+        "zest_scale": (_int, [_vp, _i64, ctypes.c_float, ctypes.c_float, _vp, _vp]),
+        "zest_glu": (_int, [_int, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp]),
+        "zest_rope_table": (_int, [_vp, _i64, _int, _int, ctypes.POINTER(ctypes.c_float), _vp, _vp, _vp]),
+        "zest_rope": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp]),
         "zest_usable": (_int, [_int, ctypes.c_char_p, ctypes.c_size_t]),
         "zest_open": (_vp, [_int]),
         "zest_close": (None, [_vp]),
@@ -86,6 +93,8 @@ def lib() -> ctypes.CDLL:
 def exported_symbols() -> list[str]:
     return [n for n in ("zest_version", "zest_last_error", "zest_load_iq3s_grid", "zest_pack_activations",
                         "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_mul_mat_noalloc",
+                        "zest_rms_norm", "zest_mul_row", "zest_add", "zest_scale", "zest_glu", "zest_rope_table",
+                        "zest_rope",
                         "zest_usable", "zest_open",
                         "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
                         "zest_add_weight_values",

@@ -123,6 +123,39 @@ int zest_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64
 int zest_mul_mat_noalloc(const float *x, int64_t T, int64_t K, int64_t ldx, const uint16_t *w_bf16, int64_t ldw,
                          int64_t N, int mode, float *y, int64_t ldy, unsigned *err, void *stream);
 
+/* The block executor's small ops, on device rows of d contiguous floats,
+ * float arithmetic in the reference's order.
+ * Replaces: the host passes' run_rows (src/xdna-exec.cpp:253-346) and its
+ * rope table (src/xdna-exec.cpp:194-239), for the ops xdna_exec_supports
+ * admits (src/xdna-exec.cpp:97-131). */
+#define ZEST_GLU_REGLU 0 /* ggml_glu_op ids */
+#define ZEST_GLU_GEGLU 1
+#define ZEST_GLU_SWIGLU 2
+#define ZEST_GLU_GEGLU_ERF 4
+#define ZEST_GLU_GEGLU_QUICK 5
+#define ZEST_ROPE_NORMAL 0 /* ggml rope modes */
+#define ZEST_ROPE_NEOX 2
+/* y = x / sqrt(mean(x^2) + eps), per row of d (RMS_NORM) */
+int zest_rms_norm(const float *x, int64_t rows, int64_t d, float eps, float *y, void *stream);
+/* y = x * w, w one row of d broadcast over every row (MUL by a norm's scale) */
+int zest_mul_row(const float *x, const float *w, int64_t rows, int64_t d, float *y, void *stream);
+/* y = x + b, b the same shape or (bias_row) one row of d (ADD) */
+int zest_add(const float *x, const float *b, int bias_row, int64_t rows, int64_t d, float *y, void *stream);
+/* y = x * s + bias (SCALE) */
+int zest_scale(const float *x, int64_t n, float s, float bias, float *y, void *stream);
+/* y = act(g) * u row by row, g and u with their own row strides (GLU: split
+ * tensors, or the two halves of one tensor) */
+int zest_glu(int kind, const float *g, int64_t g_stride, const float *u, int64_t u_stride, int64_t rows, int64_t f,
+             float *y, void *stream);
+/* the [T][n_dims] cos/sin table of positions pos (device), YaRN and optional
+ * per-frequency factors ff (device, may be NULL); par (host) = freq_base,
+ * freq_scale, ext_factor, attn_factor, beta_fast, beta_slow */
+int zest_rope_table(const int32_t *pos, int64_t T, int n_dims, int n_ctx_orig, const float *par, const float *ff,
+                    float *table, void *stream);
+/* x [T][heads][d] -> y, the first n_dims of each head rotated (ROPE) */
+int zest_rope(const float *x, int64_t T, int64_t heads, int64_t d, int n_dims, int mode, const float *table, float *y,
+              void *stream);
+
 /* ---------------------------------------------------------------------------
  * 2. The matmul service (xdna_npu)
  * ------------------------------------------------------------------------- */

@@ -313,3 +313,85 @@ def nmax_err(got: np.ndarray, want: np.ndarray) -> float:
     """max |got - want| / max |want|: the parity metric of the GEMM."""
     w = np.asarray(want, dtype=np.float64)
     return float(np.max(np.abs(np.asarray(got, dtype=np.float64) - w)) / max(np.max(np.abs(w)), 1e-30))
+
+
+# --- the block executor's small ops (src/xdna-exec.cpp:253-346) ---------------------
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def rms_norm(x: np.ndarray, d: int, eps: float) -> np.ndarray:
+    x = _f32(x)
+    y = np.empty_like(x)
+    orc().zo_rms_norm(_p(x), _i64(x.size // d), _i64(d), ctypes.c_float(eps), _p(y))
+    return y
+
+
+def mul_row(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    x, w = _f32(x), _f32(w)
+    y = np.empty_like(x)
+    orc().zo_mul_row(_p(x), _p(w), _i64(x.size // w.size), _i64(w.size), _p(y))
+    return y
+
+
+def add(x: np.ndarray, b: np.ndarray) -> np.ndarray:
+    x, b = _f32(x), _f32(b)
+    y = np.empty_like(x)
+    d = b.size if b.size != x.size else x.shape[-1]
+    orc().zo_add(_p(x), _p(b), ctypes.c_int(int(b.size != x.size)), _i64(x.size // d), _i64(d), _p(y))
+    return y
+
+
+def scale(x: np.ndarray, s: float, bias: float) -> np.ndarray:
+    x = _f32(x)
+    y = np.empty_like(x)
+    orc().zo_scale(_p(x), _i64(x.size), ctypes.c_float(s), ctypes.c_float(bias), _p(y))
+    return y
+
+
+def glu(kind: int, g: np.ndarray, u: np.ndarray | None = None, swapped: bool = False) -> np.ndarray:
+    """split: g, u [rows][f]; one tensor: g [rows][2f] holding gate then up (or up then gate when swapped)."""
+    g = _f32(g)
+    if u is not None:
+        u = _f32(u)
+        rows, f = g.shape
+        gp, up, gs, us = g, u, f, f
+        y = np.empty((rows, f), np.float32)
+        orc().zo_glu(ctypes.c_int(kind), _p(gp), _i64(gs), _p(up), _i64(us), _i64(rows), _i64(f), _p(y))
+        return y
+    rows, f2 = g.shape
+    f = f2 // 2
+    y = np.empty((rows, f), np.float32)
+    gate = g[:, f:] if swapped else g[:, :f]
+    upv = g[:, :f] if swapped else g[:, f:]
+    base = g.ctypes.data
+    gp = ctypes.c_void_p(base + (f * 4 if swapped else 0))
+    upp = ctypes.c_void_p(base + (0 if swapped else f * 4))
+    orc().zo_glu(ctypes.c_int(kind), gp, _i64(f2), upp, _i64(f2), _i64(rows), _i64(f), _p(y))
+    del gate, upv
+    return y
+
+
+def rope_table(pos: np.ndarray, n_dims: int, n_ctx_orig: int, par, ff: np.ndarray | None = None) -> np.ndarray:
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    par = _f32(par)
+    t = np.empty((pos.size, n_dims), np.float32)
+    ffp = _p(_f32(ff)) if ff is not None else None
+    orc().zo_rope_table(_p(pos), _i64(pos.size), ctypes.c_int(n_dims), ctypes.c_int(n_ctx_orig), _p(par), ffp, _p(t))
+    return t
+
+
+def rope(x: np.ndarray, n_dims: int, mode: int, table: np.ndarray) -> np.ndarray:
+    """x [T][heads][d]"""
+    x = _f32(x)
+    T, H, d = x.shape
+    y = np.empty_like(x)
+    orc().zo_rope(_p(x), _i64(T), _i64(H), _i64(d), ctypes.c_int(n_dims), ctypes.c_int(mode), _p(_f32(table)), _p(y))
+    return y
+
+
+def nrmse(got: np.ndarray, want: np.ndarray) -> float:
+    g = np.asarray(got, np.float64)
+    w = np.asarray(want, np.float64)
+    return float(np.sqrt(np.sum((g - w) ** 2) / max(np.sum(w ** 2), 1e-300)))

@@ -5,6 +5,7 @@
  */
 #include "zest_oracle.h"
 
+#define _GNU_SOURCE
 #include <math.h>
 #include <pthread.h>
 #include <stdlib.h>
@@ -570,5 +571,119 @@ void zo_selftest_operands(int64_t M, int64_t K, int64_t N, int8_t *a, int8_t *w)
     for (int64_t i = 0; i < N * K; i++) {
         seed = seed * 1664525u + 1013904223u;
         w[i] = (int8_t) ((int) (seed >> 24) % 7 - 7 / 2);
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* the block executor's small ops (src/xdna-exec.cpp:253-346)               */
+/* ------------------------------------------------------------------------ */
+
+void zo_rms_norm(const float *x, int64_t rows, int64_t d, float eps, float *y) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float *xr = x + r * d;
+        float ss = 0.0f;
+        for (int64_t j = 0; j < d; j++) ss += xr[j] * xr[j];
+        const float sc = 1.0f / sqrtf(ss / (float) d + eps);
+        for (int64_t j = 0; j < d; j++) y[r * d + j] = xr[j] * sc;
+    }
+}
+
+void zo_mul_row(const float *x, const float *w, int64_t rows, int64_t d, float *y) {
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t j = 0; j < d; j++) y[r * d + j] = x[r * d + j] * w[j];
+}
+
+void zo_add(const float *x, const float *b, int bias_row, int64_t rows, int64_t d, float *y) {
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t j = 0; j < d; j++) y[r * d + j] = x[r * d + j] + (bias_row ? b[j] : b[r * d + j]);
+}
+
+void zo_scale(const float *x, int64_t n, float s, float bias, float *y) {
+    for (int64_t i = 0; i < n; i++) y[i] = x[i] * s + bias;
+}
+
+/* the activations, in float (src/xdna-exec.cpp:54-58) */
+static float zo_silu(float x) { return x / (1.0f + expf(-x)); }
+static float zo_gelu(float x) { return 0.5f * x * (1.0f + tanhf(0.7978845608f * x * (1.0f + 0.044715f * x * x))); }
+static float zo_gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067812f)); }
+static float zo_gelu_quick(float x) { return x / (1.0f + expf(-1.702f * x)); }
+
+void zo_glu(int kind, const float *g, int64_t g_stride, const float *u, int64_t u_stride, int64_t rows, int64_t f,
+            float *y) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float *gr = g + r * g_stride, *ur = u + r * u_stride;
+        float *o = y + r * f;
+        for (int64_t j = 0; j < f; j++) {
+            switch (kind) {
+                case ZO_GLU_SWIGLU: o[j] = zo_silu(gr[j]) * ur[j]; break;
+                case ZO_GLU_GEGLU: o[j] = zo_gelu(gr[j]) * ur[j]; break;
+                case ZO_GLU_GEGLU_ERF: o[j] = zo_gelu_erf(gr[j]) * ur[j]; break;
+                case ZO_GLU_GEGLU_QUICK: o[j] = zo_gelu_quick(gr[j]) * ur[j]; break;
+                default: o[j] = gr[j] > 0.0f ? gr[j] * ur[j] : 0.0f; break; /* REGLU */
+            }
+        }
+    }
+}
+
+static float zo_corr_dim(int n_dims, int n_ctx_orig, float n_rot, float base) {
+    return (float) n_dims * logf((float) n_ctx_orig / (n_rot * 2.0f * (float) M_PI)) / (2.0f * logf(base));
+}
+
+void zo_rope_corr_dims(int n_dims, int n_ctx_orig, float freq_base, float beta_fast, float beta_slow, float dims[2]) {
+    const float start = floorf(zo_corr_dim(n_dims, n_ctx_orig, beta_fast, freq_base));
+    const float end = ceilf(zo_corr_dim(n_dims, n_ctx_orig, beta_slow, freq_base));
+    dims[0] = start > 0.0f ? start : 0.0f;
+    dims[1] = end < (float) (n_dims - 1) ? end : (float) (n_dims - 1);
+}
+
+/* ggml's YaRN rotary for one pair (src/xdna-exec.cpp:65-77) */
+static void zo_rope_yarn(float theta_extrap, float freq_scale, const float corr[2], int64_t pair, float ext_factor,
+                         float mscale, float *c, float *s) {
+    float theta = freq_scale * theta_extrap;
+    if (ext_factor != 0.0f) {
+        const float lim = corr[1] - corr[0] > 0.001f ? corr[1] - corr[0] : 0.001f;
+        const float y = ((float) pair - corr[0]) / lim;
+        const float cl = y < 0.0f ? 0.0f : (y > 1.0f ? 1.0f : y);
+        const float ramp_mix = (1.0f - cl) * ext_factor;
+        theta = theta * (1.0f - ramp_mix) + theta_extrap * ramp_mix;
+        mscale *= 1.0f + 0.1f * logf(1.0f / freq_scale);
+    }
+    *c = cosf(theta) * mscale;
+    *s = sinf(theta) * mscale;
+}
+
+void zo_rope_table(const int32_t *pos, int64_t T, int n_dims, int n_ctx_orig, const float *par, const float *ff,
+                   float *table) {
+    const float freq_base = par[0], freq_scale = par[1], ext_factor = par[2], attn_factor = par[3];
+    float corr[2];
+    zo_rope_corr_dims(n_dims, n_ctx_orig, freq_base, par[4], par[5], corr);
+    const float theta_scale = powf(freq_base, -2.0f / (float) n_dims);
+    for (int64_t t = 0; t < T; t++) {
+        float theta = (float) pos[t];
+        float *cs = table + t * n_dims;
+        for (int p = 0; p < n_dims / 2; p++) {
+            zo_rope_yarn(ff ? theta / ff[p] : theta, freq_scale, corr, p, ext_factor, attn_factor, &cs[2 * p],
+                         &cs[2 * p + 1]);
+            theta *= theta_scale;
+        }
+    }
+}
+
+void zo_rope(const float *x, int64_t T, int64_t heads, int64_t d, int n_dims, int mode, const float *table, float *y) {
+    const int64_t off_n = mode == ZO_ROPE_NEOX ? n_dims / 2 : 1;
+    for (int64_t t = 0; t < T; t++) {
+        const float *cs = table + t * n_dims;
+        for (int64_t h = 0; h < heads; h++) {
+            const float *src = x + (t * heads + h) * d;
+            float *dst = y + (t * heads + h) * d;
+            for (int64_t i = 0; i < n_dims; i += 2) {
+                const int64_t ic = mode == ZO_ROPE_NEOX ? i / 2 : i;
+                const float c = cs[i], sn = cs[i + 1];
+                const float x0 = src[ic], x1 = src[ic + off_n];
+                dst[ic] = x0 * c - x1 * sn;
+                dst[ic + off_n] = x0 * sn + x1 * c;
+            }
+            for (int64_t i = n_dims; i < d; i++) dst[i] = src[i];
+        }
     }
 }

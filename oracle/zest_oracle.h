@@ -81,6 +81,30 @@ void zo_mul_mat_f64(const float *W, int64_t N, const float *X, int64_t M, int64_
 float zo_round_bf16(float x);
 float zo_swiglu_bf16(float g, float u);
 
+/* --- the block executor's small ops (src/xdna-exec.cpp:253-346), float
+ *     arithmetic in the reference's order; rows are contiguous ne0 runs --- */
+/* ggml_glu_op ids */
+enum { ZO_GLU_REGLU = 0, ZO_GLU_GEGLU = 1, ZO_GLU_SWIGLU = 2, ZO_GLU_GEGLU_ERF = 4, ZO_GLU_GEGLU_QUICK = 5 };
+/* ggml rope modes */
+enum { ZO_ROPE_NORMAL = 0, ZO_ROPE_NEOX = 2 };
+void zo_rms_norm(const float *x, int64_t rows, int64_t d, float eps, float *y);
+void zo_mul_row(const float *x, const float *w, int64_t rows, int64_t d, float *y);
+/* b: same shape as x, or (bias_row) one row of d broadcast over every row */
+void zo_add(const float *x, const float *b, int bias_row, int64_t rows, int64_t d, float *y);
+void zo_scale(const float *x, int64_t n, float s, float bias, float *y);
+/* g and u rows with their own strides (split tensors, or the two halves of
+ * one tensor); y rows of f */
+void zo_glu(int kind, const float *g, int64_t g_stride, const float *u, int64_t u_stride, int64_t rows, int64_t f,
+            float *y);
+/* ggml_rope_yarn_corr_dims (ggml's published YaRN correction range) */
+void zo_rope_corr_dims(int n_dims, int n_ctx_orig, float freq_base, float beta_fast, float beta_slow, float dims[2]);
+/* the per-token cos/sin table, [T][n_dims] (src/xdna-exec.cpp:194-239);
+ * par = freq_base, freq_scale, ext_factor, attn_factor, beta_fast, beta_slow */
+void zo_rope_table(const int32_t *pos, int64_t T, int n_dims, int n_ctx_orig, const float *par, const float *ff,
+                   float *table);
+/* x [T][heads][d] -> y, rotating the first n_dims of each head */
+void zo_rope(const float *x, int64_t T, int64_t heads, int64_t d, int n_dims, int mode, const float *table, float *y);
+
 /* --- the start-up self-test's operands (src/xdna-npu.cpp:142-152) -------- */
 void zo_selftest_operands(int64_t M, int64_t K, int64_t N, int8_t *a, int8_t *w);
 

@@ -7,6 +7,7 @@ backend interfaces in the slot order of the reference's initialisers.
 from __future__ import annotations
 
 import ctypes
+import struct
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
@@ -152,8 +153,14 @@ class Harness:
         return self.fake.fake_op_id(name.encode())
 
     def tensor(self, type_: int, ne, name="t", buffer=None, data=None, op="NONE", src=(), view_src=None,
-               flags=0) -> Tensor:
+               flags=0, params=None) -> Tensor:
+        """params: op_params as a list of ints and floats (floats stored as their bits)."""
         t = Tensor()
+        for i, v in enumerate(params or []):
+            if isinstance(v, float):
+                t.op_params[i] = struct.unpack("<i", struct.pack("<f", v))[0]
+            elif v is not None:
+                t.op_params[i] = int(v)
         t.type = type_
         t.buffer = buffer
         ne = list(ne) + [1] * (4 - len(ne))
@@ -178,3 +185,30 @@ class Harness:
         # ggml_mul_mat: dst ne = [w.ne1, x.ne1, x.ne2, x.ne3], f32
         return self.tensor(F32, [w.ne[1], x.ne[1], x.ne[2], x.ne[3]], name=name, buffer=buffer, data=data,
                            op="MUL_MAT", src=(w, x))
+
+    # the small ops, shaped as ggml builds them
+    def like(self, a: Tensor, op: str, src, name="op", params=None, buffer=None, data=None, ne=None) -> Tensor:
+        return self.tensor(F32, list(ne or a.ne), name=name, buffer=buffer, data=data, op=op, src=src,
+                           params=params)
+
+    def rms_norm(self, a, eps=1e-6, **kw):
+        return self.like(a, "RMS_NORM", (a,), params=[eps], **kw)
+
+    def mul(self, a, w, **kw):
+        return self.like(a, "MUL", (a, w), **kw)
+
+    def add(self, a, b, **kw):
+        return self.like(a, "ADD", (a, b), **kw)
+
+    def scale(self, a, s, bias=0.0, **kw):
+        return self.like(a, "SCALE", (a,), params=[float(s), float(bias)], **kw)
+
+    def glu(self, a, b=None, kind=2, swapped=0, **kw):
+        ne = list(a.ne) if b is not None else [a.ne[0] // 2, a.ne[1], a.ne[2], a.ne[3]]
+        return self.like(a, "GLU", (a, b) if b is not None else (a,), params=[kind, swapped], ne=ne, **kw)
+
+    def rope(self, a, pos, n_dims, mode, n_ctx_orig=0, freq_base=10000.0, freq_scale=1.0, ext_factor=0.0,
+             attn_factor=1.0, beta_fast=32.0, beta_slow=1.0, ff=None, **kw):
+        params = [0, n_dims, mode, 0, n_ctx_orig, float(freq_base), float(freq_scale), float(ext_factor),
+                  float(attn_factor), float(beta_fast), float(beta_slow)]
+        return self.like(a, "ROPE", (a, pos, ff) if ff is not None else (a, pos), params=params, **kw)

@@ -117,6 +117,49 @@ def test_supports_op_needs_a_usable_gpu(h):
     assert h.supports_op(t) == gpu
 
 
+def test_block_claiming(h):
+    # the small ops next to claimed matmuls (test-dispatch-gate.cpp:96-133, the NPU-mode answers)
+    k, n = 2048, 2048
+    x = h.tensor(F32, [k, 2048], buffer=h.buffer(USAGE_COMPUTE))
+    mm1 = h.mul_mat(h.tensor(Q4_0, [k, n], buffer=h.buffer(USAGE_WEIGHTS)), x)
+    mm2 = h.mul_mat(h.tensor(Q4_0, [k, n], buffer=h.buffer(USAGE_WEIGHTS)), x)
+    assert h.policy(h.add(mm1, mm2)), "an ADD of two claimed matmuls is claimed"
+    table = h.tensor(Q4_0, [k, 32000], buffer=h.buffer(USAGE_WEIGHTS))
+    emb = h.tensor(F32, [k, 2048], op="GET_ROWS", src=(table, h.tensor(26, [2048])))
+    assert not h.policy(h.add(emb, mm1)), "ADD of a matmul and the token embeddings (GET_ROWS) is not claimed"
+    assert not h.policy(h.add(mm1, emb)), "... in either order"
+    inp = h.tensor(F32, [k, 2048], flags=FLAG_INPUT)
+    assert not h.policy(h.add(inp, mm1)), "ADD of a matmul and a graph input is not claimed"
+    bias = h.tensor(F32, [n], buffer=h.buffer(USAGE_WEIGHTS))
+    assert h.policy(h.add(mm1, bias)), "an ADD of a bias row to a claimed matmul is claimed"
+    made = h.scale(h.tensor(F32, [n]), 2.0)
+    assert not h.policy(h.add(mm1, made)), "an ADD of a computed row (not a kept leaf) is not claimed"
+    assert h.policy(h.scale(mm1, 0.25)), "a SCALE of a claimed matmul is claimed"
+    assert h.policy(h.glu(mm1, mm2, kind=1)), "a GeGLU of two claimed matmuls is claimed"
+    fused = h.mul_mat(h.tensor(Q4_0, [k, 2 * n], buffer=h.buffer(USAGE_WEIGHTS)), x)
+    assert h.policy(h.glu(fused, kind=2)), "a SwiGLU on one matmul holding gate and up is claimed"
+    assert not h.policy(h.glu(fused, kind=3)), "an unsupported GLU kind is not claimed"
+    normed = h.rms_norm(h.add(mm1, mm2))
+    assert h.policy(normed), "an RMS_NORM fed by a claimed ADD is claimed (claims grow out from the matmuls)"
+    assert h.policy(h.mul(normed, h.tensor(F32, [k], buffer=h.buffer(USAGE_WEIGHTS))))
+    small = h.mul_mat(h.tensor(Q4_0, [k, n], buffer=h.buffer(USAGE_WEIGHTS)), h.tensor(F32, [k, 512]))
+    assert not h.policy(h.add(small, small)), "small ops of a short batch are not claimed"
+
+
+def test_block_ops_env():
+    code = ("import sys; sys.path.insert(0, %r); from harness import *; h = Harness(); "
+            "x = h.tensor(F32, [2048, 2048]); "
+            "mm = h.mul_mat(h.tensor(Q4_K, [2048, 2048], buffer=h.buffer(USAGE_WEIGHTS)), x); "
+            "print('ADD', h.policy(h.add(mm, mm)), 'SCALE', h.policy(h.scale(mm, 0.5)))"
+            % os.path.join(os.path.dirname(__file__), "ggml_harness"))
+    env = dict(os.environ, GGML_XDNA_BLOCK_OPS="ADD")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
+    assert "ADD True SCALE False" in out.stdout, out.stdout + out.stderr
+    env = dict(os.environ, GGML_XDNA_BLOCKS="0")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
+    assert "ADD False SCALE False" in out.stdout, out.stdout + out.stderr
+
+
 def test_min_batch_env():
     code = ("import sys; sys.path.insert(0, %r); from harness import *; h = Harness(); "
             "w = h.tensor(Q4_K, [2048, 2048], buffer=h.buffer(USAGE_WEIGHTS)); "
