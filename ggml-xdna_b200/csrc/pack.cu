@@ -30,37 +30,54 @@ __device__ __forceinline__ void store_run(uint8_t *dst, const uint8_t *stage, in
 // K2: f32 activations [T][K] (row stride ldx) -> A operand
 // ---------------------------------------------------------------------------
 
+// A work unit is 16 rows x UNROLL consecutive k tiles; every thread owns one
+// block (row, block column) in each of those tiles and issues all its loads
+// before encoding any, so each thread keeps UNROLL x 32 bytes in flight.
 template <bool BYTES, bool BF16>
 __global__ void __launch_bounds__(128) pack_activations_kernel(const float *__restrict__ x, int64_t T, int64_t K,
                                                                int64_t ldx, int64_t m_pad, uint8_t *__restrict__ a_bytes,
                                                                uint16_t *__restrict__ a_bf16, int64_t ldb) {
-    __shared__ __align__(16) uint8_t stage[SUB_BYTES];
+    constexpr int UNROLL = 4;
+    __shared__ __align__(16) uint8_t stage[BYTES ? UNROLL * SUB_BYTES : 16];
     const int tid = threadIdx.x;
-    const int row = tid % 16, c = tid / 16;  // block (row, block column c) of the unit
-    const int64_t nkt = K / TILE_K, units = (m_pad / 16) * nkt;
+    const int row = tid % 16, c = tid / 16;  // block (row, block column c) of each tile
+    const int nkt = (int) (K / TILE_K), ngroups = (nkt + UNROLL - 1) / UNROLL;
+    const int64_t units = (m_pad / 16) * ngroups;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
-        const int64_t r0 = (u / nkt) * 16, kt = u % nkt;
-        const int64_t r = r0 + row, col = kt * TILE_K + c * 8;
-        float v[8];
-        if (r < T) {
-            const float4 *p = reinterpret_cast<const float4 *>(x + r * ldx + col);
-            const float4 lo = __ldg(p), hi = __ldg(p + 1);
-            v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
-            v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
-        } else {
+        const int64_t r0 = (u / ngroups) * 16, r = r0 + row;
+        const int kt0 = (int) (u % ngroups) * UNROLL, nt = min(UNROLL, nkt - kt0);
+        float4 ld[UNROLL][2];
+        const bool live = r < T;  // rows past the prompt are zeros (xdna-npu.cpp:416-418)
 #pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = 0.0f;  // rows past the prompt: zeros (xdna-npu.cpp:416-418)
+        for (int i = 0; i < UNROLL; i++) {
+            if (live && i < nt) {
+                const float4 *p = reinterpret_cast<const float4 *>(x + r * ldx + (kt0 + i) * TILE_K + c * 8);
+                ld[i][0] = __ldg(p);
+                ld[i][1] = __ldg(p + 1);
+            } else {
+                ld[i][0] = ld[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
-        uint8_t enc[9];
-        uint32_t bf[4];
-        encode_block(v, enc, bf);
-        if (BF16) *reinterpret_cast<uint4 *>(a_bf16 + r * ldb + col) = make_uint4(bf[0], bf[1], bf[2], bf[3]);
-        if (BYTES) {
-            uint8_t *s = stage + (c * 16 + row) * BLOCK_BYTES;
 #pragma unroll
-            for (int i = 0; i < 9; i++) s[i] = enc[i];
+        for (int i = 0; i < UNROLL; i++) {
+            if (i >= nt) break;
+            const float v[8] = { ld[i][0].x, ld[i][0].y, ld[i][0].z, ld[i][0].w,
+                                 ld[i][1].x, ld[i][1].y, ld[i][1].z, ld[i][1].w };
+            uint8_t enc[9];
+            uint32_t bf[4];
+            encode_block(v, enc, bf);
+            if (BF16)
+                *reinterpret_cast<uint4 *>(a_bf16 + r * ldb + (kt0 + i) * TILE_K + c * 8) =
+                    make_uint4(bf[0], bf[1], bf[2], bf[3]);
+            if (BYTES) {
+                uint8_t *s = stage + i * SUB_BYTES + (c * 16 + row) * BLOCK_BYTES;
+#pragma unroll
+                for (int j = 0; j < 9; j++) s[j] = enc[j];
+            }
+        }
+        if (BYTES) {
             __syncthreads();
-            store_run(a_bytes + a_run_offset(r0, kt, K), stage, tid, 128);
+            for (int i = 0; i < nt; i++) store_run(a_bytes + a_run_offset(r0, kt0 + i, K), stage + i * SUB_BYTES, tid, 128);
             __syncthreads();
         }
     }
@@ -295,7 +312,7 @@ int launch_pack_activations(const float *x, int64_t T, int64_t K, int64_t ldx, i
                          "and rows 16-byte aligned");
     if (a_bf16 && (ldb < K || ldb % 8 || ((uintptr_t) a_bf16 & 15)))
         return set_error("pack_activations: bf16 rows must be 16-byte aligned");
-    const int64_t units = (m_pad / 16) * (K / TILE_K);
+    const int64_t units = (m_pad / 16) * ((K / TILE_K + 3) / 4);
     if (units == 0) return 0;
     const int grid = grid_for(units, 16);
     if (a_bytes && a_bf16)
