@@ -980,6 +980,22 @@ ggml_backend_reg_t ggml_backend_xdna_reg(void) {
 
 int ggml_zest_policy_supports(const ggml_tensor *op) { return op && policy(op) ? 1 : 0; }
 
+int ggml_zest_piece_fusions(ggml_cgraph *cgraph) {
+    std::vector<ggml_tensor *> nodes;
+    std::unordered_map<const ggml_tensor *, int> in_piece_map;
+    const int n = ggml_graph_n_nodes(cgraph);
+    for (int i = 0; i < n; i++) {
+        ggml_tensor *node = ggml_graph_node(cgraph, i);
+        in_piece_map[node] = i;
+        if (!op_is(node, "NONE")) nodes.push_back(node);
+    }
+    struct piece_set {
+        const std::unordered_map<const ggml_tensor *, int> &m;
+        size_t count(const ggml_tensor *t) const { return m.count(t); }
+    } in_piece{ in_piece_map };
+    return (int) find_fusions(nodes, in_piece).size();
+}
+
 GGML_BACKEND_API ggml_backend_reg_t ggml_backend_init(void) { return ggml_backend_xdna_reg(); }
 
 GGML_BACKEND_API int ggml_backend_score(void) { return 1; }

@@ -32,6 +32,12 @@ __attribute__((visibility("default"))) ggml_backend_reg_t ggml_backend_xdna_reg(
  * and for hosts that plan placement themselves; no GPU is touched. */
 __attribute__((visibility("default"))) int ggml_zest_policy_supports(const struct ggml_tensor *op);
 
+/* How many SwiGLU gate/up pairs graph_compute would run as one fused GEMM in
+ * this piece (find_fusions, src/xdna-exec.cpp:392-431), from the readers the
+ * supports_op questions recorded. Host logic only; for tests. */
+struct ggml_cgraph;
+__attribute__((visibility("default"))) int ggml_zest_piece_fusions(struct ggml_cgraph *cgraph);
+
 #ifdef __cplusplus
 }
 #endif

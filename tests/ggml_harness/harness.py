@@ -73,6 +73,9 @@ class Props(ctypes.Structure):
                 ("memory_total", ctypes.c_size_t), ("type", _int), ("device_id", ctypes.c_char_p), ("caps", Caps)]
 
 
+_KEEP: list = []
+
+
 def fn(ptr, restype, *argtypes):
     return ctypes.CFUNCTYPE(restype, *argtypes)(ptr)
 
@@ -94,7 +97,17 @@ class Harness:
         self.plugin.ggml_backend_init.restype = ctypes.POINTER(Reg)
         self.plugin.ggml_backend_score.restype = _int
         self.plugin.ggml_zest_policy_supports.argtypes = [ctypes.POINTER(Tensor)]
-        self.keep = []  # ctypes objects the C side points at
+        self.plugin.ggml_zest_piece_fusions.argtypes = [_vp]
+        # ctypes objects the C side points at, kept for the whole process: the
+        # plugin remembers who read each tensor by address (as the reference
+        # does), and a freed tensor's address reused by a later test's tensor
+        # would carry stale readers into it
+        self.keep = _KEEP
+
+    def piece_fusions(self, nodes: list[Tensor]) -> int:
+        arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])
+        self.keep.append(arr)
+        return self.plugin.ggml_zest_piece_fusions(self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp)))
 
     # --- registry / device / backend ------------------------------------------
     def reg(self):

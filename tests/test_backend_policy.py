@@ -146,6 +146,39 @@ def test_block_claiming(h):
     assert not h.policy(h.add(small, small)), "small ops of a short batch are not claimed"
 
 
+def test_swiglu_fusion_rules(h):
+    # find_fusions (src/xdna-exec.cpp:392-431): SiLU(gate) * up as one GEMM only when
+    # gate and up share their input and nothing else reads them
+    k, f, t = 1024, 2816, 1024
+
+    def ffn(kind=2, split=True, other_input=False, extra_reader=False, gate_output=False):
+        x = h.tensor(F32, [k, t], buffer=h.buffer(USAGE_COMPUTE))
+        x2 = h.tensor(F32, [k, t], buffer=h.buffer(USAGE_COMPUTE)) if other_input else x
+        if split:
+            g = h.mul_mat(h.tensor(Q4_K, [k, f], buffer=h.buffer(USAGE_WEIGHTS)), x)
+            u = h.mul_mat(h.tensor(Q4_K, [k, f], buffer=h.buffer(USAGE_WEIGHTS)), x2)
+            s = h.glu(g, u, kind=kind)
+            nodes = [g, u, s]
+        else:
+            g = h.mul_mat(h.tensor(Q4_K, [k, 2 * f], buffer=h.buffer(USAGE_WEIGHTS)), x)
+            s = h.glu(g, kind=kind)
+            nodes = [g, s]
+        if extra_reader:
+            nodes.append(h.scale(g, 2.0))
+        if gate_output:
+            g.flags = 2
+        for nd in nodes:
+            h.supports_op(nd)  # records readers, as the scheduler's questions do
+        return h.piece_fusions(nodes)
+
+    assert ffn() == 1
+    assert ffn(split=False) == 1, "one weight holding gate then up"
+    assert ffn(kind=1) == 0, "only SwiGLU runs as the fused epilogue"
+    assert ffn(other_input=True) == 0, "gate and up on different inputs"
+    assert ffn(extra_reader=True) == 0, "another op in the piece reads the gate"
+    assert ffn(gate_output=True) == 0, "the gate is a graph output"
+
+
 def test_block_ops_env():
     code = ("import sys; sys.path.insert(0, %r); from harness import *; h = Harness(); "
             "x = h.tensor(F32, [2048, 2048]); "

@@ -27,8 +27,13 @@ def normal(shape, seed):
     return (rng(seed).standard_normal(shape) * 1.5).astype(np.float32)
 
 
+_alive = []  # device copies must outlive the kernels that read them
+
+
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _alive.append(t)
+    return t
 
 
 def call(name, *args):
@@ -36,6 +41,7 @@ def call(name, *args):
     rc = getattr(L, name)(*args, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0, L.zest_last_error().decode()
     torch.cuda.synchronize()
+    _alive.clear()
 
 
 def p(t):
