@@ -292,6 +292,201 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// The CTA-pair kernel: a cluster of 2 CTAs on one TPC computes a 256x256
+// tile with tcgen05.mma.cta_group::2 (M=256 across the pair, N=256). Each CTA
+// loads only its 128 rows of A and its 128 rows (half) of B, so per SM every
+// 64-deep k step moves 32 KB into shared memory instead of 48 KB for the same
+// 128x256 of output, and the pair leader issues one MMA for both SMs.
+//
+// Barriers (same offsets in both CTAs):
+//   full[s]    leader: armed by the leader's producer with both CTAs' bytes;
+//              both CTAs' TMA loads complete on it
+//   empty[s]   each CTA: the leader's commit, multicast to both
+//   tfull[a]   each CTA: the leader's commit, multicast to both
+//   tempty[a]  leader: all 256 epilogue threads of the pair arrive
+// Cluster syncs bracket barrier set-up and TMEM release, so neither CTA's
+// barriers are used before they exist or after it exits.
+// ---------------------------------------------------------------------------
+
+constexpr int P_BM = 256, P_BN = 256, P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK * 2;  // this CTA's half of A
+constexpr int P_B_BYTES = 128 * BK * 2;  // this CTA's half of B
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_NUM_BARRIERS = 2 * P_STAGES + 5;
+constexpr int P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + P_NUM_BARRIERS * 8 + 16;
+constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (P_BN >> 3) << 17) |
+                             ((uint32_t) (P_BM >> 4) << 24);
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const gemm_params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+    uint64_t *full = bars, *empty = bars + P_STAGES, *tfull = bars + 2 * P_STAGES, *tempty = tfull + 2,
+             *drain = tempty + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + P_NUM_BARRIERS);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 256);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_holder, TMEM_COLS);
+        tmem_relinquish_pair();
+        tc_fence_before();
+    }
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+    const int total = p.num_m * p.num_n;  // in 256 x 256 tiles
+
+    auto fail = [&]() {
+        *abort_flag = 1;
+        atomicOr(p.err, ERR_TIMEOUT);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0, armed_phase = 0;
+            bool ok = true;
+            for (int t = pair; t < total && ok; t += npairs) {
+                int mb, nb;
+                tile_coords(t, p.num_m, p.num_n, mb, nb);
+                for (int kb = 0; kb < p.num_k; kb++) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, WAIT_LIMIT_NS)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+                    const uint32_t bar = map_to_rank(&full[stage], 0);
+                    uint8_t *sa = smem + stage * P_STAGE_BYTES;
+                    tma_load_2d_pair(sa, &tmA, bar, kb * BK, mb * P_BM + (int) rank * 128);
+                    tma_load_2d_pair(sa + P_A_BYTES, &tmB, bar, kb * BK, nb * P_BN + (int) rank * 128);
+                    armed |= 1u << stage;
+                    armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // our copies have all landed before the pair tears down: the
+            // leader sees them complete on its full barriers, the peer waits
+            // for the leader's MMAs (which consumed them) through empty
+            for (int s = 0; s < P_STAGES; s++) {
+                if (!(armed & (1u << s))) continue;
+                const bool done = leader ? mbar_wait_bounded(&full[s], (armed_phase >> s) & 1u, nullptr, WAIT_LIMIT_NS)
+                                         : mbar_wait_bounded(&empty[s], (armed_phase >> s) & 1u, nullptr, WAIT_LIMIT_NS);
+                if (!done) fail();
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            bool ok = true;
+            for (int t = pair; t < total && ok; t += npairs) {
+                if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag, WAIT_LIMIT_NS)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t) (acc * ACC_COLS);
+                for (int kb = 0; kb < p.num_k; kb++) {
+                    if (!mbar_wait_bounded(&full[stage], phase, abort_flag, WAIT_LIMIT_NS)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t *sa = smem + stage * P_STAGE_BYTES;
+                    const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + P_A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++)
+                        tc_mma_bf16_pair(d, adesc + 2 * k, bdesc + 2 * k, P_IDESC, (kb | k) != 0 ? 1u : 0u);
+                    tc_commit_pair_mc(&empty[stage], 0x3);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair_mc(&tfull[acc], 0x3);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+            tc_commit_pair(map_to_rank(drain, 0));
+            if (!mbar_wait_bounded(drain, 0, nullptr, WAIT_LIMIT_NS)) fail();
+        }
+    } else {
+        const int q = warp % 4;
+        const uint32_t tempty_leader[2] = { map_to_rank(&tempty[0], 0), map_to_rank(&tempty[1], 0) };
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        uint32_t bad = 0;
+        for (int t = pair; t < total; t += npairs) {
+            int mb, nb;
+            tile_coords(t, p.num_m, p.num_n, mb, nb);
+            if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, WAIT_LIMIT_NS)) {
+                fail();
+                break;
+            }
+            tc_fence_after();
+            const int64_t row = (int64_t) mb * P_BM + rank * 128 + q * 32 + lane;
+            const uint32_t tbase = tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * ACC_COLS);
+            uint32_t r[32];
+            for (int ch = 0; ch < P_BN / 32; ch++) {
+                tmem_ld_32x32b_x32(tbase + (uint32_t) (ch * 32), r);
+                tmem_ld_wait();
+                if (ch == P_BN / 32 - 1) {
+                    tc_fence_before();
+                    mbar_arrive_cluster(tempty_leader[acc]);
+                }
+                const int64_t col0 = (int64_t) nb * P_BN + ch * 32;
+                if (col0 < p.N) bad |= store_chunk(p, r, row, col0);
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.err, ERR_NOT_FINITE);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no barrier of either CTA is signalled after this
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+}
+
 // Plain CUDA-core GEMM: one thread per output, fp32 accumulation.
 __global__ void gemm_simt_kernel(const uint16_t *a, int64_t lda, const uint16_t *b, int64_t ldb, int64_t M, int64_t N,
                                  int64_t K, float *c, int64_t ldc) {
@@ -353,9 +548,49 @@ int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int
     const int64_t width = mode == MODE_SWIGLU ? N / 2 : N;
     if (n_out <= 0 || n_out > width) n_out = width;
     if (ldc < n_out) return set_error("gemm: ldc smaller than the output width");
+    // The CTA-pair kernel unless ZEST_GEMM_PAIR=0 or the rows fit one 128-row tile.
+    const char *pair_env = getenv("ZEST_GEMM_PAIR");
+    const bool pair = M > BM && !(pair_env && pair_env[0] == '0');
     CUtensorMap ta, tb;
-    if (!make_tmap(&ta, a_bf16, M, K, lda, BM) || !make_tmap(&tb, b_bf16, N, K, ldb, BN))
+    if (!make_tmap(&ta, a_bf16, M, K, lda, BM) || !make_tmap(&tb, b_bf16, N, K, ldb, pair ? 128 : BN))
         return set_error("gemm: cannot build the TMA descriptors");
+    if (pair) {
+        gemm_params p;
+        p.M = M;
+        p.N = N;
+        p.K = K;
+        p.ldc = ldc;
+        p.n_out = n_out;
+        p.c = c;
+        p.err = err_flag;
+        p.mode = mode;
+        p.num_m = (int) ((M + P_BM - 1) / P_BM);
+        p.num_n = (int) ((N + P_BN - 1) / P_BN);
+        p.num_k = (int) ((K + BK - 1) / BK);
+        static bool pattr = false;
+        if (!pattr) {
+            if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     P_SMEM_BYTES) != cudaSuccess)
+                return check_launch("gemm (shared memory size)");
+            pattr = true;
+        }
+        const int64_t tiles = (int64_t) p.num_m * p.num_n;
+        const int pairs = (int) (tiles < num_sms() / 2 ? tiles : num_sms() / 2);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned) (2 * pairs));
+        cfg.blockDim = dim3(NUM_THREADS);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel, ta, tb, p) != cudaSuccess) return check_launch("gemm");
+        return check_launch("gemm");
+    }
     gemm_params p;
     p.M = M;
     p.N = N;
