@@ -7,12 +7,10 @@
 // src/xdna-npu.cpp:339-390 (ggml to_float, then bfp16_pack_b,
 // bfp16_interleave_gate_up).
 //
-// Work unit of both kernels: 16 rows x one 64-wide k tile = 128 bfp16 blocks.
-// In the reference layout those 128 blocks are one contiguous 1152-byte run
-// (a 16-row pair, all 8 block columns), so each unit is encoded into shared
-// memory and stored as 72 aligned 16-byte vectors. Each thread owns whole
-// blocks of 8 values: its 32 input bytes come in two 128-bit loads and the
-// block's max exponent is a register-local reduction.
+// In the reference layout the 128 blocks of 16 rows x one 64-wide k tile are
+// one contiguous 1152-byte run (a 16-row pair, all 8 block columns), so both
+// kernels encode their bytes into shared memory and store whole runs as
+// aligned 16-byte vectors.
 #include "zest_device.cuh"
 #include "zest_internal.h"
 
@@ -30,54 +28,67 @@ __device__ __forceinline__ void store_run(uint8_t *dst, const uint8_t *stage, in
 // K2: f32 activations [T][K] (row stride ldx) -> A operand
 // ---------------------------------------------------------------------------
 
-// A work unit is 16 rows x UNROLL consecutive k tiles; every thread owns one
-// block (row, block column) in each of those tiles and issues all its loads
-// before encoding any, so each thread keeps UNROLL x 32 bytes in flight.
+// A work unit is 16 rows x 256 columns (4 k tiles). Warp w streams rows w
+// and w + 8, each as two 512-byte segments of 128 floats: every load
+// instruction is one fully coalesced 512-byte run. Lane l holds values
+// [4l, 4l + 4) of a segment, so lanes 2j and 2j+1 share block j and combine
+// its max exponent with one shuffle. All four loads are issued before any
+// encoding. The bfp16 bytes go through shared memory to leave as the four
+// tiles' 1152-byte runs.
+constexpr int PACK_THREADS = 256;
+
 template <bool BYTES, bool BF16>
-__global__ void __launch_bounds__(128) pack_activations_kernel(const float *__restrict__ x, int64_t T, int64_t K,
-                                                               int64_t ldx, int64_t m_pad, uint8_t *__restrict__ a_bytes,
-                                                               uint16_t *__restrict__ a_bf16, int64_t ldb) {
-    constexpr int UNROLL = 4;
-    __shared__ __align__(16) uint8_t stage[BYTES ? UNROLL * SUB_BYTES : 16];
-    const int tid = threadIdx.x;
-    const int row = tid % 16, c = tid / 16;  // block (row, block column c) of each tile
-    const int nkt = (int) (K / TILE_K), ngroups = (nkt + UNROLL - 1) / UNROLL;
+__global__ void __launch_bounds__(PACK_THREADS) pack_activations_kernel(const float *__restrict__ x, int64_t T,
+                                                                        int64_t K, int64_t ldx, int64_t m_pad,
+                                                                        uint8_t *__restrict__ a_bytes,
+                                                                        uint16_t *__restrict__ a_bf16, int64_t ldb) {
+    constexpr int W = 256;  // columns per unit
+    __shared__ __align__(16) uint8_t stage[BYTES ? (W / TILE_K) * SUB_BYTES : 16];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int nkt = (int) (K / TILE_K), ngroups = (nkt + 3) / 4;
     const int64_t units = (m_pad / 16) * ngroups;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
-        const int64_t r0 = (u / ngroups) * 16, r = r0 + row;
-        const int kt0 = (int) (u % ngroups) * UNROLL, nt = min(UNROLL, nkt - kt0);
-        float4 ld[UNROLL][2];
-        const bool live = r < T;  // rows past the prompt are zeros (xdna-npu.cpp:416-418)
+        const int64_t r0 = (u / ngroups) * 16;
+        const int c0 = (int) (u % ngroups) * W, width = min(W, (int) K - c0);  // a multiple of 64
+        float4 ld[2][2];
 #pragma unroll
-        for (int i = 0; i < UNROLL; i++) {
-            if (live && i < nt) {
-                const float4 *p = reinterpret_cast<const float4 *>(x + r * ldx + (kt0 + i) * TILE_K + c * 8);
-                ld[i][0] = __ldg(p);
-                ld[i][1] = __ldg(p + 1);
-            } else {
-                ld[i][0] = ld[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int h = 0; h < 2; h++) {
+            const int64_t r = r0 + warp + 8 * h;
+#pragma unroll
+            for (int s = 0; s < 2; s++) {
+                const int col = c0 + s * 128 + 4 * lane;
+                // rows past the prompt are zeros (xdna-npu.cpp:416-418)
+                ld[h][s] = (r < T && s * 128 + 4 * lane < width)
+                               ? __ldg(reinterpret_cast<const float4 *>(x + r * ldx + col))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
 #pragma unroll
-        for (int i = 0; i < UNROLL; i++) {
-            if (i >= nt) break;
-            const float v[8] = { ld[i][0].x, ld[i][0].y, ld[i][0].z, ld[i][0].w,
-                                 ld[i][1].x, ld[i][1].y, ld[i][1].z, ld[i][1].w };
-            uint8_t enc[9];
-            uint32_t bf[4];
-            encode_block(v, enc, bf);
-            if (BF16)
-                *reinterpret_cast<uint4 *>(a_bf16 + r * ldb + (kt0 + i) * TILE_K + c * 8) =
-                    make_uint4(bf[0], bf[1], bf[2], bf[3]);
-            if (BYTES) {
-                uint8_t *s = stage + i * SUB_BYTES + (c * 16 + row) * BLOCK_BYTES;
+        for (int h = 0; h < 2; h++) {
+            const int rr = warp + 8 * h;
 #pragma unroll
-                for (int j = 0; j < 9; j++) s[j] = enc[j];
+            for (int s = 0; s < 2; s++) {
+                const int cu = s * 128 + 4 * lane;  // column within the unit
+                uint32_t q, e;
+                uint2 bf;
+                encode_half_block(ld[h][s], q, e, bf);
+                if (cu >= width) continue;
+                if (BF16) *reinterpret_cast<uint2 *>(a_bf16 + (r0 + rr) * ldb + c0 + cu) = bf;
+                if (BYTES) {
+                    const int kt = cu / TILE_K, cb = (cu % TILE_K) / 8;
+                    uint8_t *blk = stage + kt * SUB_BYTES + (cb * 16 + rr) * BLOCK_BYTES;
+                    const int off = (lane & 1) ? 5 : 1;
+                    if (!(lane & 1)) blk[0] = (uint8_t) e;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) blk[off + j] = (uint8_t) (q >> (8 * j));
+                }
             }
         }
         if (BYTES) {
             __syncthreads();
-            for (int i = 0; i < nt; i++) store_run(a_bytes + a_run_offset(r0, kt0 + i, K), stage + i * SUB_BYTES, tid, 128);
+            for (int i = 0; i < width / TILE_K; i++)
+                store_run(a_bytes + a_run_offset(r0, c0 / TILE_K + i, K), stage + i * SUB_BYTES, threadIdx.x,
+                          PACK_THREADS);
             __syncthreads();
         }
     }
@@ -314,13 +325,13 @@ int launch_pack_activations(const float *x, int64_t T, int64_t K, int64_t ldx, i
         return set_error("pack_activations: bf16 rows must be 16-byte aligned");
     const int64_t units = (m_pad / 16) * ((K / TILE_K + 3) / 4);
     if (units == 0) return 0;
-    const int grid = grid_for(units, 16);
+    const int grid = grid_for(units, 8);
     if (a_bytes && a_bf16)
-        pack_activations_kernel<true, true><<<grid, 128, 0, st>>>(x, T, K, ldx, m_pad, a_bytes, a_bf16, ldb);
+        pack_activations_kernel<true, true><<<grid, PACK_THREADS, 0, st>>>(x, T, K, ldx, m_pad, a_bytes, a_bf16, ldb);
     else if (a_bytes)
-        pack_activations_kernel<true, false><<<grid, 128, 0, st>>>(x, T, K, ldx, m_pad, a_bytes, a_bf16, ldb);
+        pack_activations_kernel<true, false><<<grid, PACK_THREADS, 0, st>>>(x, T, K, ldx, m_pad, a_bytes, a_bf16, ldb);
     else if (a_bf16)
-        pack_activations_kernel<false, true><<<grid, 128, 0, st>>>(x, T, K, ldx, m_pad, a_bytes, a_bf16, ldb);
+        pack_activations_kernel<false, true><<<grid, PACK_THREADS, 0, st>>>(x, T, K, ldx, m_pad, a_bytes, a_bf16, ldb);
     else
         return 0;
     return check_launch("pack_activations");

@@ -84,6 +84,56 @@ __device__ __forceinline__ void encode_block(const float (&x)[8], uint8_t (&out)
     for (int i = 0; i < 4; i++) bf[i] = h[2 * i] | (h[2 * i + 1] << 16);
 }
 
+// The same encoding with a block split over two lanes (lane ^ 1 holds the
+// other four values): the block's max exponent and its all-zero test are
+// combined with one warp shuffle each. Returns this lane's four int8
+// mantissas packed in a word, the block's exponent byte, and the four
+// decoded values as bf16 bits. Every lane of the warp must call it.
+__device__ __forceinline__ void encode_half_block(const float4 x4, uint32_t &q_packed, uint32_t &exp_byte,
+                                                  uint2 &bf) {
+    const float x[4] = { x4.x, x4.y, x4.z, x4.w };
+    uint32_t mx = 0, any = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t u = f2u(x[i]);
+        mx = max(mx, (u >> 23) & 0xffu);
+        any |= u & 0x7fffffffu;
+    }
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    any |= __shfl_xor_sync(0xffffffffu, any, 1);
+    int q[4];
+    if (mx >= 6) {
+        const float scale = u2f((260u - mx) << 23);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int v = ((f2u(x[i]) >> 23) & 0xffu) == 0xffu ? -128 : __float2int_rn(__fmul_rn(x[i], scale));
+            q[i] = min(127, max(-128, v));
+        }
+    } else if (any == 0) {
+        mx = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) q[i] = 0;
+    } else {
+        const float s1 = u2f((127u + 64u) << 23), s2 = u2f((127u + (133u - mx) - 64u) << 23);
+#pragma unroll
+        for (int i = 0; i < 4; i++) q[i] = min(127, max(-128, __float2int_rn(__fmul_rn(__fmul_rn(x[i], s1), s2))));
+    }
+    exp_byte = mx;
+    q_packed = (uint32_t) (q[0] & 0xff) | ((uint32_t) (q[1] & 0xff) << 8) | ((uint32_t) (q[2] & 0xff) << 16) |
+               ((uint32_t) (q[3] & 0xff) << 24);
+    uint32_t h[4];
+    if (mx >= 7) {
+        const float scale = u2f((mx - 6u) << 23);
+#pragma unroll
+        for (int i = 0; i < 4; i++) h[i] = f2u(__fmul_rn((float) q[i], scale)) >> 16;
+    } else {
+        const float s1 = u2f((mx + 58u) << 23), s2 = u2f((127u - 64u) << 23);
+#pragma unroll
+        for (int i = 0; i < 4; i++) h[i] = f2u(__fmul_rn(__fmul_rn((float) q[i], s1), s2)) >> 16;
+    }
+    bf = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+}
+
 // Where block column cb of row rr sits inside one tile, in blocks:
 // 16-row pairs, then block columns, then the 16 rows (bfp16_pack.cpp:172-175).
 __host__ __device__ __forceinline__ int64_t in_tile(int64_t rr, int64_t cb) {
