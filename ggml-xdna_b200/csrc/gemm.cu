@@ -53,6 +53,7 @@ struct gemm_params {
     float *c;
     unsigned *err;
     int mode, num_m, num_n, num_k;
+    int tma_store;  // pair kernel: the epilogue stores through shared memory with TMA
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
@@ -314,16 +315,18 @@ constexpr int P_A_BYTES = 128 * BK * 2;  // this CTA's half of A
 constexpr int P_B_BYTES = 128 * BK * 2;  // this CTA's half of B
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 constexpr int P_NUM_BARRIERS = 2 * P_STAGES + 5;
-constexpr int P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + P_NUM_BARRIERS * 8 + 16;
+constexpr int P_EPI_BYTES = 4 * 2 * 32 * 32 * 4;  // per epilogue warp, two 32 x 32 fp32 staging buffers
+constexpr int P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + P_NUM_BARRIERS * 8 + 16;
 constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (P_BN >> 3) << 17) |
                              ((uint32_t) (P_BM >> 4) << 24);
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                             const gemm_params p) {
+                             const __grid_constant__ CUtensorMap tmC, const gemm_params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+    uint8_t *epi = smem + P_STAGES * P_STAGE_BYTES;  // 1 KB aligned
+    uint64_t *bars = reinterpret_cast<uint64_t *>(epi + P_EPI_BYTES);
     uint64_t *full = bars, *empty = bars + P_STAGES, *tfull = bars + 2 * P_STAGES, *tempty = tfull + 2,
              *drain = tempty + 2;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + P_NUM_BARRIERS);
@@ -457,7 +460,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 break;
             }
             tc_fence_after();
-            const int64_t row = (int64_t) mb * P_BM + rank * 128 + q * 32 + lane;
+            const int64_t row0 = (int64_t) mb * P_BM + rank * 128 + q * 32, row = row0 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * ACC_COLS);
             uint32_t r[32];
             for (int ch = 0; ch < P_BN / 32; ch++) {
@@ -468,13 +471,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     mbar_arrive_cluster(tempty_leader[acc]);
                 }
                 const int64_t col0 = (int64_t) nb * P_BN + ch * 32;
-                if (col0 < p.N) bad |= store_chunk(p, r, row, col0);
+                if (col0 >= p.N) continue;
+                if (!p.tma_store) {
+                    bad |= store_chunk(p, r, row, col0);
+                    continue;
+                }
+                // this warp's 32 rows x 32 columns through a 128-byte-swizzled
+                // staging buffer (double-buffered) and one TMA store
+                uint8_t *buf = epi + (q * 2 + (ch & 1)) * 4096;
+                if (lane == 0) bulk_wait_read_1();  // the store from two chunks ago has read this buffer
+                __syncwarp();
+                float o[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const float v = __uint_as_float(r[i]);
+                    o[i] = p.mode == MODE_BF16 ? bf16_round(v) : v;
+                    if (row < p.M && col0 + i < p.n_out) bad |= not_finite(o[i]);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    *reinterpret_cast<float4 *>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmC, buf, (int32_t) col0, (int32_t) row0);
+                    bulk_commit_group();
+                }
             }
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
             }
         }
+        if (p.tma_store && lane == 0) bulk_wait_all();  // every store has landed before the block exits
         if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.err, ERR_NOT_FINITE);
     }
 
@@ -524,6 +554,20 @@ bool make_tmap(CUtensorMap *m, const void *base, int64_t rows, int64_t cols, int
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The f32 output [rows][ld] as 32 x 32 tiles, 128-byte swizzle, for the
+// epilogue's TMA stores.
+bool make_tmap_out(CUtensorMap *m, void *base, int64_t rows, int64_t cols, int64_t ld) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = { (cuuint64_t) cols, (cuuint64_t) rows };
+    cuuint64_t strides[1] = { (cuuint64_t) ld * 4 };
+    cuuint32_t box[2] = { 32, 32 };
+    cuuint32_t estr[2] = { 1, 1 };
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
 int num_sms() {
     static int sms = 0;
     if (!sms) {
@@ -567,6 +611,11 @@ int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int
         p.num_m = (int) ((M + P_BM - 1) / P_BM);
         p.num_n = (int) ((N + P_BN - 1) / P_BN);
         p.num_k = (int) ((K + BK - 1) / BK);
+        // TMA stores need 16-byte aligned rows; SwiGLU halves the width and keeps direct stores
+        CUtensorMap tc;
+        memset(&tc, 0, sizeof tc);
+        p.tma_store = mode != MODE_SWIGLU && ldc % 4 == 0 && ((uintptr_t) c & 15) == 0 &&
+                      make_tmap_out(&tc, c, M, n_out, ldc);
         static bool pattr = false;
         if (!pattr) {
             if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -588,7 +637,8 @@ int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel, ta, tb, p) != cudaSuccess) return check_launch("gemm");
+        if (cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel, ta, tb, tc, p) != cudaSuccess)
+            return check_launch("gemm");
         return check_launch("gemm");
     }
     gemm_params p;
@@ -603,6 +653,7 @@ int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int
     p.num_m = (int) ((M + BM - 1) / BM);
     p.num_n = (int) ((N + BN - 1) / BN);
     p.num_k = (int) ((K + BK - 1) / BK);
+    p.tma_store = 0;
     static bool attr = false;
     if (!attr) {
         if (cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=

@@ -362,6 +362,29 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
                  : "memory");
 }
 
+// --- bulk tensor stores (shared -> global), for the GEMM epilogue -------------
+
+// Makes this thread's shared-memory writes visible to the TMA engine.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2D TMA tile store from shared memory; the engine clips rows and columns
+// outside the tensor. No reduction, no multicast.
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, int32_t c0, int32_t c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Until at most one committed store group still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+// Until every committed store group has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Shared-memory matrix descriptor for a K-major bf16 tile written by TMA
 // with 128-byte swizzle: rows of 128 B (64 values), 8-row atoms of 1 KB.
 __device__ __forceinline__ uint64_t sw128_desc(const void *tile) {
