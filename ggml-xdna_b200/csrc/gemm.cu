@@ -310,19 +310,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // barriers are used before they exist or after it exits.
 // ---------------------------------------------------------------------------
 
-constexpr int P_BM = 256, P_BN = 256, P_STAGES = 6;
-constexpr int P_A_BYTES = 128 * BK * 2;  // this CTA's half of A
-constexpr int P_B_BYTES = 128 * BK * 2;  // this CTA's half of B
-constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-constexpr int P_NUM_BARRIERS = 2 * P_STAGES + 5;
+constexpr int P_BM = 256;
 constexpr int P_EPI_BYTES = 4 * 2 * 32 * 32 * 4;  // per epilogue warp, two 32 x 32 fp32 staging buffers
-constexpr int P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + P_NUM_BARRIERS * 8 + 16;
-constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (P_BN >> 3) << 17) |
-                             ((uint32_t) (P_BM >> 4) << 24);
 
+// The pair kernel's shape for an N tile of P_BN columns (a multiple of 32,
+// at most 256): each CTA holds 128 rows of A and P_BN/2 rows of B per stage,
+// in about 192 KB of ring; the two accumulators sit 256 TMEM columns apart.
+template <int BN_T>
+struct pair_cfg {
+    static constexpr int P_BN = BN_T;
+    static constexpr int P_A_BYTES = 128 * BK * 2;       // this CTA's half of A
+    static constexpr int P_B_BYTES = (BN_T / 2) * BK * 2; // this CTA's half of B
+    static constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+    static constexpr int P_STAGES = 196608 / P_STAGE_BYTES;
+    static constexpr int P_NUM_BARRIERS = 2 * P_STAGES + 5;
+    static constexpr int P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + P_NUM_BARRIERS * 8 + 16;
+    static constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (BN_T >> 3) << 17) |
+                                        ((uint32_t) (P_BM >> 4) << 24);
+    static_assert(BN_T % 32 == 0 && BN_T <= 256 && P_STAGE_BYTES % 1024 == 0, "pair tile shape");
+};
+
+template <int BN_T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ CUtensorMap tmC, const gemm_params p) {
+    using C = pair_cfg<BN_T>;
+    constexpr int P_BN = C::P_BN, P_A_BYTES = C::P_A_BYTES, P_STAGE_BYTES = C::P_STAGE_BYTES,
+                  P_STAGES = C::P_STAGES, P_NUM_BARRIERS = C::P_NUM_BARRIERS;
+    constexpr uint32_t P_IDESC = C::P_IDESC;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t *epi = smem + P_STAGES * P_STAGE_BYTES;  // 1 KB aligned
@@ -387,7 +402,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t bar = map_to_rank(&full[stage], 0);
                     uint8_t *sa = smem + stage * P_STAGE_BYTES;
                     tma_load_2d_pair(sa, &tmA, bar, kb * BK, mb * P_BM + (int) rank * 128);
-                    tma_load_2d_pair(sa + P_A_BYTES, &tmB, bar, kb * BK, nb * P_BN + (int) rank * 128);
+                    tma_load_2d_pair(sa + P_A_BYTES, &tmB, bar, kb * BK, nb * P_BN + (int) rank * (P_BN / 2));
                     armed |= 1u << stage;
                     armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == P_STAGES) {
@@ -579,6 +594,56 @@ int num_sms() {
     return sms;
 }
 
+// The pair kernel for an N tile of BN_T: B's tensor map (BN_T/2-row boxes,
+// one per CTA), the output's for TMA stores, a cluster-of-2 launch.
+template <int BN_T>
+int launch_pair(const CUtensorMap &ta, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N, int64_t K,
+                int mode, float *c, int64_t ldc, int64_t n_out, unsigned *err_flag, cudaStream_t st) {
+    using C = pair_cfg<BN_T>;
+    CUtensorMap tb;
+    if (!make_tmap(&tb, b_bf16, N, K, ldb, BN_T / 2)) return set_error("gemm: cannot build the TMA descriptors");
+    gemm_params p;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.ldc = ldc;
+    p.n_out = n_out;
+    p.c = c;
+    p.err = err_flag;
+    p.mode = mode;
+    p.num_m = (int) ((M + P_BM - 1) / P_BM);
+    p.num_n = (int) ((N + BN_T - 1) / BN_T);
+    p.num_k = (int) ((K + BK - 1) / BK);
+    // TMA stores need 16-byte aligned rows; SwiGLU halves the width and keeps direct stores
+    CUtensorMap tc;
+    memset(&tc, 0, sizeof tc);
+    p.tma_store = mode != MODE_SWIGLU && ldc % 4 == 0 && ((uintptr_t) c & 15) == 0 &&
+                  make_tmap_out(&tc, c, M, n_out, ldc);
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::P_SMEM_BYTES) != cudaSuccess)
+            return check_launch("gemm (shared memory size)");
+        attr_set = true;
+    }
+    const int64_t tiles = (int64_t) p.num_m * p.num_n;
+    const int pairs = (int) (tiles < num_sms() / 2 ? tiles : num_sms() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) (2 * pairs));
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = C::P_SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T>, ta, tb, tc, p);
+    return check_launch("gemm");
+}
+
 }  // namespace
 
 int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
@@ -596,50 +661,33 @@ int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int
     const char *pair_env = getenv("ZEST_GEMM_PAIR");
     const bool pair = M > BM && !(pair_env && pair_env[0] == '0');
     CUtensorMap ta, tb;
-    if (!make_tmap(&ta, a_bf16, M, K, lda, BM) || !make_tmap(&tb, b_bf16, N, K, ldb, pair ? 128 : BN))
+    if (!make_tmap(&ta, a_bf16, M, K, lda, BM) || (!pair && !make_tmap(&tb, b_bf16, N, K, ldb, BN)))
         return set_error("gemm: cannot build the TMA descriptors");
     if (pair) {
-        gemm_params p;
-        p.M = M;
-        p.N = N;
-        p.K = K;
-        p.ldc = ldc;
-        p.n_out = n_out;
-        p.c = c;
-        p.err = err_flag;
-        p.mode = mode;
-        p.num_m = (int) ((M + P_BM - 1) / P_BM);
-        p.num_n = (int) ((N + P_BN - 1) / P_BN);
-        p.num_k = (int) ((K + BK - 1) / BK);
-        // TMA stores need 16-byte aligned rows; SwiGLU halves the width and keeps direct stores
-        CUtensorMap tc;
-        memset(&tc, 0, sizeof tc);
-        p.tma_store = mode != MODE_SWIGLU && ldc % 4 == 0 && ((uintptr_t) c & 15) == 0 &&
-                      make_tmap_out(&tc, c, M, n_out, ldc);
-        static bool pattr = false;
-        if (!pattr) {
-            if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     P_SMEM_BYTES) != cudaSuccess)
-                return check_launch("gemm (shared memory size)");
-            pattr = true;
+        // The N tile with the fewest tile-columns of work once rounded up to
+        // whole waves of SM pairs (e.g. N = 2560: 160-wide tiles, 7 waves of
+        // 160 instead of 5 of 256); ties go to the wider tile.
+        const int64_t pairs_avail = num_sms() / 2, mt = (M + P_BM - 1) / P_BM;
+        int best = 256;
+        int64_t best_cost = -1;
+        for (int bn : { 256, 192, 160, 128 }) {
+            const int64_t tiles = mt * ((N + bn - 1) / bn);
+            const int64_t cost = (tiles + pairs_avail - 1) / pairs_avail * bn;
+            if (best_cost < 0 || cost < best_cost) {
+                best = bn;
+                best_cost = cost;
+            }
         }
-        const int64_t tiles = (int64_t) p.num_m * p.num_n;
-        const int pairs = (int) (tiles < num_sms() / 2 ? tiles : num_sms() / 2);
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned) (2 * pairs));
-        cfg.blockDim = dim3(NUM_THREADS);
-        cfg.dynamicSmemBytes = P_SMEM_BYTES;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        if (cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel, ta, tb, tc, p) != cudaSuccess)
-            return check_launch("gemm");
-        return check_launch("gemm");
+        if (const char *force = getenv("ZEST_GEMM_BN")) {  // a fixed N tile, for tests and tuning
+            const int bn = atoi(force);
+            if (bn == 256 || bn == 192 || bn == 160 || bn == 128) best = bn;
+        }
+        switch (best) {
+            case 192: return launch_pair<192>(ta, b_bf16, ldb, M, N, K, mode, c, ldc, n_out, err_flag, st);
+            case 160: return launch_pair<160>(ta, b_bf16, ldb, M, N, K, mode, c, ldc, n_out, err_flag, st);
+            case 128: return launch_pair<128>(ta, b_bf16, ldb, M, N, K, mode, c, ldc, n_out, err_flag, st);
+            default: return launch_pair<256>(ta, b_bf16, ldb, M, N, K, mode, c, ldc, n_out, err_flag, st);
+        }
     }
     gemm_params p;
     p.M = M;

@@ -37,6 +37,33 @@ def test_gemm_f32_vs_oracle(M, N, K):
     assert O.nmax_err(c, want) <= TOL
 
 
+@pytest.mark.parametrize("bn", ["256", "192", "160", "128"])
+@pytest.mark.parametrize("mode", [Z.MODE_F32, Z.MODE_BF16])
+def test_gemm_pair_tile_widths(bn, mode, monkeypatch):
+    # every N tile of the CTA-pair kernel, on a ragged shape (M, N not tile multiples)
+    monkeypatch.setenv("ZEST_GEMM_BN", bn)
+    M, N, K = 777, 1000, 576
+    ah, bh, a_dec, b_dec, _, _ = operands(M, N, K, seed=int(bn))
+    c = host(Z.gemm(ah, bh, M, N, mode))
+    want = O.mul_mat(b_dec, a_dec)
+    if mode == Z.MODE_BF16:
+        assert np.array_equal(c, O.round_bf16(c))
+        assert O.nmax_err(c, want) <= 4e-3
+    else:
+        assert O.nmax_err(c, want) <= TOL
+
+
+def test_gemm_pair_and_single_agree(monkeypatch):
+    # the CTA-pair kernel and the one-CTA kernel accumulate in the same k order
+    M, N, K = 640, 768, 1024
+    ah, bh, _, _, _, _ = operands(M, N, K, seed=4)
+    monkeypatch.setenv("ZEST_GEMM_PAIR", "0")
+    c1 = host(Z.gemm(ah, bh, M, N))
+    monkeypatch.setenv("ZEST_GEMM_PAIR", "1")
+    c2 = host(Z.gemm(ah, bh, M, N))
+    assert O.nmax_err(c2, c1) <= 1e-6
+
+
 def test_gemm_exact_integers():
     a, w = O.selftest_operands(512, 128, 512)
     ah = dev(O.decode_blocks(O.encode_blocks(a.astype(np.float32))).reshape(512, 128))
