@@ -74,6 +74,7 @@ def seed_of(name: str, salt: int = 0) -> int:
 
 def quantize_threaded(qtype: int, w: np.ndarray, threads: int) -> np.ndarray:
     from oracle import oracle as O
+    O.orc()  # load the library (and the IQ3_S codebook) before the worker threads use it
     rows = w.shape[0]
     chunks = [(i, min(rows, i + max(1, rows // threads))) for i in range(0, rows, max(1, rows // threads))]
     with ThreadPoolExecutor(threads) as ex:

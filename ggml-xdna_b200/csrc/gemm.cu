@@ -664,21 +664,11 @@ int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int
     if (!make_tmap(&ta, a_bf16, M, K, lda, BM) || (!pair && !make_tmap(&tb, b_bf16, N, K, ldb, BN)))
         return set_error("gemm: cannot build the TMA descriptors");
     if (pair) {
-        // The N tile with the fewest tile-columns of work once rounded up to
-        // whole waves of SM pairs (e.g. N = 2560: 160-wide tiles, 7 waves of
-        // 160 instead of 5 of 256); ties go to the wider tile.
-        const int64_t pairs_avail = num_sms() / 2, mt = (M + P_BM - 1) / P_BM;
+        // 256-wide N tiles: measured on every shape of the configs, narrower
+        // tiles lose 15-45 % per flop, more than they win back by rounding
+        // to fewer waves. Narrower ones stay selectable for tests and tuning.
         int best = 256;
-        int64_t best_cost = -1;
-        for (int bn : { 256, 192, 160, 128 }) {
-            const int64_t tiles = mt * ((N + bn - 1) / bn);
-            const int64_t cost = (tiles + pairs_avail - 1) / pairs_avail * bn;
-            if (best_cost < 0 || cost < best_cost) {
-                best = bn;
-                best_cost = cost;
-            }
-        }
-        if (const char *force = getenv("ZEST_GEMM_BN")) {  // a fixed N tile, for tests and tuning
+        if (const char *force = getenv("ZEST_GEMM_BN")) {
             const int bn = atoi(force);
             if (bn == 256 || bn == 192 || bn == 160 || bn == 128) best = bn;
         }

@@ -69,11 +69,12 @@ def orc() -> ctypes.CDLL:
         L.zo_selftest_operands.argtypes = [_i64, _i64, _i64, _vp, _vp]
         L.zo_row_bytes.restype = _i64
         L.zo_row_bytes.argtypes = [_int, _i64]
-        _orc = L
-        try:
-            set_iq3s_grid(iq3s_grid())
+        try:  # the codebook goes in before any other thread can see the library
+            g = np.ascontiguousarray(iq3s_grid(), dtype=np.uint32)
+            L.zo_set_iq3s_grid(_p(g))
         except ImportError:
             pass
+        _orc = L
     return _orc
 
 
