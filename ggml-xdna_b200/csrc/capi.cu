@@ -397,36 +397,52 @@ const uint16_t *zest_weight_bf16(const zest_npu *npu, const zest_wkey *key, int 
 
 void *zest_stream(zest_npu *npu) { return npu ? (void *) npu->st : nullptr; }
 
-int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x, int64_t T, float *y, int on_device) {
-    if (!npu || !key) return set_error("zest_mul_mat: no service or key");
-    const zest_npu::weight *w = npu->find(key, fused);
-    if (!w) return set_error("zest_mul_mat: weight not added");
+int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *fused, const float *x, int64_t T,
+                       float *const *y, int on_device) {
+    if (!npu || !keys || n <= 0 || n > 4) return set_error("zest_mul_mat: no service, or not 1 to 4 weights");
+    const zest_npu::weight *w[4];
+    for (int i = 0; i < n; i++) {
+        w[i] = npu->find(&keys[i], fused ? fused[i] : 0);
+        if (!w[i]) return set_error("zest_mul_mat: weight not added");
+        if (w[i]->K != w[0]->K) return set_error("zest_mul_mat: a group's weights differ in K");
+    }
     if (T <= 0) return 0;
     if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_mul_mat: cannot select the device");
     if (npu->inject && injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
-    const int64_t K = w->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
-    const size_t x_bytes = (size_t) (T * K) * 4, y_bytes = (size_t) (T * w->n_out) * 4;
+    const int64_t K = w[0]->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
+    const size_t x_bytes = (size_t) (T * K) * 4;
+    size_t y_off[4], y_total = 0;
+    for (int i = 0; i < n; i++) {
+        y_off[i] = y_total;
+        y_total += (size_t) (T * w[i]->n_out) * 4;
+    }
     if (!grow((void **) &npu->a_bf16, &npu->a_cap, (size_t) (m_pad * K) * 2) ||
         (!on_device && (!grow((void **) &npu->x_dev, &npu->x_cap, x_bytes) ||
-                        !grow((void **) &npu->y_dev, &npu->y_cap, y_bytes))))
+                        !grow((void **) &npu->y_dev, &npu->y_cap, y_total))))
         return set_error("zest_mul_mat: out of GPU memory for the call's buffers");
     cudaStream_t st = npu->st;
     const float *xd = on_device ? x : npu->x_dev;
-    float *yd = on_device ? y : npu->y_dev;
+    float *yd[4];
+    for (int i = 0; i < n; i++) yd[i] = on_device ? y[i] : (float *) ((char *) npu->y_dev + y_off[i]);
     cudaEventRecord(npu->ev[0], st);
     if (!on_device) cudaMemcpyAsync(npu->x_dev, x, x_bytes, cudaMemcpyHostToDevice, st);
     cudaMemsetAsync(npu->err_dev, 0, sizeof(unsigned), st);
     cudaEventRecord(npu->ev[1], st);
     int rc = launch_pack_activations(xd, T, K, K, m_pad, nullptr, npu->a_bf16, K, st);
     cudaEventRecord(npu->ev[2], st);
-    if (!rc) rc = launch_gemm(npu->a_bf16, K, w->bf16, K, T, w->n_pad, K, w->mode, yd, w->n_out, w->n_out,
-                                  npu->err_dev, st);
+    gemm_seg segs[4];
+    for (int i = 0; i < n; i++) segs[i] = { w[i]->bf16, K, w[i]->n_pad, w[i]->n_out, w[i]->n_out, w[i]->mode, yd[i] };
+    if (!rc) rc = launch_gemm_group(npu->a_bf16, K, T, K, n, segs, npu->err_dev, st);
     if (!rc && npu->inject && injected_nan()) {
-        cudaMemsetAsync(yd, 0xff, y_bytes, st);
-        check_finite_kernel<<<148, 256, 0, st>>>(yd, T * w->n_out, npu->err_dev);
+        for (int i = 0; i < n; i++) {
+            cudaMemsetAsync(yd[i], 0xff, (size_t) (T * w[i]->n_out) * 4, st);
+            check_finite_kernel<<<148, 256, 0, st>>>(yd[i], T * w[i]->n_out, npu->err_dev);
+        }
     }
     cudaEventRecord(npu->ev[3], st);
-    if (!on_device) cudaMemcpyAsync(y, npu->y_dev, y_bytes, cudaMemcpyDeviceToHost, st);
+    if (!on_device)
+        for (int i = 0; i < n; i++)
+            cudaMemcpyAsync(y[i], yd[i], (size_t) (T * w[i]->n_out) * 4, cudaMemcpyDeviceToHost, st);
     cudaMemcpyAsync(npu->err_host, npu->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
     cudaEventRecord(npu->ev[4], st);
     const cudaError_t e = cudaStreamSynchronize(st);
@@ -440,10 +456,26 @@ int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x,
     npu->times.copy_ms += a + d;
     npu->times.encode_ms += b;
     npu->times.gemm_ms += c;
-    npu->times.calls++;
+    npu->times.calls += n;
     if (*npu->err_host & ERR_TIMEOUT) return set_error("a GPU kernel's bounded wait ran out");
     if (*npu->err_host & ERR_NOT_FINITE) return set_error("the GPU's results held NaN or infinity");
     return 0;
+}
+
+int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x, int64_t T, float *y, int on_device) {
+    if (!key) return set_error("zest_mul_mat: no service or key");
+    float *ys[1] = { y };
+    return zest_mul_mat_group(npu, 1, key, &fused, x, T, ys, on_device);
+}
+
+int zest_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int n, const uint16_t *const *b_bf16,
+                    const int64_t *ldb, const int64_t *N, const int *mode, float *const *c, const int64_t *ldc,
+                    unsigned *err, void *stream) {
+    if (n <= 0 || n > 4 || !b_bf16 || !ldb || !N || !mode || !c || !ldc)
+        return set_error("zest_gemm_group: 1 to 4 weights, every array given");
+    gemm_seg segs[4];
+    for (int i = 0; i < n; i++) segs[i] = { b_bf16[i], ldb[i], N[i], ldc[i], 0, mode[i], c[i] };
+    return launch_gemm_group(a_bf16, lda, M, K, n, segs, err, (cudaStream_t) stream);
 }
 
 int zest_take_times(zest_npu *npu, zest_times *out) {

@@ -330,10 +330,29 @@ struct pair_cfg {
     static_assert(BN_T % 32 == 0 && BN_T <= 256 && P_STAGE_BYTES % 1024 == 0, "pair tile shape");
 };
 
+// A grouped launch: up to MAX_SEG weights sharing one A (q, k and v; gate
+// and up), each with its own B, output and mode. Their N tiles are laid end
+// to end, so one persistent launch runs them all and no kernel tail
+// separates them (the reference submits such a group as one NPU runlist,
+// src/xdna-npu.cpp:476-531).
+constexpr int MAX_SEG = 4;
+
+struct pair_maps {
+    CUtensorMap b[MAX_SEG], c[MAX_SEG];
+};
+
+struct pair_params {
+    gemm_params seg[MAX_SEG];  // per weight: N, n_out, ldc, c, mode, tma_store (M, K, err shared)
+    int tile0[MAX_SEG + 1];    // first N tile of each segment; tile0[nseg] = all N tiles
+    int nseg, num_m, num_n, num_k;
+    int64_t M;
+    unsigned *err;
+};
+
 template <int BN_T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                             const __grid_constant__ CUtensorMap tmC, const gemm_params p) {
+    gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ pair_maps maps,
+                             const __grid_constant__ pair_params pp) {
     using C = pair_cfg<BN_T>;
     constexpr int P_BN = C::P_BN, P_A_BYTES = C::P_A_BYTES, P_STAGE_BYTES = C::P_STAGE_BYTES,
                   P_STAGES = C::P_STAGES, P_NUM_BARRIERS = C::P_NUM_BARRIERS;
@@ -365,7 +384,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmA);
-        prefetch_tmap(&tmB);
+        for (int s = 0; s < pp.nseg; s++) prefetch_tmap(&maps.b[s]);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_holder, TMEM_COLS);
@@ -376,11 +395,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
     const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
-    const int total = p.num_m * p.num_n;  // in 256 x 256 tiles
+    const int total = pp.num_m * pp.num_n;  // 256-row M tiles x all segments' N tiles
 
+    // global N tile -> (segment, its own N tile)
+    auto locate = [&](int nbg, int &seg, int &nb) {
+        seg = 0;
+        while (seg + 1 < pp.nseg && nbg >= pp.tile0[seg + 1]) seg++;
+        nb = nbg - pp.tile0[seg];
+    };
     auto fail = [&]() {
         *abort_flag = 1;
-        atomicOr(p.err, ERR_TIMEOUT);
+        atomicOr(pp.err, ERR_TIMEOUT);
     };
 
     if (warp == 0) {
@@ -390,9 +415,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t armed = 0, armed_phase = 0;
             bool ok = true;
             for (int t = pair; t < total && ok; t += npairs) {
-                int mb, nb;
-                tile_coords(t, p.num_m, p.num_n, mb, nb);
-                for (int kb = 0; kb < p.num_k; kb++) {
+                int mb, nbg, seg, nb;
+                tile_coords(t, pp.num_m, pp.num_n, mb, nbg);
+                locate(nbg, seg, nb);
+                for (int kb = 0; kb < pp.num_k; kb++) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, WAIT_LIMIT_NS)) {
                         fail();
                         ok = false;
@@ -402,7 +428,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t bar = map_to_rank(&full[stage], 0);
                     uint8_t *sa = smem + stage * P_STAGE_BYTES;
                     tma_load_2d_pair(sa, &tmA, bar, kb * BK, mb * P_BM + (int) rank * 128);
-                    tma_load_2d_pair(sa + P_A_BYTES, &tmB, bar, kb * BK, nb * P_BN + (int) rank * (P_BN / 2));
+                    tma_load_2d_pair(sa + P_A_BYTES, &maps.b[seg], bar, kb * BK, nb * P_BN + (int) rank * (P_BN / 2));
                     armed |= 1u << stage;
                     armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == P_STAGES) {
@@ -433,7 +459,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t) (acc * ACC_COLS);
-                for (int kb = 0; kb < p.num_k; kb++) {
+                for (int kb = 0; kb < pp.num_k; kb++) {
                     if (!mbar_wait_bounded(&full[stage], phase, abort_flag, WAIT_LIMIT_NS)) {
                         fail();
                         ok = false;
@@ -467,9 +493,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t bad = 0;
+        bool stored = false;
         for (int t = pair; t < total; t += npairs) {
-            int mb, nb;
-            tile_coords(t, p.num_m, p.num_n, mb, nb);
+            int mb, nbg, seg, nb;
+            tile_coords(t, pp.num_m, pp.num_n, mb, nbg);
+            locate(nbg, seg, nb);
+            const gemm_params &p = pp.seg[seg];
             if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, WAIT_LIMIT_NS)) {
                 fail();
                 break;
@@ -510,8 +539,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 fence_proxy_async_shared();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&tmC, buf, (int32_t) col0, (int32_t) row0);
+                    tma_store_2d(&maps.c[seg], buf, (int32_t) col0, (int32_t) row0);
                     bulk_commit_group();
+                    stored = true;
                 }
             }
             if (++acc == 2) {
@@ -519,8 +549,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 acc_phase ^= 1;
             }
         }
-        if (p.tma_store && lane == 0) bulk_wait_all();  // every store has landed before the block exits
-        if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.err, ERR_NOT_FINITE);
+        if (stored) bulk_wait_all();  // every store has landed before the block exits
+        if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(pp.err, ERR_NOT_FINITE);
     }
 
     tc_fence_before();
@@ -594,31 +624,44 @@ int num_sms() {
     return sms;
 }
 
-// The pair kernel for an N tile of BN_T: B's tensor map (BN_T/2-row boxes,
-// one per CTA), the output's for TMA stores, a cluster-of-2 launch.
+// The pair kernel for an N tile of BN_T over a group of weights sharing A:
+// B's tensor maps (BN_T/2-row boxes, one per CTA), the outputs' for TMA
+// stores, a cluster-of-2 launch.
 template <int BN_T>
-int launch_pair(const CUtensorMap &ta, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N, int64_t K,
-                int mode, float *c, int64_t ldc, int64_t n_out, unsigned *err_flag, cudaStream_t st) {
+int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, const gemm_seg *segs, unsigned *err_flag,
+                      cudaStream_t st) {
     using C = pair_cfg<BN_T>;
-    CUtensorMap tb;
-    if (!make_tmap(&tb, b_bf16, N, K, ldb, BN_T / 2)) return set_error("gemm: cannot build the TMA descriptors");
-    gemm_params p;
-    p.M = M;
-    p.N = N;
-    p.K = K;
-    p.ldc = ldc;
-    p.n_out = n_out;
-    p.c = c;
-    p.err = err_flag;
-    p.mode = mode;
-    p.num_m = (int) ((M + P_BM - 1) / P_BM);
-    p.num_n = (int) ((N + BN_T - 1) / BN_T);
-    p.num_k = (int) ((K + BK - 1) / BK);
-    // TMA stores need 16-byte aligned rows; SwiGLU halves the width and keeps direct stores
-    CUtensorMap tc;
-    memset(&tc, 0, sizeof tc);
-    p.tma_store = mode != MODE_SWIGLU && ldc % 4 == 0 && ((uintptr_t) c & 15) == 0 &&
-                  make_tmap_out(&tc, c, M, n_out, ldc);
+    pair_maps maps;
+    pair_params pp;
+    memset(&maps, 0, sizeof maps);
+    memset(&pp, 0, sizeof pp);
+    pp.nseg = nseg;
+    pp.M = M;
+    pp.err = err_flag;
+    pp.num_m = (int) ((M + P_BM - 1) / P_BM);
+    pp.num_k = (int) ((K + BK - 1) / BK);
+    int tiles_n = 0;
+    for (int s = 0; s < nseg; s++) {
+        const gemm_seg &g = segs[s];
+        if (!make_tmap(&maps.b[s], g.b, g.N, K, g.ldb, BN_T / 2))
+            return set_error("gemm: cannot build the TMA descriptors");
+        gemm_params &p = pp.seg[s];
+        p.M = M;
+        p.N = g.N;
+        p.K = K;
+        p.ldc = g.ldc;
+        p.n_out = g.n_out;
+        p.c = g.c;
+        p.err = err_flag;
+        p.mode = g.mode;
+        // TMA stores need 16-byte aligned rows; SwiGLU halves the width and keeps direct stores
+        p.tma_store = g.mode != MODE_SWIGLU && g.ldc % 4 == 0 && ((uintptr_t) g.c & 15) == 0 &&
+                      make_tmap_out(&maps.c[s], g.c, M, g.n_out, g.ldc);
+        pp.tile0[s] = tiles_n;
+        tiles_n += (int) ((g.N + BN_T - 1) / BN_T);
+    }
+    pp.tile0[nseg] = tiles_n;
+    pp.num_n = tiles_n;
     static bool attr_set = false;
     if (!attr_set) {
         if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -626,7 +669,7 @@ int launch_pair(const CUtensorMap &ta, const uint16_t *b_bf16, int64_t ldb, int6
             return check_launch("gemm (shared memory size)");
         attr_set = true;
     }
-    const int64_t tiles = (int64_t) p.num_m * p.num_n;
+    const int64_t tiles = (int64_t) pp.num_m * pp.num_n;
     const int pairs = (int) (tiles < num_sms() / 2 ? tiles : num_sms() / 2);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) (2 * pairs));
@@ -640,56 +683,26 @@ int launch_pair(const CUtensorMap &ta, const uint16_t *b_bf16, int64_t ldb, int6
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T>, ta, tb, tc, p);
+    cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T>, ta, maps, pp);
     return check_launch("gemm");
 }
 
-}  // namespace
-
-int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
-                int64_t K, int mode, float *c, int64_t ldc, int64_t n_out, unsigned *err_flag, cudaStream_t st) {
-    if (M <= 0 || N <= 0) return 0;
-    if (K <= 0 || K % 8 || lda < K || ldb < K || lda % 8 || ldb % 8 || ((uintptr_t) a_bf16 & 15) ||
-        ((uintptr_t) b_bf16 & 15) || !err_flag)
-        return set_error("gemm: K and the row strides must be multiples of 8 and the operands 16-byte aligned");
-    if (mode < MODE_F32 || mode > MODE_SWIGLU || (mode == MODE_SWIGLU && N % 16))
-        return set_error("gemm: bad output mode");
-    const int64_t width = mode == MODE_SWIGLU ? N / 2 : N;
-    if (n_out <= 0 || n_out > width) n_out = width;
-    if (ldc < n_out) return set_error("gemm: ldc smaller than the output width");
-    // The CTA-pair kernel unless ZEST_GEMM_PAIR=0 or the rows fit one 128-row tile.
-    const char *pair_env = getenv("ZEST_GEMM_PAIR");
-    const bool pair = M > BM && !(pair_env && pair_env[0] == '0');
-    CUtensorMap ta, tb;
-    if (!make_tmap(&ta, a_bf16, M, K, lda, BM) || (!pair && !make_tmap(&tb, b_bf16, N, K, ldb, BN)))
-        return set_error("gemm: cannot build the TMA descriptors");
-    if (pair) {
-        // 256-wide N tiles: measured on every shape of the configs, narrower
-        // tiles lose 15-45 % per flop, more than they win back by rounding
-        // to fewer waves. Narrower ones stay selectable for tests and tuning.
-        int best = 256;
-        if (const char *force = getenv("ZEST_GEMM_BN")) {
-            const int bn = atoi(force);
-            if (bn == 256 || bn == 192 || bn == 160 || bn == 128) best = bn;
-        }
-        switch (best) {
-            case 192: return launch_pair<192>(ta, b_bf16, ldb, M, N, K, mode, c, ldc, n_out, err_flag, st);
-            case 160: return launch_pair<160>(ta, b_bf16, ldb, M, N, K, mode, c, ldc, n_out, err_flag, st);
-            case 128: return launch_pair<128>(ta, b_bf16, ldb, M, N, K, mode, c, ldc, n_out, err_flag, st);
-            default: return launch_pair<256>(ta, b_bf16, ldb, M, N, K, mode, c, ldc, n_out, err_flag, st);
-        }
-    }
+// The one-CTA kernel (128 x 256 tiles), for calls of at most 128 rows.
+int launch_single(const CUtensorMap &ta, int64_t M, int64_t K, const gemm_seg &g, unsigned *err_flag,
+                  cudaStream_t st) {
+    CUtensorMap tb;
+    if (!make_tmap(&tb, g.b, g.N, K, g.ldb, BN)) return set_error("gemm: cannot build the TMA descriptors");
     gemm_params p;
     p.M = M;
-    p.N = N;
+    p.N = g.N;
     p.K = K;
-    p.ldc = ldc;
-    p.n_out = n_out;
-    p.c = c;
+    p.ldc = g.ldc;
+    p.n_out = g.n_out;
+    p.c = g.c;
     p.err = err_flag;
-    p.mode = mode;
+    p.mode = g.mode;
     p.num_m = (int) ((M + BM - 1) / BM);
-    p.num_n = (int) ((N + BN - 1) / BN);
+    p.num_n = (int) ((g.N + BN - 1) / BN);
     p.num_k = (int) ((K + BK - 1) / BK);
     p.tma_store = 0;
     static bool attr = false;
@@ -703,6 +716,57 @@ int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int
     const int grid = (int) (tiles < num_sms() ? tiles : num_sms());
     gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, p);
     return check_launch("gemm");
+}
+
+}  // namespace
+
+int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int nseg, gemm_seg *segs,
+                      unsigned *err_flag, cudaStream_t st) {
+    if (M <= 0 || nseg <= 0) return 0;
+    if (nseg > MAX_SEG) return set_error("gemm: at most 4 weights in a group");
+    if (K <= 0 || K % 8 || lda < K || lda % 8 || ((uintptr_t) a_bf16 & 15) || !err_flag)
+        return set_error("gemm: K and the row strides must be multiples of 8 and the operands 16-byte aligned");
+    for (int s = 0; s < nseg; s++) {
+        gemm_seg &g = segs[s];
+        if (g.N <= 0 || g.ldb < K || g.ldb % 8 || ((uintptr_t) g.b & 15))
+            return set_error("gemm: K and the row strides must be multiples of 8 and the operands 16-byte aligned");
+        if (g.mode < MODE_F32 || g.mode > MODE_SWIGLU || (g.mode == MODE_SWIGLU && g.N % 16))
+            return set_error("gemm: bad output mode");
+        const int64_t width = g.mode == MODE_SWIGLU ? g.N / 2 : g.N;
+        if (g.n_out <= 0 || g.n_out > width) g.n_out = width;
+        if (g.ldc < g.n_out) return set_error("gemm: ldc smaller than the output width");
+    }
+    // The CTA-pair kernel unless ZEST_GEMM_PAIR=0 or the rows fit one 128-row tile.
+    const char *pair_env = getenv("ZEST_GEMM_PAIR");
+    const bool pair = M > BM && !(pair_env && pair_env[0] == '0');
+    CUtensorMap ta;
+    if (!make_tmap(&ta, a_bf16, M, K, lda, BM)) return set_error("gemm: cannot build the TMA descriptors");
+    if (!pair) {
+        for (int s = 0; s < nseg; s++)
+            if (launch_single(ta, M, K, segs[s], err_flag, st)) return -1;
+        return 0;
+    }
+    // 256-wide N tiles: measured on every shape of the configs, narrower
+    // tiles lose 15-45 % per flop, more than they win back by rounding to
+    // fewer waves. Narrower ones stay selectable for tests and tuning.
+    int bn = 256;
+    if (const char *force = getenv("ZEST_GEMM_BN")) {
+        const int f = atoi(force);
+        if (f == 192 || f == 160 || f == 128) bn = f;
+    }
+    switch (bn) {
+        case 192: return launch_pair_group<192>(ta, M, K, nseg, segs, err_flag, st);
+        case 160: return launch_pair_group<160>(ta, M, K, nseg, segs, err_flag, st);
+        case 128: return launch_pair_group<128>(ta, M, K, nseg, segs, err_flag, st);
+        default: return launch_pair_group<256>(ta, M, K, nseg, segs, err_flag, st);
+    }
+}
+
+int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
+                int64_t K, int mode, float *c, int64_t ldc, int64_t n_out, unsigned *err_flag, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return 0;
+    gemm_seg g = { b_bf16, ldb, N, ldc, n_out, mode, c };
+    return launch_gemm_group(a_bf16, lda, M, K, 1, &g, err_flag, st);
 }
 
 int launch_gemm_simt(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,

@@ -37,6 +37,18 @@ int launch_convert_weight(int type, const void *src0, const void *src1, int fuse
                           int64_t src_rows_total, int64_t K, int64_t n_pad, uint8_t *b_bytes, uint16_t *b_bf16,
                           cudaStream_t st);
 
+// One weight of a grouped GEMM: its B operand (N rows), output and mode.
+struct gemm_seg {
+    const uint16_t *b;
+    int64_t ldb, N, ldc, n_out;  // n_out <= 0: all (N, or N/2 for SwiGLU)
+    int mode;
+    float *c;
+};
+
+// Up to 4 weights sharing one A (q, k and v; gate and up) in one launch.
+int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int nseg, gemm_seg *segs,
+                      unsigned *err_flag, cudaStream_t st);
+
 // n_out: output columns to write (<= 0: all, N or N/2 for SwiGLU); a fused
 // gate/up copy padded to f_pad writes only the real F.
 int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,

@@ -25,6 +25,7 @@ QUANT = {TYPE_F32: (1, 4), TYPE_F16: (1, 2), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (25
          TYPE_Q6_K: (256, 210), TYPE_IQ3_S: (256, 110)}
 
 _i64, _vp, _int, _u32p = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)
+_vpp, _i64p, _intp = ctypes.POINTER(_vp), ctypes.POINTER(_i64), ctypes.POINTER(_int)
 
 
 class ZestError(RuntimeError):
@@ -60,6 +61,7 @@ def lib() -> ctypes.CDLL:
         "zest_convert_weight": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
         "zest_convert_gate_up": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
         "zest_gemm": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
+        "zest_gemm_group": (_int, [_vp, _i64, _i64, _i64, _int, _vpp, _i64p, _i64p, _intp, _vpp, _i64p, _vp, _vp]),
         "zest_mul_mat_noalloc": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
         "zest_rms_norm": (_int, [_vp, _i64, _i64, ctypes.c_float, _vp, _vp]),
         "zest_mul_row": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
@@ -80,6 +82,7 @@ def lib() -> ctypes.CDLL:
         "zest_weight_bfp16": (_vp, [_vp, ctypes.POINTER(WKey), _int]),
         "zest_weight_bf16": (_vp, [_vp, ctypes.POINTER(WKey), _int, ctypes.POINTER(_i64)]),
         "zest_mul_mat": (_int, [_vp, ctypes.POINTER(WKey), _int, _vp, _i64, _vp, _int]),
+        "zest_mul_mat_group": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, _i64, _vpp, _int]),
         "zest_stream": (_vp, [_vp]),
         "zest_take_times": (_int, [_vp, ctypes.POINTER(Times)]),
     }
@@ -92,14 +95,15 @@ def lib() -> ctypes.CDLL:
 
 def exported_symbols() -> list[str]:
     return [n for n in ("zest_version", "zest_last_error", "zest_load_iq3s_grid", "zest_pack_activations",
-                        "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_mul_mat_noalloc",
+                        "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_gemm_group",
+                        "zest_mul_mat_noalloc",
                         "zest_rms_norm", "zest_mul_row", "zest_add", "zest_scale", "zest_glu", "zest_rope_table",
                         "zest_rope",
                         "zest_usable", "zest_open",
                         "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
                         "zest_add_weight_values",
-                        "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_mul_mat", "zest_stream",
-                        "zest_take_times")]
+                        "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_mul_mat",
+                        "zest_mul_mat_group", "zest_stream", "zest_take_times")]
 
 
 def _check(rc: int, what: str) -> None:
@@ -197,6 +201,29 @@ def gemm(a_bf16, b_bf16, M: int, N: int, mode: int = MODE_F32, out=None, err=Non
     return out
 
 
+def gemm_group(a_bf16, bs, M: int, Ns, modes, outs=None, err=None):
+    """K3 over up to 4 weights sharing A in one launch: outs[i] = A * bs[i]^T."""
+    import torch
+    n = len(bs)
+    K = a_bf16.shape[1]
+    if outs is None:
+        outs = [torch.empty((M, N // 2 if m == MODE_SWIGLU else N), dtype=torch.float32, device=a_bf16.device)
+                for N, m in zip(Ns, modes)]
+    own_err = err is None
+    if own_err:
+        err = torch.zeros(1, dtype=torch.int32, device=a_bf16.device)
+    arr = lambda t, vals: (t * n)(*vals)
+    _check(lib().zest_gemm_group(_ptr(a_bf16), a_bf16.stride(0), M, K, n, arr(_vp, [b.data_ptr() for b in bs]),
+                                 arr(_i64, [b.stride(0) for b in bs]), arr(_i64, Ns), arr(_int, modes),
+                                 arr(_vp, [o.data_ptr() for o in outs]), arr(_i64, [o.stride(0) for o in outs]),
+                                 _ptr(err), _stream()), "zest_gemm_group")
+    if own_err:
+        e = int(err.item())
+        if e:
+            raise ZestError(f"zest_gemm_group raised device error bits {e:#x}")
+    return outs
+
+
 # --- the matmul service -------------------------------------------------------
 
 class Npu:
@@ -247,6 +274,14 @@ class Npu:
     def mul_mat(self, key: WKey, x_ptr: int, T: int, y_ptr: int, on_device: bool, fused: bool = False):
         _check(lib().zest_mul_mat(self.h, ctypes.byref(key), int(fused), ctypes.c_void_p(x_ptr), T,
                                   ctypes.c_void_p(y_ptr), int(on_device)), "zest_mul_mat")
+
+    def mul_mat_group(self, keys, x_ptr: int, T: int, y_ptrs, on_device: bool, fused=None):
+        """One activation pack and one GEMM launch for weights sharing x."""
+        n = len(keys)
+        fused = fused or [False] * n
+        _check(lib().zest_mul_mat_group(self.h, n, (WKey * n)(*keys), (_int * n)(*[int(f) for f in fused]),
+                                        ctypes.c_void_p(x_ptr), T, (_vp * n)(*y_ptrs), int(on_device)),
+               "zest_mul_mat_group")
 
     def stream(self) -> int:
         return int(lib().zest_stream(self.h) or 0)

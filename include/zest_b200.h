@@ -103,6 +103,16 @@ int zest_convert_gate_up(int type, const void *gate, const void *up, int64_t row
 int zest_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
               int64_t K, int mode, float *c, int64_t ldc, unsigned *err, void *stream);
 
+/* K3 for up to 4 weights that share one A (q, k and v; gate and up) in one
+ * launch: c_i[M][ldc_i] = A * B_i^T with B_i of N_i rows and its own mode.
+ * The weights' tiles run end to end in one persistent launch, with no kernel
+ * tail between them.
+ * Replaces: a group of NPU calls submitted as one runlist
+ * (xdna_npu::begin / submit, src/xdna-npu.cpp:476-531). */
+int zest_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int n, const uint16_t *const *b_bf16,
+                    const int64_t *ldb, const int64_t *N, const int *mode, float *const *c, const int64_t *ldc,
+                    unsigned *err, void *stream);
+
 /* K2 + K3 without allocating anything: y[T][ldy] = x[T][K] * W^T, where w_bf16
  * is a weight's bf16 B operand (zest_convert_weight / zest_weight_bf16) of N
  * rows and the same mode and err word as zest_gemm. No counterpart in the
@@ -224,6 +234,14 @@ const uint16_t *zest_weight_bf16(const zest_npu *npu, const zest_wkey *key, int 
  * when on_device. Checks every result for NaN/Inf.
  * Replaces: xdna_npu::mul_mat (src/xdna-npu.cpp:392-444). */
 int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x, int64_t T, float *y, int on_device);
+
+/* The same for up to 4 weights added above that share the input x (same K):
+ * one pack and one grouped launch; y[i] gets weight i's out_width values a
+ * row (fused[i]: the SwiGLU of a fused pair).
+ * Replaces: xdna_npu::begin / encode_row / submit / wait / decode_row for
+ * one group (src/xdna-npu.cpp:476-551). */
+int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *fused, const float *x, int64_t T,
+                       float *const *y, int on_device);
 
 /* The service's CUDA stream (a cudaStream_t). */
 void *zest_stream(zest_npu *npu);

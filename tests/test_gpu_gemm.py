@@ -148,3 +148,52 @@ def test_gemm_full_size_vs_torch_fp32():
     ref = a32 @ b32.T
     err = ((c - ref).abs().max() / ref.abs().max()).item()
     assert err <= TOL, err
+
+
+@pytest.mark.parametrize("pair", ["1", "0"])
+@pytest.mark.parametrize("bn", ["256", "128"])
+def test_gemm_group_equals_separate_launches(pair, bn, monkeypatch):
+    # q/k/v-like segments of ragged widths plus a SwiGLU gate/up segment sharing A:
+    # one grouped launch gives bit for bit what a launch per weight gives
+    monkeypatch.setenv("ZEST_GEMM_PAIR", pair)
+    monkeypatch.setenv("ZEST_GEMM_BN", bn)
+    M, K = 900, 640
+    _, ah = Z.pack_activations(dev(O.activations(M, K, 7)))
+    Ns, modes, bs = [1000, 300, 512], [Z.MODE_F32, Z.MODE_BF16, Z.MODE_F32], []
+    for i, N in enumerate(Ns):
+        _, bh = Z.convert_weight(O.Q8_0, dev(O.quantize(O.Q8_0, O.weights_f32(N, K, 20 + i))), N, K)
+        bs.append(bh)
+    F = 200
+    gr = O.quantize(O.Q8_0, O.weights_f32(F, K, 30))
+    ur = O.quantize(O.Q8_0, O.weights_f32(F, K, 31))
+    _, gu = Z.convert_gate_up(O.Q8_0, dev(gr), dev(ur), F, K)
+    bs.append(gu)
+    Ns.append(gu.shape[0])
+    modes.append(Z.MODE_SWIGLU)
+    outs = Z.gemm_group(ah, bs, M, Ns, modes)
+    for b, N, m, o in zip(bs, Ns, modes, outs):
+        assert np.array_equal(host(o), host(Z.gemm(ah, b, M, N, m)))
+
+
+def test_gemm_group_vs_oracle():
+    M, K = 1300, 512
+    x = O.activations(M, K, 9)
+    _, ah = Z.pack_activations(dev(x))
+    a_dec = bf16_to_f32(host(ah)[:M].view(np.uint16))
+    Ns, bs, decs = [768, 256], [], []
+    for i, N in enumerate(Ns):
+        _, bh = Z.convert_weight(O.Q6_K, dev(O.quantize(O.Q6_K, O.weights_f32(N, K, 40 + i))), N, K)
+        bs.append(bh)
+        decs.append(bf16_to_f32(host(bh)[:N].view(np.uint16)))
+    outs = Z.gemm_group(ah, bs, M, Ns, [Z.MODE_F32, Z.MODE_F32])
+    for o, d in zip(outs, decs):
+        assert O.nmax_err(host(o), O.mul_mat(d, a_dec)) <= TOL
+
+
+def test_gemm_group_rejects_bad_groups():
+    _, ah = Z.pack_activations(dev(O.activations(256, 64, 1)))
+    _, bh = Z.convert_weight(O.F32, dev(O.weights_f32(512, 64, 2).view(np.uint8)), 512, 64)
+    with pytest.raises(Z.ZestError, match="1 to 4"):
+        Z.gemm_group(ah, [bh] * 5, 256, [512] * 5, [Z.MODE_F32] * 5)
+    with pytest.raises(Z.ZestError, match="mode"):
+        Z.gemm_group(ah, [bh, bh], 256, [512, 500], [Z.MODE_F32, Z.MODE_SWIGLU])

@@ -121,3 +121,59 @@ def test_injected_nan_is_caught():
     """)
     assert r.returncode == 0, r.stderr
     assert "NaN or infinity" in r.stdout
+
+
+@pytest.mark.parametrize("on_device", [False, True])
+def test_mul_mat_group_equals_separate_calls(on_device):
+    # q, k, v and a fused gate/up sharing one input: one pack, one launch,
+    # the same bits as a call per weight
+    npu = Z.Npu(0)
+    npu.set_out16(False)
+    K, T = 512, 700
+    raws = [O.quantize(O.Q4_K, O.weights_f32(N, K, 50 + i)) for i, N in enumerate((1024, 256, 256))]
+    keys = [Z.Npu.key(r.ctypes.data, O.Q4_K, K, N) for r, N in zip(raws, (1024, 256, 256))]
+    for k, r in zip(keys, raws):
+        npu.add_weight(k, r.ctypes.data, on_device=False)
+    F = 600
+    g = O.quantize(O.Q6_K, O.weights_f32(F, K, 60))
+    u = O.quantize(O.Q6_K, O.weights_f32(F, K, 61))
+    gkey = Z.Npu.key(g.ctypes.data, O.Q6_K, K, F)
+    npu.add_fused(gkey, g.ctypes.data, u.ctypes.data, on_device=False)
+    keys.append(gkey)
+    fused = [False, False, False, True]
+    widths = [1024, 256, 256, F]
+    x = O.activations(T, K, 62)
+    if on_device:
+        xd = dev(x)
+        ys = [torch.empty((T, w), dtype=torch.float32, device="cuda") for w in widths]
+        solo = [torch.empty((T, w), dtype=torch.float32, device="cuda") for w in widths]
+        torch.cuda.synchronize()
+        npu.mul_mat_group(keys, xd.data_ptr(), T, [y.data_ptr() for y in ys], True, fused)
+        for k, f, y in zip(keys, fused, solo):
+            npu.mul_mat(k, xd.data_ptr(), T, y.data_ptr(), True, fused=f)
+        got, want = [host(y) for y in ys], [host(y) for y in solo]
+    else:
+        got = [np.empty((T, w), np.float32) for w in widths]
+        want = [np.empty((T, w), np.float32) for w in widths]
+        npu.mul_mat_group(keys, x.ctypes.data, T, [y.ctypes.data for y in got], False, fused)
+        for k, f, y in zip(keys, fused, want):
+            npu.mul_mat(k, x.ctypes.data, T, y.ctypes.data, False, fused=f)
+    for a, b in zip(got, want):
+        assert np.array_equal(a, b)
+    t = npu.take_times()
+    assert t.calls == 8
+    npu.close()
+
+
+def test_mul_mat_group_rejects_mixed_k():
+    npu = Z.Npu(0)
+    r1 = O.quantize(O.Q8_0, O.weights_f32(512, 256, 1))
+    r2 = O.quantize(O.Q8_0, O.weights_f32(512, 512, 2))
+    k1, k2 = Z.Npu.key(r1.ctypes.data, O.Q8_0, 256, 512), Z.Npu.key(r2.ctypes.data, O.Q8_0, 512, 512)
+    npu.add_weight(k1, r1.ctypes.data, on_device=False)
+    npu.add_weight(k2, r2.ctypes.data, on_device=False)
+    x = O.activations(128, 256, 3)
+    y1, y2 = np.empty((128, 512), np.float32), np.empty((128, 512), np.float32)
+    with pytest.raises(Z.ZestError, match="differ in K"):
+        npu.mul_mat_group([k1, k2], x.ctypes.data, 128, [y1.ctypes.data, y2.ctypes.data], False)
+    npu.close()
