@@ -5,6 +5,7 @@
 #include "zest_device.cuh"
 #include "zest_internal.h"
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -125,8 +126,11 @@ struct zest_npu {
     };
     using key_t = std::tuple<const void *, const void *, int, int64_t, int64_t, int>;
 
+    // a host-buffer call is cut into at most MAX_CHUNKS row chunks whose input
+    // copies (st_in), kernels (st) and output copies (st_out) overlap
+    static constexpr int MAX_CHUNKS = 16;
     int device = 0;
-    cudaStream_t st = nullptr;
+    cudaStream_t st = nullptr, st_in = nullptr, st_out = nullptr;
     bool out16 = true;
     std::map<key_t, weight> weights;
     // per-call workspace; grows only
@@ -135,6 +139,8 @@ struct zest_npu {
     size_t x_cap = 0, y_cap = 0, a_cap = 0;
     unsigned *err_dev = nullptr, *err_host = nullptr;
     cudaEvent_t ev[5] = {};
+    cudaEvent_t in_ev[MAX_CHUNKS] = {}, done_ev[MAX_CHUNKS] = {}, out_ev = nullptr;  // ordering only
+    cudaEvent_t t_pack[MAX_CHUNKS] = {}, t_gemm[MAX_CHUNKS] = {}, t_end[MAX_CHUNKS] = {};
     zest_times times = {};
     // whether GGML_XDNA_FAIL_AFTER / _NAN_AFTER apply: not to the start-up
     // self-test, which the reference runs outside its injection points too
@@ -143,6 +149,8 @@ struct zest_npu {
     ~zest_npu() {
         cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);
+        if (st_in) cudaStreamSynchronize(st_in);
+        if (st_out) cudaStreamSynchronize(st_out);
         for (auto &kv : weights) {
             cudaFree(kv.second.bytes);
             cudaFree(kv.second.bf16);
@@ -154,7 +162,13 @@ struct zest_npu {
         if (err_host) cudaFreeHost(err_host);
         for (cudaEvent_t e : ev)
             if (e) cudaEventDestroy(e);
+        for (int c = 0; c < MAX_CHUNKS; c++)
+            for (cudaEvent_t e : { in_ev[c], done_ev[c], t_pack[c], t_gemm[c], t_end[c] })
+                if (e) cudaEventDestroy(e);
+        if (out_ev) cudaEventDestroy(out_ev);
         if (st) cudaStreamDestroy(st);
+        if (st_in) cudaStreamDestroy(st_in);
+        if (st_out) cudaStreamDestroy(st_out);
     }
 
     static key_t key_of(const zest_wkey *k, int fused) { return key_t(k->buffer, k->data, k->type, k->K, k->N, fused); }
@@ -191,6 +205,18 @@ static bool injected_nan() {
     static const long long after = env_ll("GGML_XDNA_NAN_AFTER", -1);
     static std::atomic<long long> n{ 0 };
     return after >= 0 && ++n > after;
+}
+
+// Rows per chunk of a host-buffer call: whole below 2048 rows, else about a
+// sixteenth of the call (at least 512 rows) so the first copy in and the last
+// copy out, which nothing hides, stay short; GGML_ZEST_CHUNK_ROWS overrides.
+// PCIe, not the kernels, bounds such a call: a B200's Gen5 x16 link moves
+// about 55 GB/s one way and 96 GB/s both ways at once.
+static int64_t chunk_rows(int64_t T) {
+    static const long long force = env_ll("GGML_ZEST_CHUNK_ROWS", 0);
+    int64_t rows = force > 0 ? force : (T < 2048 ? T : std::max<int64_t>(512, T / 16));
+    rows = std::max<int64_t>(rows, (T + zest_npu::MAX_CHUNKS - 1) / zest_npu::MAX_CHUNKS);
+    return (rows + TILE_M - 1) / TILE_M * TILE_M;
 }
 
 static int cuda_fail(const char *what, cudaError_t e) {
@@ -329,8 +355,18 @@ zest_npu *zest_open(int device) {
     npu->device = device;
     npu->out16 = env_ll("GGML_XDNA_OUT16", 1) != 0;
     cudaError_t e = cudaStreamCreateWithFlags(&npu->st, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&npu->st_in, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&npu->st_out, cudaStreamNonBlocking);
     for (cudaEvent_t &ev : npu->ev)
         if (e == cudaSuccess) e = cudaEventCreate(&ev);
+    for (int c = 0; c < zest_npu::MAX_CHUNKS && e == cudaSuccess; c++) {
+        e = cudaEventCreateWithFlags(&npu->in_ev[c], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&npu->done_ev[c], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreate(&npu->t_pack[c]);
+        if (e == cudaSuccess) e = cudaEventCreate(&npu->t_gemm[c]);
+        if (e == cudaSuccess) e = cudaEventCreate(&npu->t_end[c]);
+    }
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&npu->out_ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc(&npu->err_dev, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMallocHost(&npu->err_host, sizeof(unsigned));
     if (e != cudaSuccess) {
@@ -424,38 +460,69 @@ int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *f
     const float *xd = on_device ? x : npu->x_dev;
     float *yd[4];
     for (int i = 0; i < n; i++) yd[i] = on_device ? y[i] : (float *) ((char *) npu->y_dev + y_off[i]);
+    const bool nan = npu->inject && injected_nan();
+    // Device buffers: one chunk. Host buffers: row chunks (multiples of the
+    // 128-row tile) whose copies in and out overlap the other chunks' kernels.
+    const int64_t rows = on_device ? T : chunk_rows(T);
+    const int nch = (int) ((T + rows - 1) / rows);
     cudaEventRecord(npu->ev[0], st);
-    if (!on_device) cudaMemcpyAsync(npu->x_dev, x, x_bytes, cudaMemcpyHostToDevice, st);
     cudaMemsetAsync(npu->err_dev, 0, sizeof(unsigned), st);
-    cudaEventRecord(npu->ev[1], st);
-    int rc = launch_pack_activations(xd, T, K, K, m_pad, nullptr, npu->a_bf16, K, st);
-    cudaEventRecord(npu->ev[2], st);
-    gemm_seg segs[4];
-    for (int i = 0; i < n; i++) segs[i] = { w[i]->bf16, K, w[i]->n_pad, w[i]->n_out, w[i]->n_out, w[i]->mode, yd[i] };
-    if (!rc) rc = launch_gemm_group(npu->a_bf16, K, T, K, n, segs, npu->err_dev, st);
-    if (!rc && npu->inject && injected_nan()) {
-        for (int i = 0; i < n; i++) {
-            cudaMemsetAsync(yd[i], 0xff, (size_t) (T * w[i]->n_out) * 4, st);
-            check_finite_kernel<<<148, 256, 0, st>>>(yd[i], T * w[i]->n_out, npu->err_dev);
+    cudaStreamWaitEvent(npu->st_in, npu->ev[0], 0);
+    cudaStreamWaitEvent(npu->st_out, npu->ev[0], 0);
+    int rc = 0;
+    for (int c = 0; c < nch && !rc; c++) {
+        const int64_t r0 = c * rows, m = std::min(rows, T - r0);
+        if (!on_device) {
+            cudaMemcpyAsync(npu->x_dev + r0 * K, x + r0 * K, (size_t) (m * K) * 4, cudaMemcpyHostToDevice,
+                            npu->st_in);
+            cudaEventRecord(npu->in_ev[c], npu->st_in);
+            cudaStreamWaitEvent(st, npu->in_ev[c], 0);
+        }
+        cudaEventRecord(npu->t_pack[c], st);
+        rc = launch_pack_activations(xd + r0 * K, m, K, K, (m + TILE_M - 1) / TILE_M * TILE_M, nullptr,
+                                     npu->a_bf16 + r0 * K, K, st);
+        cudaEventRecord(npu->t_gemm[c], st);
+        gemm_seg segs[4];
+        for (int i = 0; i < n; i++)
+            segs[i] = { w[i]->bf16, K, w[i]->n_pad, w[i]->n_out, w[i]->n_out, w[i]->mode, yd[i] + r0 * w[i]->n_out };
+        if (!rc) rc = launch_gemm_group(npu->a_bf16 + r0 * K, K, m, K, n, segs, npu->err_dev, st);
+        if (!rc && nan) {
+            for (int i = 0; i < n; i++) {
+                cudaMemsetAsync(segs[i].c, 0xff, (size_t) (m * w[i]->n_out) * 4, st);
+                check_finite_kernel<<<148, 256, 0, st>>>(segs[i].c, m * w[i]->n_out, npu->err_dev);
+            }
+        }
+        cudaEventRecord(npu->t_end[c], st);
+        if (!on_device) {
+            cudaEventRecord(npu->done_ev[c], st);
+            cudaStreamWaitEvent(npu->st_out, npu->done_ev[c], 0);
+            for (int i = 0; i < n; i++)
+                cudaMemcpyAsync(y[i] + r0 * w[i]->n_out, segs[i].c, (size_t) (m * w[i]->n_out) * 4,
+                                cudaMemcpyDeviceToHost, npu->st_out);
         }
     }
-    cudaEventRecord(npu->ev[3], st);
-    if (!on_device)
-        for (int i = 0; i < n; i++)
-            cudaMemcpyAsync(y[i], yd[i], (size_t) (T * w[i]->n_out) * 4, cudaMemcpyDeviceToHost, st);
     cudaMemcpyAsync(npu->err_host, npu->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
+    cudaEventRecord(npu->out_ev, npu->st_out);
+    cudaStreamWaitEvent(st, npu->out_ev, 0);
     cudaEventRecord(npu->ev[4], st);
     const cudaError_t e = cudaStreamSynchronize(st);
-    if (rc) return rc;
+    if (rc) {
+        cudaStreamSynchronize(npu->st_in);
+        cudaStreamSynchronize(npu->st_out);
+        return rc;
+    }
     if (e != cudaSuccess) return cuda_fail("zest_mul_mat", e);
-    float a = 0, b = 0, c = 0, d = 0;
-    cudaEventElapsedTime(&a, npu->ev[0], npu->ev[1]);
-    cudaEventElapsedTime(&b, npu->ev[1], npu->ev[2]);
-    cudaEventElapsedTime(&c, npu->ev[2], npu->ev[3]);
-    cudaEventElapsedTime(&d, npu->ev[3], npu->ev[4]);
-    npu->times.copy_ms += a + d;
-    npu->times.encode_ms += b;
-    npu->times.gemm_ms += c;
+    float total = 0, busy = 0;
+    cudaEventElapsedTime(&total, npu->ev[0], npu->ev[4]);
+    for (int c = 0; c < nch; c++) {
+        float a = 0, b = 0;
+        cudaEventElapsedTime(&a, npu->t_pack[c], npu->t_gemm[c]);
+        cudaEventElapsedTime(&b, npu->t_gemm[c], npu->t_end[c]);
+        npu->times.encode_ms += a;
+        npu->times.gemm_ms += b;
+        busy += a + b;
+    }
+    npu->times.copy_ms += std::max(0.0f, total - busy);  // the copies the kernels did not hide
     npu->times.calls += n;
     if (*npu->err_host & ERR_TIMEOUT) return set_error("a GPU kernel's bounded wait ran out");
     if (*npu->err_host & ERR_NOT_FINITE) return set_error("the GPU's results held NaN or infinity");

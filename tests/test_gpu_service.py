@@ -177,3 +177,36 @@ def test_mul_mat_group_rejects_mixed_k():
     with pytest.raises(Z.ZestError, match="differ in K"):
         npu.mul_mat_group([k1, k2], x.ctypes.data, 128, [y1.ctypes.data, y2.ctypes.data], False)
     npu.close()
+
+
+def test_host_buffer_chunks_equal_one_pass():
+    # host buffers cut into 256-row chunks (the last one ragged) overlap their
+    # copies with the kernels; the results are those of one device-buffer pass
+    code = textwrap.dedent(f"""
+        import sys
+        sys.path[:0] = [{str(ROOT)!r}, {str(ROOT / 'ggml-xdna_b200')!r}]
+        import numpy as np, torch, zest_b200 as Z
+        from oracle import oracle as O
+        npu = Z.Npu(0)
+        npu.set_out16(False)
+        K, T = 512, 1000
+        raws = [O.quantize(O.Q8_0, O.weights_f32(N, K, 70 + N)) for N in (768, 512)]
+        keys = [Z.Npu.key(r.ctypes.data, O.Q8_0, K, N) for r, N in zip(raws, (768, 512))]
+        for k, r in zip(keys, raws):
+            npu.add_weight(k, r.ctypes.data, on_device=False)
+        x = O.activations(T, K, 71)
+        ys = [torch.empty((T, N), dtype=torch.float32).pin_memory() for N in (768, 512)]
+        npu.mul_mat_group(keys, torch.from_numpy(x).pin_memory().data_ptr(), T, [y.data_ptr() for y in ys], False)
+        xd = torch.from_numpy(x).cuda()
+        yd = [torch.empty((T, N), dtype=torch.float32, device="cuda") for N in (768, 512)]
+        torch.cuda.synchronize()
+        npu.mul_mat_group(keys, xd.data_ptr(), T, [y.data_ptr() for y in yd], True)
+        ok = all(np.array_equal(a.numpy(), b.cpu().numpy()) for a, b in zip(ys, yd))
+        ph = np.empty((T, 768), np.float32)  # pageable host memory takes the same path
+        npu.mul_mat(keys[0], x.ctypes.data, T, ph.ctypes.data, False)
+        ok = ok and np.array_equal(ph, ys[0].numpy())
+        print("CHUNKS", "OK" if ok else "DIFFER")
+    """)
+    env = dict(os.environ, GGML_ZEST_CHUNK_ROWS="256")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
+    assert "CHUNKS OK" in r.stdout, r.stdout + r.stderr
