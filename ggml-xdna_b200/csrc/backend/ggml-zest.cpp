@@ -365,6 +365,12 @@ bool blocks() {
     return v;
 }
 
+// GGML_ZEST_GROUPS=0 runs every MUL_MAT on its own (find_groups).
+bool groups_on() {
+    static const bool v = env_int("GGML_ZEST_GROUPS", 1) != 0;
+    return v;
+}
+
 // Whether a tensor may live in host memory once allocated: a graph input, an
 // embedding lookup, or one in a host buffer (src/ggml-zest.cpp:1149-1158).
 bool maybe_host(const ggml_tensor *t) {
@@ -454,7 +460,7 @@ struct context {
     size_t rope_cap = 0;
     // where the time goes, printed with GGML_XDNA_TRACE=1
     double compute_ms = 0, copy_ms = 0;
-    int64_t matmuls = 0, pieces = 0, late_copies = 0, small_ops = 0, fused = 0;
+    int64_t matmuls = 0, pieces = 0, late_copies = 0, small_ops = 0, fused = 0, grouped = 0;
 
     void *stage_slot(size_t n) {
         if (stage_next == stage.size()) stage.emplace_back(nullptr, 0);
@@ -637,6 +643,73 @@ bool ensure_fused(context &ctx, const fusion &f, zest_wkey &key, std::string &er
     return rc == 0;
 }
 
+// MUL_MATs of a piece on one input, run as one grouped call (one pack, one
+// launch) at the first one's turn, as the reference submits a piece's
+// matmuls as one runlist (src/xdna-npu.cpp:476-531). A later matmul joins
+// only where running it early is safe: no node between the two turns
+// writes or reads its output's bytes, which ggml's allocator may have lent
+// to a tensor whose life ends in between. Input and outputs share one
+// residency (all device memory, or all host memory), at most 4 per group.
+bool overlaps(const ggml_tensor *a, const ggml_tensor *b) {
+    if (!a || !b || !a->data || !b->data) return false;
+    const char *a0 = (const char *) a->data, *b0 = (const char *) b->data;
+    return a0 < b0 + ggml_nbytes(b) && b0 < a0 + ggml_nbytes(a);
+}
+
+template <typename Skip>
+std::vector<std::vector<ggml_tensor *>> find_groups(const std::vector<ggml_tensor *> &nodes, const Skip &skip) {
+    std::vector<std::vector<ggml_tensor *>> out;
+    std::unordered_map<const ggml_tensor *, bool> taken;
+    for (size_t i = 0; i < nodes.size(); i++) {
+        ggml_tensor *first = nodes[i];
+        if (!op_is(first, "MUL_MAT") || skip.count(first) || taken.count(first)) continue;
+        const ggml_tensor *x = first->src[1];
+        const bool host = is_host(x);
+        if (is_host(first) != host) continue;
+        std::vector<ggml_tensor *> g{ first };
+        for (size_t j = i + 1; j < nodes.size() && g.size() < 4; j++) {
+            ggml_tensor *m = nodes[j];
+            if (!op_is(m, "MUL_MAT") || skip.count(m) || taken.count(m) || m->src[1] != x || is_host(m) != host)
+                continue;
+            bool safe = true;
+            for (size_t k = i + 1; k < j && safe; k++) {
+                const ggml_tensor *p = nodes[k];
+                if (std::find(g.begin(), g.end(), p) != g.end()) continue;
+                safe = !overlaps(p, m);
+                for (int s = 0; s < GGML_MAX_SRC && safe; s++) safe = !overlaps(p->src[s], m);
+            }
+            for (const ggml_tensor *o : g) safe = safe && !overlaps(o, m) && !overlaps(x, m);
+            if (safe) g.push_back(m);
+        }
+        if (g.size() > 1) {
+            for (ggml_tensor *m : g) taken[m] = true;
+            out.push_back(std::move(g));
+        }
+    }
+    return out;
+}
+
+// One group of MUL_MATs sharing an input (find_groups).
+bool mul_mat_group(context &ctx, const std::vector<ggml_tensor *> &g, std::string &err) {
+    std::vector<zest_wkey> keys;
+    std::vector<float *> ys;
+    for (const ggml_tensor *m : g) {
+        const ggml_tensor *w = m->src[0];
+        if (!ensure_weight(ctx, w, err)) return false;
+        keys.push_back({ w->buffer, w->data, (int) w->type, w->ne[0], w->ne[1] });
+        ys.push_back((float *) m->data);
+    }
+    const ggml_tensor *x = g[0]->src[1];
+    ctx.matmuls += (int64_t) g.size();
+    ctx.grouped += (int64_t) g.size() - 1;
+    if (zest_mul_mat_group(ctx.npu, (int) g.size(), keys.data(), nullptr, (const float *) x->data, x->ne[1],
+                           ys.data(), is_host(x) ? 0 : 1)) {
+        err = std::string(g[0]->name) + ": " + zest_last_error();
+        return false;
+    }
+    return true;
+}
+
 // A tensor's bytes on the device: in place, or a staged copy of a
 // host-memory tensor (a graph input such as the rotary positions).
 const void *device_in(context &ctx, const ggml_tensor *t, cudaStream_t st) {
@@ -747,6 +820,15 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
         if (f.up) fused_skip[f.up] = true;
         fused_skip[f.glu] = true;
     }
+    std::unordered_map<const ggml_tensor *, bool> unfused;
+    for (const auto &kv : fused_gate) unfused[kv.first] = true;
+    for (const auto &kv : fused_skip) unfused[kv.first] = true;
+    const auto groups = groups_on() ? find_groups(nodes, unfused) : std::vector<std::vector<ggml_tensor *>>();
+    std::unordered_map<const ggml_tensor *, const std::vector<ggml_tensor *> *> group_first;
+    for (const auto &g : groups) {
+        group_first[g[0]] = &g;
+        for (size_t j = 1; j < g.size(); j++) fused_skip[g[j]] = true;
+    }
     cudaStream_t st = (cudaStream_t) zest_stream(ctx.npu);
     for (ggml_tensor *node : nodes) {
         if (status != GGML_STATUS_SUCCESS) break;
@@ -768,6 +850,8 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
             }
             ctx.matmuls += f.up ? 2 : 1;
             ctx.fused++;
+        } else if (auto gi = group_first.find(node); gi != group_first.end()) {
+            ok = mul_mat_group(ctx, *gi->second, err);
         } else if (op_is(node, "MUL_MAT")) {
             ok = mul_mat(ctx, node, err);
         } else {
@@ -789,12 +873,12 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
         zest_times t = {};
         zest_take_times(ctx.npu, &t);
         fprintf(stderr,
-                "xdna times, %lld matmuls in %lld pieces: all %.1f ms | copies %.1f, encode %.1f, GEMM %.1f "
-                "(%d calls), weight copies %.1f ms\n",
-                (long long) ctx.matmuls, (long long) ctx.pieces, ctx.compute_ms, t.copy_ms, t.encode_ms, t.gemm_ms,
-                t.calls, ctx.copy_ms);
+                "xdna times, %lld matmuls (%lld grouped, %lld fused) in %lld pieces: all %.1f ms | copies %.1f, "
+                "encode %.1f, GEMM %.1f (%d calls), weight copies %.1f ms\n",
+                (long long) ctx.matmuls, (long long) ctx.grouped, (long long) ctx.fused, (long long) ctx.pieces,
+                ctx.compute_ms, t.copy_ms, t.encode_ms, t.gemm_ms, t.calls, ctx.copy_ms);
         ctx.compute_ms = ctx.copy_ms = 0;
-        ctx.matmuls = ctx.pieces = 0;
+        ctx.matmuls = ctx.pieces = ctx.grouped = ctx.fused = 0;
     }
     return status;
 }
@@ -979,6 +1063,19 @@ ggml_backend_reg_t ggml_backend_xdna_reg(void) {
 }
 
 int ggml_zest_policy_supports(const ggml_tensor *op) { return op && policy(op) ? 1 : 0; }
+
+int ggml_zest_piece_groups(ggml_cgraph *cgraph, int *sizes, int max_groups) {
+    std::vector<ggml_tensor *> nodes;
+    const int n = ggml_graph_n_nodes(cgraph);
+    for (int i = 0; i < n; i++) {
+        ggml_tensor *node = ggml_graph_node(cgraph, i);
+        if (!op_is(node, "NONE")) nodes.push_back(node);
+    }
+    const std::unordered_map<const ggml_tensor *, bool> none;
+    const auto groups = find_groups(nodes, none);
+    for (int i = 0; i < (int) groups.size() && i < max_groups; i++) sizes[i] = (int) groups[i].size();
+    return (int) groups.size();
+}
 
 int ggml_zest_piece_fusions(ggml_cgraph *cgraph) {
     std::vector<ggml_tensor *> nodes;

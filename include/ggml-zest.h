@@ -38,6 +38,14 @@ __attribute__((visibility("default"))) int ggml_zest_policy_supports(const struc
 struct ggml_cgraph;
 __attribute__((visibility("default"))) int ggml_zest_piece_fusions(struct ggml_cgraph *cgraph);
 
+/* The MUL_MATs of this piece that graph_compute would run as grouped calls
+ * (one activation pack and one launch per input shared by 2 to 4 matmuls,
+ * the counterpart of submitting a piece's matmuls as one runlist,
+ * src/xdna-npu.cpp:476-531): returns the number of groups and writes each
+ * one's size to sizes[0 .. max_groups). Host logic only; for tests. */
+__attribute__((visibility("default"))) int ggml_zest_piece_groups(struct ggml_cgraph *cgraph, int *sizes,
+                                                                  int max_groups);
+
 #ifdef __cplusplus
 }
 #endif

@@ -98,6 +98,7 @@ class Harness:
         self.plugin.ggml_backend_score.restype = _int
         self.plugin.ggml_zest_policy_supports.argtypes = [ctypes.POINTER(Tensor)]
         self.plugin.ggml_zest_piece_fusions.argtypes = [_vp]
+        self.plugin.ggml_zest_piece_groups.argtypes = [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
         # ctypes objects the C side points at, kept for the whole process: the
         # plugin remembers who read each tensor by address (as the reference
         # does), and a freed tensor's address reused by a later test's tensor
@@ -108,6 +109,13 @@ class Harness:
         arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])
         self.keep.append(arr)
         return self.plugin.ggml_zest_piece_fusions(self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp)))
+
+    def piece_groups(self, nodes: list[Tensor]) -> list[int]:
+        arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])
+        self.keep.append(arr)
+        sizes = (ctypes.c_int * 16)()
+        n = self.plugin.ggml_zest_piece_groups(self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp)), sizes, 16)
+        return list(sizes[:n])
 
     # --- registry / device / backend ------------------------------------------
     def reg(self):

@@ -204,3 +204,31 @@ def test_min_batch_env():
     env = dict(os.environ, GGML_XDNA_MIN_BATCH="")  # empty means unset: the default 1024
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
     assert "NOT" in out.stdout, out.stderr
+
+
+def test_matmul_groups(h):
+    # MUL_MATs on one input run as one grouped call at the first one's turn,
+    # when no node in between touches a later one's output bytes
+    k, t = 1024, 1024
+    C, W = h.buffer(USAGE_COMPUTE), h.buffer(USAGE_WEIGHTS)
+    base = 0x7f0000000000
+    addr = iter(range(base, base + (64 << 30), 1 << 30))  # 1 GiB apart: no overlaps unless asked
+
+    def piece(alias=False, host_out=False, n_extra=0):
+        x = h.tensor(F32, [k, t], "x", C, next(addr))
+        q = h.mul_mat(h.tensor(Q4_K, [k, 2048], "wq", W, next(addr)), x, "q", C, next(addr))
+        qn = h.rms_norm(q, name="q_norm", buffer=C, data=next(addr))
+        qs = h.scale(qn, 0.5, name="q_scaled", buffer=C, data=next(addr))
+        k_data = qn.data if alias else next(addr)  # the allocator lent q_norm's bytes to k's output
+        kk = h.mul_mat(h.tensor(Q4_K, [k, 512], "wk", W, next(addr)), x, "k", h.buffer(USAGE_COMPUTE, host=True)
+                       if host_out else C, k_data)
+        v = h.mul_mat(h.tensor(Q4_K, [k, 512], "wv", W, next(addr)), x, "v", C, next(addr))
+        extra = [h.mul_mat(h.tensor(Q4_K, [k, 256], "we", W, next(addr)), x, "e", C, next(addr))
+                 for _ in range(n_extra)]
+        other = h.mul_mat(h.tensor(Q4_K, [k, 256], "wo", W, next(addr)), qs, "o", C, next(addr))
+        return h.piece_groups([q, qn, qs, kk, v, *extra, other])
+
+    assert piece() == [3], "q, k and v on the same input"
+    assert piece(alias=True) == [2], "k's bytes are q_norm's, live between q and k: k runs at its own turn"
+    assert piece(host_out=True) == [2], "an output in host memory with the input on the device"
+    assert piece(n_extra=2) == [4], "at most 4 to a group"

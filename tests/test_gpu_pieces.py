@@ -136,3 +136,60 @@ def test_attention_input_piece_with_rope(h):
     want = O.rope(qmv, HD, 2, O.rope_table(pos, HD, 0, par))
     assert O.nrmse(r_out.cpu().numpy(), want) <= 1e-5
     h.backend_free(b)
+
+
+@pytest.mark.parametrize("host", [False, True])
+def test_qkv_piece_grouped(h, host):
+    # q, k and v on one input run as one grouped call at q's turn, with q's
+    # per-head norm between them in the node order; inputs and outputs in
+    # device memory, or all in host memory (chunked copies)
+    K, T = 1024, 1100
+    HD, HQ, HK = 128, 8, 2
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal((T, K)) * 1.5).astype(np.float32)
+    raws = {n: O.quantize(Q4_K, O.weights_f32(rows, K, 10 + i))
+            for i, (n, rows) in enumerate([("q", HQ * HD), ("k", HK * HD), ("v", HK * HD)])}
+    B = Buffers(h)
+    W = h.buffer(USAGE_WEIGHTS)
+    C = h.buffer(USAGE_COMPUTE, host=host)
+    keep = []
+
+    def buf(*shape, src=None):
+        if host:
+            a = np.full(shape, np.nan, np.float32) if src is None else np.ascontiguousarray(src)
+            keep.append(a)
+            return a.ctypes.data, a
+        t = B.out(*shape) if src is None else torch.from_numpy(np.ascontiguousarray(src)).cuda()
+        keep.append(t)
+        return t.data_ptr(), t
+
+    xp, _ = buf(T, K, src=x)
+    xt = h.tensor(F32, [K, T], "x", C, xp)
+    outs, nodes = {}, []
+    wts = {n: h.tensor(Q4_K, [K, r.size // (K // 256 * 144)], f"blk.0.attn_{n}.weight", W, B.dev(r))
+           for n, r in raws.items()}
+    qp, outs["q"] = buf(T, HQ * HD)
+    q = h.mul_mat(wts["q"], xt, "q", C, qp)
+    q3 = h.tensor(F32, [HD, HQ, T], "q3", C, qp, op="RESHAPE", src=(q,), view_src=q)
+    qnp, qn_out = buf(T, HQ, HD)
+    qn = h.rms_norm(q3, name="q_norm", buffer=C, data=qnp)
+    kp, outs["k"] = buf(T, HK * HD)
+    kk = h.mul_mat(wts["k"], xt, "k", C, kp)
+    vp, outs["v"] = buf(T, HK * HD)
+    v = h.mul_mat(wts["v"], xt, "v", C, vp)
+    nodes = [q, q3, qn, kk, v]
+    assert h.piece_groups(nodes) == [3]
+    for nd in nodes:
+        h.supports_op(nd)
+    b, _ = h.init_backend()
+    torch.cuda.synchronize()
+    assert h.graph_compute(b, nodes) == STATUS_SUCCESS
+    torch.cuda.synchronize()
+    for n, r in raws.items():
+        rows = r.size // (K // 256 * 144)
+        got = outs[n] if host else outs[n].cpu().numpy()
+        assert O.nrmse(got, mm_bf16(O.dequant(Q4_K, r, rows, K), x)) <= 1e-3, n
+    qv = outs["q"] if host else outs["q"].cpu().numpy()
+    qnv = qn_out if host else qn_out.cpu().numpy()
+    assert O.nrmse(qnv.reshape(T * HQ, HD), O.rms_norm(qv.reshape(T * HQ, HD), HD, 1e-6)) <= 1e-5
+    h.backend_free(b)
