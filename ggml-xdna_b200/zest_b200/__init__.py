@@ -19,6 +19,8 @@ BACKEND_PATH = PKG_DIR / "libggml-zest.so"
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_IQ3_S = 0, 1, 8, 12, 14, 21
 MODE_F32, MODE_BF16, MODE_SWIGLU = 0, 1, 2
 ERR_NOT_FINITE, ERR_TIMEOUT = 1, 2
+GLU_REGLU, GLU_GEGLU, GLU_SWIGLU, GLU_GEGLU_ERF, GLU_GEGLU_QUICK = 0, 1, 2, 4, 5
+ROPE_NORMAL, ROPE_NEOX = 0, 2
 BLOCK_BYTES = 9
 # (values per quant block, bytes per quant block)
 QUANT = {TYPE_F32: (1, 4), TYPE_F16: (1, 2), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144),
