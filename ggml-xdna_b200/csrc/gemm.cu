@@ -10,16 +10,32 @@
 // raises a device flag on any NaN/Inf result (all_finite,
 // src/xdna-npu.cpp:59-67).
 //
-// Shape: a persistent kernel, one CTA per SM, 192 threads:
-//   warp 0      TMA producer: 128x64 A and 256x64 B bf16 tiles, 128-byte
-//               swizzle, into a 4-stage shared-memory ring
-//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
-//               (M=128, N=256, K=16 per instruction, fp32 in TMEM)
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, mode, store
-// Two 256-column accumulators (all 512 TMEM columns) let the epilogue of
-// one tile overlap the MMAs of the next. Every wait is bounded; on timeout
-// the kernel raises ERR_TIMEOUT, drains its own copies and MMAs, frees TMEM
-// and returns.
+// Two kernels, both persistent (one CTA, or one CTA pair, per SM) and warp-
+// specialised:
+//
+// gemm_bf16_tc_pair_kernel<BN_T> (the default; M > 128): a cluster of two
+// CTAs on one 256 x BN_T output tile with cta_group::2 MMAs (M=256 split
+// 128 + 128 across the pair, N=BN_T, K=16 per instruction). 192 threads:
+//   warp 0      TMA producer: this CTA's 128x64 A half and BN_T/2 x 64 B half,
+//               128-byte swizzle, into a shared-memory ring (stages sized to
+//               fill ~192 KB), completing on the leader CTA's barrier
+//   warp 1      TMEM allocator (cta_group::2) and, in the leader, the single-
+//               thread MMA issuer; its commits multicast to both CTAs
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, the output mode,
+//               then a double-buffered, swizzled 32x32 staging tile per warp
+//               stored by TMA (direct stores where TMA cannot: misaligned
+//               output rows)
+// The tile loop walks up to 4 weights sharing A (q, k, v; gate, up) as one
+// space of N tiles: a grouped launch is one kernel, no tails between them.
+//
+// gemm_bf16_tc_kernel (M <= 128, and ZEST_GEMM_PAIR=0): one CTA on a 128x256
+// tile, 192 threads: warp 0 TMA, warp 1 TMEM + MMA (M=128, N=256), warps 2-5
+// epilogue with direct stores.
+//
+// Two 256-column accumulators (all 512 TMEM columns) let the epilogue of one
+// tile overlap the MMAs of the next. Every wait is bounded; on timeout the
+// kernel raises ERR_TIMEOUT, drains its own copies and MMAs, frees TMEM and
+// returns. No TMA load uses cluster multicast: each CTA loads its own halves.
 #include "zest_device.cuh"
 #include "zest_internal.h"
 
