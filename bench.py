@@ -601,6 +601,8 @@ class Prefill:
         self.q, self.k, self.v = f32(Tm, hq * hd), f32(Tm, hk * hd), f32(Tm, hk * hd)
         self.qn, self.kn, self.qr, self.kr = f32(Tm, hq * hd), f32(Tm, hk * hd), f32(Tm, hq * hd), f32(Tm, hk * hd)
         self.att, self.o_out, self.s, self.d_out = f32(Tm, hq * hd), f32(Tm, H), f32(Tm, F), f32(Tm, H)
+        self.q16 = torch.empty((Tm, hq * hd), dtype=torch.bfloat16, device="cuda")
+        self.fused = True
         self.a_h = {K: torch.empty((mp, K), dtype=torch.int16, device="cuda") for K in (H, hq * hd, F)}
         self.kc = torch.empty((nL, P, hk, hd), dtype=torch.bfloat16, device="cuda")
         self.vc = torch.empty((nL, P, hk, hd), dtype=torch.bfloat16, device="cuda")
@@ -675,9 +677,30 @@ class Prefill:
             self.graphs[ci] = g
         torch.cuda.synchronize()
 
+    def _segs(self, K, T, items, ev):
+        """One zest_gemm_segs launch: items = [(weight, N, mode, c, residual, a_next)]."""
+        Z, p = self.Z, self._p
+        n = len(items)
+        arr = (Z.GemmSeg * n)(*[Z.GemmSeg(b.data_ptr(), K, N, mode, c.data_ptr() if c is not None else None,
+                                          c.shape[1] if c is not None else 0,
+                                          r.data_ptr() if r is not None else None, r.shape[1] if r is not None else 0,
+                                          a.data_ptr() if a is not None else None, a.shape[1] if a is not None else 0)
+                                for b, N, mode, c, r, a in items])
+        if ev is not None:
+            ev[0].record()
+        self._ok(self.L.zest_gemm_segs(p(self.a_h[K]), K, T, K, n, arr, p(self.err), self._sp()))
+        if ev is not None:
+            ev[1].record()
+
     def claimed_chunk(self, p0, T, evs=None, att_ev=None):
         """Every op of a claimed chunk through the C ABI (attention aside);
-        the chunk's hidden state ends in self.x[:T]."""
+        the chunk's hidden state ends in self.x[:T]. With self.fused the
+        block executor's ops ride in the kernels beside them (the norm in
+        the pack, q/k norm with rope, the residual ADDs in the GEMM epilogue,
+        SwiGLU writing the down projection's operand): 8 launches of ours a
+        layer instead of 20."""
+        if self.fused:
+            return self._claimed_chunk_fused(p0, T, evs, att_ev)
         torch, Z, L, p, sp = self.torch, self.Z, self.L, self._p, self._sp()
         nL, H, hq, hk, hd, F = self.dims
         B = Z.MODE_BF16
@@ -712,7 +735,39 @@ class Prefill:
             self._ok(L.zest_add(p(x), p(self.d_out), 0, T, H, p(x), sp))
         return x[:T]
 
-    LAUNCHES_PER_LAYER = 20  # our kernels per layer of a claimed chunk
+    LAUNCHES_PER_LAYER = 20  # our kernels per layer of a claimed chunk, unfused
+    LAUNCHES_PER_LAYER_FUSED = 8
+
+    def _claimed_chunk_fused(self, p0, T, evs, att_ev):
+        torch, Z, L, p, sp = self.torch, self.Z, self.L, self._p, self._sp()
+        nL, H, hq, hk, hd, F = self.dims
+        B, eps, mp = Z.MODE_BF16, ctypes.c_float(self.c["eps"]), Z.pad_to(T, 128)
+        x = self.x
+        x[:T] = self.emb[self.ids[p0:p0 + T]].float()
+        self._ok(L.zest_rope_table(p(self.pos[p0:]), T, hd, self.c["n_ctx_orig"], self.par, None, p(self.table), sp))
+        for li, d in enumerate(self.layers):
+            ev = evs[li] if evs is not None else [None] * 4
+            self._ok(L.zest_pack_rms_norm(p(x), T, H, H, eps, p(d["attn_norm"]), None, 0, mp, p(self.a_h[H]), H, sp))
+            self._segs(H, T, [(d["q"], hq * hd, B, self.q, None, None), (d["k"], hk * hd, B, self.k, None, None),
+                              (d["v"], hk * hd, B, self.v, None, None)], ev[0])
+            kc = self.kc[li, p0:p0 + T]
+            self._ok(L.zest_norm_rope(p(self.q), T, hq, hd, eps, p(d["q_norm"]), hd, Z.ROPE_NEOX, p(self.table),
+                                      None, p(self.q16), sp))
+            self._ok(L.zest_norm_rope(p(self.k), T, hk, hd, eps, p(d["k_norm"]), hd, Z.ROPE_NEOX, p(self.table),
+                                      None, p(kc), sp))
+            self.vc[li, p0:p0 + T] = self.v[:T].view(T, hk, hd)
+            if att_ev is not None:
+                att_ev[li][0].record()
+            self.att[:T] = self._attend(self.q16[:T].view(T, hq, hd), self.kc[li, :p0 + T],
+                                        self.vc[li, :p0 + T]).reshape(T, hq * hd)
+            if att_ev is not None:
+                att_ev[li][1].record()
+            self._pack(self.att, T, hq * hd)
+            self._segs(hq * hd, T, [(d["o"], H, B, x, x, None)], ev[1])
+            self._ok(L.zest_pack_rms_norm(p(x), T, H, H, eps, p(d["ffn_norm"]), None, 0, mp, p(self.a_h[H]), H, sp))
+            self._segs(H, T, [(d["gate_up"], d["gate_up"].shape[0], Z.MODE_SWIGLU, None, None, self.a_h[F])], ev[2])
+            self._segs(F, T, [(d["down"], H, B, x, x, None)], ev[3])
+        return x[:T]
 
     def unclaimed_chunk(self, p0, T):
         """A chunk below the gate's batch floor, as the sibling backend runs
@@ -874,6 +929,8 @@ def run_model(args, w: dict) -> None:
                                   "into every layer's own device copy",
                        "attention": "torch SDPA with a causal_lower_right bias, grouped kv heads (outside the path)",
                        "graphs": "each claimed chunk replayed from its CUDA graph",
+                       "fused": "norm in the pack, q/k norm with rope, residual ADDs and SwiGLU's packed output in "
+                                "the GEMM epilogues" if m.fused else "every op its own kernel",
                        "unclaimed": f"the {m.chunks[-1][1]}-token tail (< {c['min_batch']} tokens) in torch ops",
                        "parallelism": f"tokens{world} (each GPU its own prompt, no collective)" if world > 1
                        else "1 GPU",
@@ -900,7 +957,8 @@ def run_model(args, w: dict) -> None:
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": P * 8 * world,
                     "d2h_bytes_per_step": c["vocab"] * 4 * world,
                     "api": "token ids in, last-token logits out; claimed ops through include/zest_b200.h"},
-            "gpu_launches": steps * len(claimed) * (1 + nL * Prefill.LAUNCHES_PER_LAYER),
+            "gpu_launches": steps * len(claimed) * (1 + nL * (Prefill.LAUNCHES_PER_LAYER_FUSED if m.fused
+                                                              else Prefill.LAUNCHES_PER_LAYER)),
             "steps_note": f"{steps} timed prefills of {P} tokens (--steps capped at 20 for this workload)",
             "clocks": clocks.summary(),
         }

@@ -535,6 +535,21 @@ int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x,
     return zest_mul_mat_group(npu, 1, key, &fused, x, T, ys, on_device);
 }
 
+int zest_gemm_segs(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int n, const zest_gemm_seg *segs,
+                   unsigned *err, void *stream) {
+    if (n <= 0 || n > 4 || !segs) return set_error("zest_gemm_segs: 1 to 4 weights");
+    gemm_seg g[4];
+    for (int i = 0; i < n; i++) {
+        const zest_gemm_seg &z = segs[i];
+        g[i] = { z.b, z.ldb, z.N, z.ldc, 0, z.mode, z.c };
+        g[i].resid = z.residual;
+        g[i].ldr = z.ldr;
+        g[i].a_next = z.a_next;
+        g[i].lda_next = z.lda_next;
+    }
+    return launch_gemm_group(a_bf16, lda, M, K, n, g, err, (cudaStream_t) stream);
+}
+
 int zest_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int n, const uint16_t *const *b_bf16,
                     const int64_t *ldb, const int64_t *N, const int *mode, float *const *c, const int64_t *ldc,
                     unsigned *err, void *stream) {

@@ -70,6 +70,10 @@ struct gemm_params {
     unsigned *err;
     int mode, num_m, num_n, num_k;
     int tma_store;  // pair kernel: the epilogue stores through shared memory with TMA
+    const float *resid;  // c = resid + result (fp32 and bf16 modes), or null
+    int64_t ldr;
+    uint16_t *a_next;    // SwiGLU: the result's bfp16-rounded bf16 copy, the next GEMM's A, or null
+    int64_t lda_next;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
@@ -92,6 +96,27 @@ __device__ __forceinline__ uint32_t not_finite(float v) {
     return (__float_as_uint(v) & 0x7f800000u) == 0x7f800000u;
 }
 
+// o[i] = resid[row][col0 + i] + o[i] for the columns the output holds (the
+// ADD that follows o and down in a layer, fused: an f32 add of the same
+// operands as the separate op).
+__device__ __forceinline__ void add_residual(const gemm_params &p, float (&o)[32], int64_t row, int64_t col0) {
+    const float *src = p.resid + row * p.ldr + col0;
+    if (col0 + 32 <= p.n_out && (p.ldr % 4) == 0 && ((uintptr_t) p.resid & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const float4 q = *reinterpret_cast<const float4 *>(src + i);
+            o[i] = __fadd_rn(q.x, o[i]);
+            o[i + 1] = __fadd_rn(q.y, o[i + 1]);
+            o[i + 2] = __fadd_rn(q.z, o[i + 2]);
+            o[i + 3] = __fadd_rn(q.w, o[i + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (col0 + i < p.n_out) o[i] = __fadd_rn(src[i], o[i]);
+    }
+}
+
 // Writes one thread's 32 accumulator columns [col0, col0+32) of row `row`.
 __device__ __forceinline__ uint32_t store_chunk(const gemm_params &p, const uint32_t (&r)[32], int64_t row,
                                                 int64_t col0) {
@@ -109,6 +134,26 @@ __device__ __forceinline__ uint32_t store_chunk(const gemm_params &p, const uint
                 o[h * 8 + i] = bf16_round((g * u) * s);
             }
         const int64_t oc0 = col0 / 2;
+        if (p.a_next) {
+            // two aligned 8-value blocks (oc0 is a multiple of 16), encoded
+            // as K2 encodes the f32 values a separate pack would read
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                if (oc0 + h * 8 + 8 > p.n_out) break;
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    v[i] = o[h * 8 + i];
+                    bad |= not_finite(v[i]);
+                }
+                uint8_t enc[9];
+                uint32_t bf[4];
+                encode_block(v, enc, bf);
+                *reinterpret_cast<uint4 *>(p.a_next + row * p.lda_next + oc0 + h * 8) =
+                    make_uint4(bf[0], bf[1], bf[2], bf[3]);
+            }
+        }
+        if (!p.c) return bad;
         float *dst = p.c + row * p.ldc + oc0;
         if (oc0 + 16 <= p.n_out && (p.ldc % 4) == 0) {
 #pragma unroll
@@ -132,6 +177,7 @@ __device__ __forceinline__ uint32_t store_chunk(const gemm_params &p, const uint
         const float v = __uint_as_float(r[i]);
         o[i] = p.mode == MODE_BF16 ? bf16_round(v) : v;
     }
+    if (p.resid) add_residual(p, o, row, col0);
     float *dst = p.c + row * p.ldc + col0;
     if (col0 + 32 <= p.n_out && (p.ldc % 4) == 0) {
 #pragma unroll
@@ -546,8 +592,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int i = 0; i < 32; i++) {
                     const float v = __uint_as_float(r[i]);
                     o[i] = p.mode == MODE_BF16 ? bf16_round(v) : v;
-                    if (row < p.M && col0 + i < p.n_out) bad |= not_finite(o[i]);
                 }
+                if (p.resid && row < p.M) add_residual(p, o, row, col0);
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (row < p.M && col0 + i < p.n_out) bad |= not_finite(o[i]);
 #pragma unroll
                 for (int j = 0; j < 8; j++)
                     *reinterpret_cast<float4 *>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
@@ -670,8 +719,12 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
         p.c = g.c;
         p.err = err_flag;
         p.mode = g.mode;
+        p.resid = g.resid;
+        p.ldr = g.ldr;
+        p.a_next = g.a_next;
+        p.lda_next = g.lda_next;
         // TMA stores need 16-byte aligned rows; SwiGLU halves the width and keeps direct stores
-        p.tma_store = g.mode != MODE_SWIGLU && g.ldc % 4 == 0 && ((uintptr_t) g.c & 15) == 0 &&
+        p.tma_store = g.mode != MODE_SWIGLU && g.c && g.ldc % 4 == 0 && ((uintptr_t) g.c & 15) == 0 &&
                       make_tmap_out(&maps.c[s], g.c, M, g.n_out, g.ldc);
         pp.tile0[s] = tiles_n;
         tiles_n += (int) ((g.N + BN_T - 1) / BN_T);
@@ -717,6 +770,10 @@ int launch_single(const CUtensorMap &ta, int64_t M, int64_t K, const gemm_seg &g
     p.c = g.c;
     p.err = err_flag;
     p.mode = g.mode;
+    p.resid = g.resid;
+    p.ldr = g.ldr;
+    p.a_next = g.a_next;
+    p.lda_next = g.lda_next;
     p.num_m = (int) ((M + BM - 1) / BM);
     p.num_n = (int) ((g.N + BN - 1) / BN);
     p.num_k = (int) ((K + BK - 1) / BK);
@@ -750,7 +807,13 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
             return set_error("gemm: bad output mode");
         const int64_t width = g.mode == MODE_SWIGLU ? g.N / 2 : g.N;
         if (g.n_out <= 0 || g.n_out > width) g.n_out = width;
-        if (g.ldc < g.n_out) return set_error("gemm: ldc smaller than the output width");
+        if (!g.c && !g.a_next) return set_error("gemm: no output");
+        if (g.c && g.ldc < g.n_out) return set_error("gemm: ldc smaller than the output width");
+        if (g.resid && (g.mode == MODE_SWIGLU || !g.c || g.ldr < g.n_out))
+            return set_error("gemm: a residual needs an fp32 or bf16 output of its width");
+        if (g.a_next && (g.mode != MODE_SWIGLU || g.n_out % 8 || g.lda_next < g.n_out || g.lda_next % 8 ||
+                         ((uintptr_t) g.a_next & 15)))
+            return set_error("gemm: the next operand needs SwiGLU, a width of 8s and 16-byte aligned rows");
     }
     // The CTA-pair kernel unless ZEST_GEMM_PAIR=0 or the rows fit one 128-row tile.
     const char *pair_env = getenv("ZEST_GEMM_PAIR");

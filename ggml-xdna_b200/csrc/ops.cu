@@ -6,6 +6,7 @@
 // Arithmetic follows the reference's float expressions; transcendental
 // functions are CUDA's accurate ones (no fast-math intrinsics).
 #include "zest_b200.h"
+#include "zest_device.cuh"
 #include "zest_internal.h"
 
 #include <cmath>
@@ -24,22 +25,8 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, int64_t rows, int64
     __shared__ float part[32];
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         const float *xr = x + r * d;
-        float ss = 0.0f;
-        for (int64_t j = threadIdx.x; j < d; j += blockDim.x) ss += xr[j] * xr[j];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
-        __syncthreads();
-        if (threadIdx.x < 32) {
-            float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0f;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (threadIdx.x == 0) part[0] = v;
-        }
-        __syncthreads();
-        const float sc = 1.0f / sqrtf(part[0] / (float) d + eps);
-        for (int64_t j = threadIdx.x; j < d; j += blockDim.x) y[r * d + j] = xr[j] * sc;
-        __syncthreads();
+        const float sc = 1.0f / sqrtf(block_sumsq(xr, d, part) / (float) d + eps);
+        for (int64_t j = threadIdx.x; j < d; j += blockDim.x) y[r * d + j] = __fmul_rn(xr[j], sc);
     }
 }
 
@@ -48,9 +35,9 @@ template <int OP>  // 0 mul row, 1 add same shape, 2 add bias row
 __global__ void binary_kernel(const float *__restrict__ x, const float *__restrict__ b, int64_t n, int64_t d,
                               float *__restrict__ y) {
     for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x) {
-        if (OP == 0) y[i] = x[i] * b[i % d];
-        else if (OP == 1) y[i] = x[i] + b[i];
-        else y[i] = x[i] + b[i % d];
+        if (OP == 0) y[i] = __fmul_rn(x[i], b[i % d]);
+        else if (OP == 1) y[i] = __fadd_rn(x[i], b[i]);
+        else y[i] = __fadd_rn(x[i], b[i % d]);
     }
 }
 
@@ -120,8 +107,8 @@ __global__ void rope_kernel(const float *__restrict__ x, int64_t T, int64_t head
             const int64_t ic = neox ? q : 2 * q;
             const float c = table[t * n_dims + 2 * q], s = table[t * n_dims + 2 * q + 1];
             const float x0 = src[ic], x1 = src[ic + off_n];
-            dst[ic] = x0 * c - x1 * s;
-            dst[ic + off_n] = x0 * s + x1 * c;
+            dst[ic] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+            dst[ic + off_n] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
         } else {
             const int64_t j = n_dims + (2 * q - n_dims);
             if (j < d) dst[j] = src[j];

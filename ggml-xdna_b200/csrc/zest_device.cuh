@@ -26,6 +26,40 @@ enum : unsigned {
 __device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 
+// A row's sum of squares over a block of threads, in a fixed order: each
+// thread a strided partial of fused multiply-adds, then an xor tree within
+// each warp and another over the warps' partials (part: 32 floats of shared
+// memory). RMS_NORM and the kernels that fuse it share this, so they agree
+// bit for bit. Every thread of the block must call it.
+__device__ __forceinline__ float block_sumsq(const float *__restrict__ xr, int64_t d, float *part) {
+    float ss = 0.0f;
+    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) ss = __fmaf_rn(xr[j], xr[j], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float v = 0.0f;
+    if (threadIdx.x < 32) {
+        v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) part[0] = v;
+    __syncthreads();
+    v = part[0];
+    __syncthreads();  // part[] is free for the next row
+    return v;
+}
+
+// bf16 bits of x, rounded to nearest even (NaN stays NaN).
+__device__ __forceinline__ uint16_t bf16_bits_rne(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t) ((u | 0x00400000u) >> 16);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t) (u >> 16);
+}
+
 // One block of eight floats -> nine bytes, as bfp16_encode_block's AVX2 path
 // (bfp16_pack.cpp:85-114, compiled with -mavx2 in the reference's builds):
 //  * exponent byte = the largest biased float exponent of the eight;

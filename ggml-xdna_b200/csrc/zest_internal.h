@@ -37,12 +37,19 @@ int launch_convert_weight(int type, const void *src0, const void *src1, int fuse
                           int64_t src_rows_total, int64_t K, int64_t n_pad, uint8_t *b_bytes, uint16_t *b_bf16,
                           cudaStream_t st);
 
-// One weight of a grouped GEMM: its B operand (N rows), output and mode.
+// One weight of a grouped GEMM: its B operand (N rows), output and mode,
+// and what the epilogue fuses: a residual added to the result (the ADD
+// after o and down), or for SwiGLU the next GEMM's A operand (the bf16 copy
+// of the result's bfp16 rounding, as K2 would pack it).
 struct gemm_seg {
     const uint16_t *b;
     int64_t ldb, N, ldc, n_out;  // n_out <= 0: all (N, or N/2 for SwiGLU)
     int mode;
-    float *c;
+    float *c;                    // may be null for SwiGLU with a_next
+    const float *resid = nullptr;
+    int64_t ldr = 0;
+    uint16_t *a_next = nullptr;
+    int64_t lda_next = 0;
 };
 
 // Up to 4 weights sharing one A (q, k and v; gate and up) in one launch.

@@ -39,6 +39,12 @@ class WKey(ctypes.Structure):
     _fields_ = [("buffer", _vp), ("data", _vp), ("type", _int), ("K", _i64), ("N", _i64)]
 
 
+class GemmSeg(ctypes.Structure):
+    """zest_gemm_seg: one weight of zest_gemm_segs with its fused epilogue."""
+    _fields_ = [("b", _vp), ("ldb", _i64), ("N", _i64), ("mode", _int), ("c", _vp), ("ldc", _i64),
+                ("residual", _vp), ("ldr", _i64), ("a_next", _vp), ("lda_next", _i64)]
+
+
 class Times(ctypes.Structure):
     _fields_ = [("encode_ms", ctypes.c_double), ("gemm_ms", ctypes.c_double), ("copy_ms", ctypes.c_double),
                 ("pack_ms", ctypes.c_double), ("calls", _int)]
@@ -64,6 +70,9 @@ def lib() -> ctypes.CDLL:
         "zest_convert_gate_up": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
         "zest_gemm": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
         "zest_gemm_group": (_int, [_vp, _i64, _i64, _i64, _int, _vpp, _i64p, _i64p, _intp, _vpp, _i64p, _vp, _vp]),
+        "zest_gemm_segs": (_int, [_vp, _i64, _i64, _i64, _int, ctypes.POINTER(GemmSeg), _vp, _vp]),
+        "zest_pack_rms_norm": (_int, [_vp, _i64, _i64, _i64, ctypes.c_float, _vp, _vp, _i64, _i64, _vp, _i64, _vp]),
+        "zest_norm_rope": (_int, [_vp, _i64, _i64, _i64, ctypes.c_float, _vp, _int, _int, _vp, _vp, _vp, _vp]),
         "zest_mul_mat_noalloc": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
         "zest_rms_norm": (_int, [_vp, _i64, _i64, ctypes.c_float, _vp, _vp]),
         "zest_mul_row": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
@@ -98,9 +107,9 @@ def lib() -> ctypes.CDLL:
 def exported_symbols() -> list[str]:
     return [n for n in ("zest_version", "zest_last_error", "zest_load_iq3s_grid", "zest_pack_activations",
                         "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_gemm_group",
-                        "zest_mul_mat_noalloc",
+                        "zest_gemm_segs", "zest_mul_mat_noalloc",
                         "zest_rms_norm", "zest_mul_row", "zest_add", "zest_scale", "zest_glu", "zest_rope_table",
-                        "zest_rope",
+                        "zest_rope", "zest_pack_rms_norm", "zest_norm_rope",
                         "zest_usable", "zest_open",
                         "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
                         "zest_add_weight_values",

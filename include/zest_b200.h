@@ -113,6 +113,30 @@ int zest_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, i
                     const int64_t *ldb, const int64_t *N, const int *mode, float *const *c, const int64_t *ldc,
                     unsigned *err, void *stream);
 
+/* One weight of zest_gemm_segs, with what its epilogue fuses. */
+typedef struct {
+    const uint16_t *b;    /* the weight's bf16 copy, N rows of ldb */
+    int64_t ldb, N;
+    int mode;             /* ZEST_MODE_* */
+    float *c;             /* [M][ldc] output; may be NULL in ZEST_MODE_SWIGLU when a_next is given */
+    int64_t ldc;
+    const float *residual; /* NULL, or (fp32 and bf16 modes) c = residual + result, [M][ldr]: the ADD
+                              that follows o and down in a layer. residual may be c itself */
+    int64_t ldr;
+    uint16_t *a_next;     /* NULL, or (ZEST_MODE_SWIGLU) the result's K2 operand: the bf16 copy of
+                             its bfp16 rounding, [M][lda_next], the next GEMM's A */
+    int64_t lda_next;
+} zest_gemm_seg;
+
+/* zest_gemm_group with fused epilogues: per weight a residual ADD, or for a
+ * fused gate/up weight the down projection's packed input instead of (or
+ * besides) the f32 SwiGLU result. The same bits as the unfused ops (ADD as
+ * an f32 add of the same operands; the pack of the f32 SwiGLU values).
+ * Replaces: run_rows' ADD (src/xdna-exec.cpp:253-346) and the decode /
+ * encode passes between two NPU calls (src/xdna-exec.cpp:368-388). */
+int zest_gemm_segs(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int n, const zest_gemm_seg *segs,
+                   unsigned *err, void *stream);
+
 /* K2 + K3 without allocating anything: y[T][ldy] = x[T][K] * W^T, where w_bf16
  * is a weight's bf16 B operand (zest_convert_weight / zest_weight_bf16) of N
  * rows and the same mode and err word as zest_gemm. No counterpart in the
@@ -165,6 +189,23 @@ int zest_rope_table(const int32_t *pos, int64_t T, int n_dims, int n_ctx_orig, c
 /* x [T][heads][d] -> y, the first n_dims of each head rotated (ROPE) */
 int zest_rope(const float *x, int64_t T, int64_t heads, int64_t d, int n_dims, int mode, const float *table, float *y,
               void *stream);
+
+/* RMS_NORM of each row of x [T][ldx] (eps), times w (a row of K; NULL:
+ * none), then K2's pack: a_bf16 [m_pad][lda] receives the bf16 copy of the
+ * result's bfp16 rounding (rows past T zero), and y [T][ldy] (NULL: not
+ * written) the f32 result, as ggml's MUL tensor. The same bits as
+ * zest_rms_norm, zest_mul_row and zest_pack_activations in turn, in one pass.
+ * Replaces: run_rows' RMS_NORM and MUL (src/xdna-exec.cpp:253-346) with the
+ * encode_row of the matmul input they feed (src/xdna-npu.cpp:511-515). */
+int zest_pack_rms_norm(const float *x, int64_t T, int64_t K, int64_t ldx, float eps, const float *w, float *y,
+                       int64_t ldy, int64_t m_pad, uint16_t *a_bf16, int64_t lda, void *stream);
+/* Per-head RMS_NORM (eps) of x [T][heads][d] (d <= 256), times w (a row of
+ * d; NULL: none), then ROPE (mode, n_dims, a zest_rope_table table) into
+ * y [T][heads][d] f32 and/or y_bf16 (the bf16 rounding, nearest even); either
+ * output may be NULL. Qwen3's q/k norm and rope in one pass.
+ * Replaces: run_rows' RMS_NORM, MUL and ROPE (src/xdna-exec.cpp:253-346). */
+int zest_norm_rope(const float *x, int64_t T, int64_t heads, int64_t d, float eps, const float *w, int n_dims,
+                   int mode, const float *table, float *y, uint16_t *y_bf16, void *stream);
 
 /* ---------------------------------------------------------------------------
  * 2. The matmul service (xdna_npu)

@@ -1,0 +1,166 @@
+"""The block executor's ops fused into the kernels beside them, through the
+C ABI: RMS_NORM + MUL + K2's pack, per-head RMS_NORM + MUL + ROPE, and K3's
+epilogues (the residual ADD; SwiGLU writing the next GEMM's packed operand).
+Each is held to the bits of the same ops run one after another on the GPU,
+and, for the float ops, to the oracle's restatement of the reference's
+run_rows within the reference's small-op bar (nrmse 1e-5)."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import zest_b200 as Z
+from oracle import oracle as O
+from gpu_util import dev, host
+
+pytestmark = pytest.mark.gpu
+EXACT = 1e-5
+_alive = []
+
+
+def p(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def sp():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def call(name, *args):
+    L = Z.lib()
+    rc = getattr(L, name)(*args, sp())
+    assert rc == 0, L.zest_last_error().decode()
+
+
+def normal(shape, seed, scale=1.5):
+    return (np.random.default_rng(seed).standard_normal(shape) * scale).astype(np.float32)
+
+
+@pytest.mark.parametrize("with_w", [True, False])
+@pytest.mark.parametrize("T,K", [(1000, 2560), (2048, 4096), (37, 512)])
+def test_pack_rms_norm_equals_separate_ops(T, K, with_w):
+    x = dev(normal((T, K), T + K))
+    w = dev(np.random.default_rng(1).uniform(0.5, 1.5, K).astype(np.float32)) if with_w else None
+    m_pad = Z.pad_to(T, 128)
+    a = torch.full((m_pad, K), 0x5555, dtype=torch.int16, device="cuda")
+    y = torch.empty((T, K), device="cuda")
+    call("zest_pack_rms_norm", p(x), T, K, K, ctypes.c_float(1e-6), p(w), p(y), K, m_pad, p(a), K)
+    # the same ops one after another
+    yn = torch.empty((T, K), device="cuda")
+    call("zest_rms_norm", p(x), T, K, ctypes.c_float(1e-6), p(yn))
+    if with_w:
+        call("zest_mul_row", p(yn), p(w), T, K, p(yn))
+    _, a_ref = Z.pack_activations(yn, m_pad=m_pad, want_bytes=False)
+    torch.cuda.synchronize()
+    assert torch.equal(y, yn)
+    assert torch.equal(a, a_ref)
+    want = O.rms_norm(host(x), K, 1e-6)
+    if with_w:
+        want = O.mul_row(want, host(w))
+    assert O.nrmse(host(y), want) <= EXACT
+    # without the f32 output, the same operand
+    a2 = torch.empty_like(a)
+    call("zest_pack_rms_norm", p(x), T, K, K, ctypes.c_float(1e-6), p(w), None, 0, m_pad, p(a2), K)
+    torch.cuda.synchronize()
+    assert torch.equal(a2, a)
+
+
+@pytest.mark.parametrize("mode,n_dims", [(Z.ROPE_NEOX, 128), (Z.ROPE_NORMAL, 128), (Z.ROPE_NEOX, 64)])
+def test_norm_rope_equals_separate_ops(mode, n_dims):
+    T, H, HD = 300, 8, 128
+    x = dev(normal((T, H, HD), 3))
+    w = dev(np.random.default_rng(4).uniform(0.5, 1.5, HD).astype(np.float32))
+    pos = (5000 + 3 * np.arange(T)).astype(np.int32)
+    par = np.array([1000000.0, 1.0, 0.0, 1.0, 32.0, 1.0], np.float32)
+    table = torch.empty((T, n_dims), device="cuda")
+    posd = dev(pos)
+    L = Z.lib()
+    assert L.zest_rope_table(p(posd), T, n_dims, 40960, par.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), None,
+                             p(table), sp()) == 0
+    y = torch.empty((T, H, HD), device="cuda")
+    y16 = torch.empty((T, H, HD), dtype=torch.int16, device="cuda")
+    call("zest_norm_rope", p(x), T, H, HD, ctypes.c_float(1e-6), p(w), n_dims, mode, p(table), p(y), p(y16))
+    # separate ops
+    yn = torch.empty((T * H, HD), device="cuda")
+    call("zest_rms_norm", p(x), T * H, HD, ctypes.c_float(1e-6), p(yn))
+    call("zest_mul_row", p(yn), p(w), T * H, HD, p(yn))
+    yr = torch.empty((T, H, HD), device="cuda")
+    call("zest_rope", p(yn), T, H, HD, n_dims, mode, p(table), p(yr))
+    torch.cuda.synchronize()
+    assert O.nrmse(host(y), host(yr)) <= 1e-6  # the per-head sum runs in a warp, not a block
+    assert torch.equal(y16, y.to(torch.bfloat16).view(torch.int16))
+    want = O.rope(O.mul_row(O.rms_norm(host(x).reshape(T * H, HD), HD, 1e-6), host(w)).reshape(T, H, HD), n_dims,
+                  mode, O.rope_table(pos, n_dims, 40960, par))
+    assert O.nrmse(host(y), want) <= EXACT
+
+
+def operands(M, N, K, seed):
+    _, ah = Z.pack_activations(dev(O.activations(M, K, seed)))
+    _, bh = Z.convert_weight(O.Q8_0, dev(O.quantize(O.Q8_0, O.weights_f32(N, K, seed + 1))), N, K)
+    return ah, bh
+
+
+def segs(*items):
+    arr = (Z.GemmSeg * len(items))(*items)
+    _alive.append(arr)
+    return arr
+
+
+@pytest.mark.parametrize("M", [900, 100])  # the CTA-pair kernel and the one-CTA kernel
+@pytest.mark.parametrize("ldc_pad", [0, 1])  # TMA-stored rows, and direct stores (rows not 16-byte aligned)
+def test_gemm_residual_add(M, ldc_pad):
+    N, K = 768, 512
+    ah, bh = operands(M, N, K, 5)
+    ldc = N + ldc_pad
+    resid = dev(normal((M, ldc), 6))
+    c = torch.empty((M, ldc), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = segs(Z.GemmSeg(bh.data_ptr(), K, N, Z.MODE_BF16, c.data_ptr(), ldc, resid.data_ptr(), ldc, None, 0))
+    call("zest_gemm_segs", p(ah), K, M, K, 1, s, p(err))
+    plain = host(Z.gemm(ah, bh, M, N, Z.MODE_BF16))
+    got = host(c)[:, :N]
+    assert np.array_equal(got, host(resid)[:, :N] + plain)  # f32 add of the same operands
+    # in place: the residual stream updated where it lies (x += o)
+    x = resid.clone()
+    s = segs(Z.GemmSeg(bh.data_ptr(), K, N, Z.MODE_BF16, x.data_ptr(), ldc, x.data_ptr(), ldc, None, 0))
+    call("zest_gemm_segs", p(ah), K, M, K, 1, s, p(err))
+    assert np.array_equal(host(x)[:, :N], got)
+    assert int(err.item()) == 0
+
+
+@pytest.mark.parametrize("with_c", [True, False])
+@pytest.mark.parametrize("M", [1000, 128])
+def test_gemm_swiglu_writes_next_operand(M, with_c):
+    F, K = 600, 512
+    gr = O.quantize(O.Q4_K, O.weights_f32(F, K, 7))
+    ur = O.quantize(O.Q4_K, O.weights_f32(F, K, 8))
+    _, gu = Z.convert_gate_up(O.Q4_K, dev(gr), dev(ur), F, K)
+    _, ah = Z.pack_activations(dev(O.activations(M, K, 9)))
+    n = gu.shape[0]
+    plain = Z.gemm(ah, gu, M, n, Z.MODE_SWIGLU)  # [M][f_pad] f32
+    f_pad = n // 2
+    _, want = Z.pack_activations(plain.contiguous(), want_bytes=False)
+    a_next = torch.full((Z.pad_to(M, 128), f_pad), 0x5555, dtype=torch.int16, device="cuda")
+    c = torch.empty((M, f_pad), device="cuda") if with_c else None
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = segs(Z.GemmSeg(gu.data_ptr(), K, n, Z.MODE_SWIGLU, c.data_ptr() if with_c else None, f_pad, None, 0,
+                       a_next.data_ptr(), f_pad))
+    call("zest_gemm_segs", p(ah), K, M, K, 1, s, p(err))
+    torch.cuda.synchronize()
+    assert torch.equal(a_next[:M], want[:M])
+    if with_c:
+        assert torch.equal(c, plain)
+    assert int(err.item()) == 0
+
+
+def test_gemm_segs_rejects_bad_epilogues():
+    ah, bh = operands(256, 512, 64, 1)
+    c = torch.empty((256, 512), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L = Z.lib()
+    bad = [Z.GemmSeg(bh.data_ptr(), 64, 512, Z.MODE_SWIGLU, c.data_ptr(), 512, c.data_ptr(), 512, None, 0),
+           Z.GemmSeg(bh.data_ptr(), 64, 512, Z.MODE_F32, c.data_ptr(), 512, None, 0, c.data_ptr(), 512),
+           Z.GemmSeg(bh.data_ptr(), 64, 512, Z.MODE_F32, None, 0, None, 0, None, 0)]
+    for sg in bad:
+        assert L.zest_gemm_segs(p(ah), 64, 256, 64, 1, segs(sg), p(err), sp()) != 0
