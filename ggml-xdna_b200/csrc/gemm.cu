@@ -407,9 +407,33 @@ struct pair_params {
     gemm_params seg[MAX_SEG];  // per weight: N, n_out, ldc, c, mode, tma_store (M, K, err shared)
     int tile0[MAX_SEG + 1];    // first N tile of each segment; tile0[nseg] = all N tiles
     int nseg, num_m, num_n, num_k;
+    int raster;                // RASTER_*
     int64_t M;
     unsigned *err;
 };
+
+// The order the persistent pairs walk the tiles in. Pair p takes tiles p,
+// p + pairs, ..., so each wave is a run of consecutive tiles; the order is
+// chosen per launch so the operand every wave re-reads stays in L2:
+//   RASTER_ROWS    an M block's N tiles together: A streamed once, B (small
+//                  N x K) read from L2 by every wave
+//   RASTER_COLS    an N tile's M blocks together: B streamed once, A (small
+//                  M x K) read from L2
+//   RASTER_GROUPS  GROUP_M M blocks at a time, their N tiles within: when
+//                  neither operand fits
+enum { RASTER_GROUPS = 0, RASTER_ROWS = 1, RASTER_COLS = 2 };
+
+__device__ __forceinline__ void pair_tile_coords(int t, const pair_params &pp, int &mb, int &nb) {
+    if (pp.raster == RASTER_ROWS) {
+        mb = t / pp.num_n;
+        nb = t % pp.num_n;
+    } else if (pp.raster == RASTER_COLS) {
+        nb = t / pp.num_m;
+        mb = t % pp.num_m;
+    } else {
+        tile_coords(t, pp.num_m, pp.num_n, mb, nb);
+    }
+}
 
 template <int BN_T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -476,9 +500,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t phase = 0;
             uint32_t armed = 0, armed_phase = 0;
             bool ok = true;
+            const uint64_t pol = l2_evict_first_policy();
             for (int t = pair; t < total && ok; t += npairs) {
                 int mb, nbg, seg, nb;
-                tile_coords(t, pp.num_m, pp.num_n, mb, nbg);
+                pair_tile_coords(t, pp, mb, nbg);
                 locate(nbg, seg, nb);
                 for (int kb = 0; kb < pp.num_k; kb++) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, WAIT_LIMIT_NS)) {
@@ -489,8 +514,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
                     const uint32_t bar = map_to_rank(&full[stage], 0);
                     uint8_t *sa = smem + stage * P_STAGE_BYTES;
-                    tma_load_2d_pair(sa, &tmA, bar, kb * BK, mb * P_BM + (int) rank * 128);
-                    tma_load_2d_pair(sa + P_A_BYTES, &maps.b[seg], bar, kb * BK, nb * P_BN + (int) rank * (P_BN / 2));
+                    // the operand this raster streams is read once: evict-first
+                    if (pp.raster == RASTER_ROWS)
+                        tma_load_2d_pair_hint(sa, &tmA, bar, kb * BK, mb * P_BM + (int) rank * 128, pol);
+                    else
+                        tma_load_2d_pair(sa, &tmA, bar, kb * BK, mb * P_BM + (int) rank * 128);
+                    if (pp.raster != RASTER_ROWS)
+                        tma_load_2d_pair_hint(sa + P_A_BYTES, &maps.b[seg], bar, kb * BK,
+                                              nb * P_BN + (int) rank * (P_BN / 2), pol);
+                    else
+                        tma_load_2d_pair(sa + P_A_BYTES, &maps.b[seg], bar, kb * BK, nb * P_BN + (int) rank * (P_BN / 2));
                     armed |= 1u << stage;
                     armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == P_STAGES) {
@@ -556,9 +589,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t acc_phase = 0;
         uint32_t bad = 0;
         bool stored = false;
+        const uint64_t out_pol = l2_evict_first_policy();  // outputs are written once
         for (int t = pair; t < total; t += npairs) {
             int mb, nbg, seg, nb;
-            tile_coords(t, pp.num_m, pp.num_n, mb, nbg);
+            pair_tile_coords(t, pp, mb, nbg);
             locate(nbg, seg, nb);
             const gemm_params &p = pp.seg[seg];
             if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, WAIT_LIMIT_NS)) {
@@ -604,7 +638,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 fence_proxy_async_shared();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&maps.c[seg], buf, (int32_t) col0, (int32_t) row0);
+                    tma_store_2d_hint(&maps.c[seg], buf, (int32_t) col0, (int32_t) row0, out_pol);
                     bulk_commit_group();
                     stored = true;
                 }
@@ -731,6 +765,18 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
     }
     pp.tile0[nseg] = tiles_n;
     pp.num_n = tiles_n;
+    // keep the re-read operand within about half of the 126 MB L2 (the rest
+    // holds the streamed operand's tiles and the outputs on their way out)
+    const double l2_budget = 60e6, a_bytes = 2.0 * (double) M * (double) K;
+    double b_bytes = 0;
+    for (int s = 0; s < nseg; s++) b_bytes += 2.0 * (double) segs[s].N * (double) K;
+    pp.raster = b_bytes <= l2_budget && b_bytes <= a_bytes ? RASTER_ROWS
+                : a_bytes <= l2_budget                     ? RASTER_COLS
+                                                           : RASTER_GROUPS;
+    if (const char *force = getenv("ZEST_GEMM_RASTER")) {
+        const int f = atoi(force);
+        if (f >= RASTER_GROUPS && f <= RASTER_COLS) pp.raster = f;
+    }
     static bool attr_set = false;
     if (!attr_set) {
         if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -354,6 +354,25 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const void *tmap, ui
         : "memory");
 }
 
+// An L2 policy that marks every line a copy touches evict-first: for data
+// read or written once (the streamed operand, the outputs), so it does not
+// push the operand that every wave re-reads out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// tma_load_2d_pair with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_pair_hint(void *dst, const void *tmap, uint32_t bar_cluster_addr,
+                                                      int32_t c0, int32_t c1, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%3, %4}], [%2], %5;"
+        ::"r"(smem_u32(dst)), "l"(tmap), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                  "r"(ncols)
@@ -408,6 +427,14 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
 __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, int32_t c0, int32_t c1) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
                  "r"(smem_u32(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+// tma_store_2d with an L2 cache policy.
+__device__ __forceinline__ void tma_store_2d_hint(const void *tmap, const void *src, int32_t c0, int32_t c1,
+                                                  uint64_t policy) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;"
+                 ::"l"(tmap), "r"(smem_u32(src)), "r"(c0), "r"(c1), "l"(policy)
                  : "memory");
 }
 
