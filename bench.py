@@ -19,6 +19,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -604,8 +605,12 @@ class Prefill:
         self.q16 = torch.empty((Tm, hq * hd), dtype=torch.bfloat16, device="cuda")
         self.fused = True
         self.a_h = {K: torch.empty((mp, K), dtype=torch.int16, device="cuda") for K in (H, hq * hd, F)}
-        self.kc = torch.empty((nL, P, hk, hd), dtype=torch.bfloat16, device="cuda")
-        self.vc = torch.empty((nL, P, hk, hd), dtype=torch.bfloat16, device="cuda")
+        self.page = 64
+        Pp = Z.pad_to(P, self.page)  # the cache in 64-token pages for the paged attention kernel
+        self.kc = torch.zeros((nL, Pp, hk, hd), dtype=torch.bfloat16, device="cuda")
+        self.vc = torch.zeros((nL, Pp, hk, hd), dtype=torch.bfloat16, device="cuda")
+        self.att16 = torch.empty((Tm, hq, hd), dtype=torch.bfloat16, device="cuda")
+        self.attn_impl = self._pick_attention()
         self.table = f32(Tm, hd)
         self.pos = torch.arange(P, dtype=torch.int32, device="cuda")
         self.par = (ctypes.c_float * 6)(c["rope_base"], 1.0, 0.0, 1.0, 32.0, 1.0)
@@ -645,6 +650,58 @@ class Prefill:
         self._ok(self.L.zest_rms_norm(self._p(src), rows, d, ctypes.c_float(self.c["eps"]), self._p(dst),
                                       self._sp()))
         self._ok(self.L.zest_mul_row(self._p(dst), self._p(wt), rows, d, self._p(dst), self._sp()))
+
+    def _pick_attention(self) -> str:
+        """Attention outside the path: flashinfer's trtllm-gen paged context
+        kernel for chunks that attend over earlier ones (2-3x torch SDPA
+        there on B200), torch SDPA for a chunk on its own. Checked once
+        against SDPA; SDPA everywhere if the library is missing or differs."""
+        torch = self.torch
+        try:
+            from flashinfer.prefill import trtllm_batch_context_with_kv_cache
+            nL, H, hq, hk, hd, F = self.dims
+            Pp = self.kc.shape[1]
+            self._trt = trtllm_batch_context_with_kv_cache
+            self._ws = torch.zeros(128 << 20, dtype=torch.uint8, device="cuda")
+            self._blocks = torch.arange(Pp // self.page, dtype=torch.int32, device="cuda")[None]
+            self._meta = {}
+            for p0, T in self.chunks:
+                S = p0 + T
+                self._meta[p0] = (torch.tensor([S], dtype=torch.int32, device="cuda"),
+                                  torch.tensor([0, T], dtype=torch.int32, device="cuda"),
+                                  torch.tensor([0, S], dtype=torch.int32, device="cuda"))
+            # check on the second chunk's shape with random keys
+            p0, T = self.chunks[1] if len(self.chunks) > 1 else self.chunks[0]
+            g = torch.Generator("cuda").manual_seed(7)
+            self.kc[0, :p0 + T] = torch.randn(p0 + T, hk, hd, device="cuda", generator=g).to(torch.bfloat16)
+            self.vc[0, :p0 + T] = torch.randn(p0 + T, hk, hd, device="cuda", generator=g).to(torch.bfloat16)
+            q = torch.randn(T, hq, hd, device="cuda", generator=g).to(torch.bfloat16)
+            got = self._attend_paged(0, p0, T, q).float()
+            want = self._attend(q, self.kc[0, :p0 + T], self.vc[0, :p0 + T]).float()
+            torch.cuda.synchronize()
+            if ((got - want).abs().max() / want.abs().max()).item() > 2e-2:
+                return "torch SDPA (trtllm-gen disagreed)"
+            return "flashinfer trtllm-gen paged context attention; torch SDPA for the first chunk"
+        except Exception as e:  # the library is optional: SDPA is the stock path
+            self._trt = None
+            return f"torch SDPA ({type(e).__name__} from flashinfer)"
+
+    def _attend_paged(self, li, p0, T, q):
+        """A chunk's queries q [T, hq, hd] over layer li's cache up to the chunk's end."""
+        nL, H, hq, hk, hd, F = self.dims
+        Pp, ps = self.kc.shape[1], self.page
+        seq, cq, ckv = self._meta[p0]
+        out = self.att16[:T]
+        self._trt(q, (self.kc[li].view(Pp // ps, ps, hk, hd), self.vc[li].view(Pp // ps, ps, hk, hd)), self._ws,
+                  self._blocks, seq, T, p0 + T, 1.0 / math.sqrt(hd), 1.0, 1, cq, ckv, out=out, kv_layout="NHD",
+                  causal=True)
+        return out
+
+    def _attention(self, li, p0, T, q):
+        """Layer li's attention for a chunk (queries q [T, hq, hd] bf16)."""
+        if self._trt is not None and p0 > 0:
+            return self._attend_paged(li, p0, T, q)
+        return self._attend(q, self.kc[li, :p0 + T], self.vc[li, :p0 + T])
 
     def _attend(self, q, k, v):
         """Causal attention of a chunk's queries over the cache up to the
@@ -758,8 +815,7 @@ class Prefill:
             self.vc[li, p0:p0 + T] = self.v[:T].view(T, hk, hd)
             if att_ev is not None:
                 att_ev[li][0].record()
-            self.att[:T] = self._attend(self.q16[:T].view(T, hq, hd), self.kc[li, :p0 + T],
-                                        self.vc[li, :p0 + T]).reshape(T, hq * hd)
+            self.att[:T] = self._attention(li, p0, T, self.q16[:T].view(T, hq, hd)).reshape(T, hq * hd)
             if att_ev is not None:
                 att_ev[li][1].record()
             self._pack(self.att, T, hq * hd)
@@ -927,7 +983,7 @@ def run_model(args, w: dict) -> None:
                        "weights": f"Q4_K; Q6_K for attn_v and ffn_down on {n_six} of {nL} layers (first and last "
                                   "eighth, every third between). One seeded set of raw bytes per type, converted "
                                   "into every layer's own device copy",
-                       "attention": "torch SDPA with a causal_lower_right bias, grouped kv heads (outside the path)",
+                       "attention": m.attn_impl + " (outside the path)",
                        "graphs": "each claimed chunk replayed from its CUDA graph",
                        "fused": "norm in the pack, q/k norm with rope, residual ADDs and SwiGLU's packed output in "
                                 "the GEMM epilogues" if m.fused else "every op its own kernel",
