@@ -40,6 +40,7 @@
 #include "zest_internal.h"
 
 #include <cuda.h>
+#include <mutex>
 #include <cudaTypedefs.h>
 
 namespace zest {
@@ -408,8 +409,59 @@ struct pair_params {
     int tile0[MAX_SEG + 1];    // first N tile of each segment; tile0[nseg] = all N tiles
     int nseg, num_m, num_n, num_k;
     int raster;                // RASTER_*
+    // stream-K: tiles [0, dp_tiles) run whole, one per pair per wave; the
+    // sk_tiles after them are cut into runs of sk_q k-blocks, pair p taking
+    // [p * sk_q, (p + 1) * sk_q) of their (tile, k-block) space
+    int dp_tiles, sk_tiles;
+    int64_t sk_q;
+    int sk_epoch;  // this launch's flag value: stale flags of an abandoned launch never match
     int64_t M;
     unsigned *err;
+};
+
+// Stream-K partial sums: a CTA whose last run stops inside a tile leaves its
+// 128 rows x (at most) 256 fp32 columns here, in its own slot, and raises its
+// flag; the CTA that finishes the tile adds them in k order and clears the
+// flags. One workspace per device: launches that may use it are serialised
+// across streams by the launcher.
+constexpr int SK_SLOTS = 160;
+constexpr int SK_SLOT_FLOATS = 128 * 256;
+__device__ float g_sk_part[SK_SLOTS * SK_SLOT_FLOATS];
+__device__ int g_sk_flag[SK_SLOTS];
+
+// The runs of one pair: its whole tiles, then its stretch of the stream-K
+// space one (tile, k-block range) at a time, from the END of the stretch
+// back to its start. So a pair first computes the run that stops inside a
+// tile (whose partial sum another pair waits for) and publishes it, and only
+// then the run that finishes a tile started by the pair before it: no pair
+// waits on a pair that is itself waiting.
+struct unit_iter {
+    int i = 0;
+    int64_t u0 = 0, u1 = 0;  // the stretch still to walk, [u0, u1)
+    __device__ unit_iter(const pair_params &pp, int pair) {
+        const int64_t end = (int64_t) pp.sk_tiles * pp.num_k;
+        u0 = (int64_t) pair * pp.sk_q;
+        u1 = u0 + pp.sk_q < end ? u0 + pp.sk_q : end;
+        if (u0 > u1) u0 = u1;
+    }
+    __device__ bool next(const pair_params &pp, int pair, int npairs, int &t, int &kb0, int &kb1) {
+        const int td = pair + i * npairs;
+        if (td < pp.dp_tiles) {
+            i++;
+            t = td;
+            kb0 = 0;
+            kb1 = pp.num_k;
+            return true;
+        }
+        if (u1 <= u0) return false;
+        const int64_t st = (u1 - 1) / pp.num_k, ts = st * pp.num_k;
+        const int64_t start = u0 > ts ? u0 : ts;
+        t = pp.dp_tiles + (int) st;
+        kb0 = (int) (start - ts);
+        kb1 = (int) (u1 - ts);
+        u1 = start;
+        return true;
+    }
 };
 
 // The order the persistent pairs walk the tiles in. Pair p takes tiles p,
@@ -481,7 +533,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
     const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
-    const int total = pp.num_m * pp.num_n;  // 256-row M tiles x all segments' N tiles
 
     // global N tile -> (segment, its own N tile)
     auto locate = [&](int nbg, int &seg, int &nb) {
@@ -501,11 +552,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t armed = 0, armed_phase = 0;
             bool ok = true;
             const uint64_t pol = l2_evict_first_policy();
-            for (int t = pair; t < total && ok; t += npairs) {
+            unit_iter it(pp, pair);
+            int t, kb0, kb1;
+            while (ok && it.next(pp, pair, npairs, t, kb0, kb1)) {
                 int mb, nbg, seg, nb;
                 pair_tile_coords(t, pp, mb, nbg);
                 locate(nbg, seg, nb);
-                for (int kb = 0; kb < pp.num_k; kb++) {
+                for (int kb = kb0; kb < kb1; kb++) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, WAIT_LIMIT_NS)) {
                         fail();
                         ok = false;
@@ -547,14 +600,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
             bool ok = true;
-            for (int t = pair; t < total && ok; t += npairs) {
+            unit_iter it(pp, pair);
+            int t, kb0, kb1;
+            while (ok && it.next(pp, pair, npairs, t, kb0, kb1)) {
                 if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag, WAIT_LIMIT_NS)) {
                     fail();
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t) (acc * ACC_COLS);
-                for (int kb = 0; kb < pp.num_k; kb++) {
+                for (int kb = kb0; kb < kb1; kb++) {
                     if (!mbar_wait_bounded(&full[stage], phase, abort_flag, WAIT_LIMIT_NS)) {
                         fail();
                         ok = false;
@@ -565,7 +620,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + P_A_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; k++)
-                        tc_mma_bf16_pair(d, adesc + 2 * k, bdesc + 2 * k, P_IDESC, (kb | k) != 0 ? 1u : 0u);
+                        tc_mma_bf16_pair(d, adesc + 2 * k, bdesc + 2 * k, P_IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
                     tc_commit_pair_mc(&empty[stage], 0x3);
                     if (++stage == P_STAGES) {
                         stage = 0;
@@ -590,7 +645,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t bad = 0;
         bool stored = false;
         const uint64_t out_pol = l2_evict_first_policy();  // outputs are written once
-        for (int t = pair; t < total; t += npairs) {
+        unit_iter it(pp, pair);
+        int t, kb0, kb1;
+        bool dead = false;
+        while (it.next(pp, pair, npairs, t, kb0, kb1)) {
             int mb, nbg, seg, nb;
             pair_tile_coords(t, pp, mb, nbg);
             locate(nbg, seg, nb);
@@ -600,6 +658,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 break;
             }
             tc_fence_after();
+            // stream-K: this run stops inside the tile (its sum goes to the
+            // workspace), or finishes a tile that earlier runs started
+            const bool part = kb1 < pp.num_k, fin = !part && kb0 > 0;
+            const int j0 = fin ? (int) ((int64_t) (t - pp.dp_tiles) * pp.num_k / pp.sk_q) : 0;
+            if (fin && !dead)
+                for (int j = j0; j < pair; j++)
+                    if (!flag_wait_bounded(&g_sk_flag[2 * j + rank], pp.sk_epoch, abort_flag, WAIT_LIMIT_NS)) {
+                        fail();
+                        dead = true;  // keep step with the other warps through the barriers below
+                        break;
+                    }
+            const int row_local = q * 32 + lane;
             const int64_t row0 = (int64_t) mb * P_BM + rank * 128 + q * 32, row = row0 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * ACC_COLS);
             uint32_t r[32];
@@ -610,6 +680,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tc_fence_before();
                     mbar_arrive_cluster(tempty_leader[acc]);
                 }
+                if (part) {
+                    float *dst = g_sk_part + (size_t) blockIdx.x * SK_SLOT_FLOATS + row_local * 256 + ch * 32;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4 *>(dst + i) = make_float4(
+                            __uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
+                            __uint_as_float(r[i + 3]));
+                    continue;
+                }
+                if (fin && !dead)
+                    for (int j = j0; j < pair; j++) {
+                        const float *src =
+                            g_sk_part + (size_t) (2 * j + rank) * SK_SLOT_FLOATS + row_local * 256 + ch * 32;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            const float4 v = *reinterpret_cast<const float4 *>(src + i);
+                            r[i] = __float_as_uint(__uint_as_float(r[i]) + v.x);
+                            r[i + 1] = __float_as_uint(__uint_as_float(r[i + 1]) + v.y);
+                            r[i + 2] = __float_as_uint(__uint_as_float(r[i + 2]) + v.z);
+                            r[i + 3] = __float_as_uint(__uint_as_float(r[i + 3]) + v.w);
+                        }
+                    }
                 const int64_t col0 = (int64_t) nb * P_BN + ch * 32;
                 if (col0 >= p.N) continue;
                 if (!p.tma_store) {
@@ -641,6 +733,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tma_store_2d_hint(&maps.c[seg], buf, (int32_t) col0, (int32_t) row0, out_pol);
                     bulk_commit_group();
                     stored = true;
+                }
+            }
+            if (part || fin) {
+                // the four epilogue warps are through this tile: publish our
+                // partial, or free the partials we consumed for the next launch
+                named_barrier(1, 128);
+                if (q == 0 && lane == 0) {
+                    if (part) {
+                        __threadfence();
+                        flag_release(&g_sk_flag[blockIdx.x], pp.sk_epoch);
+                    } else {
+                        for (int j = j0; j < pair; j++) g_sk_flag[2 * j + rank] = 0;
+                    }
                 }
             }
             if (++acc == 2) {
@@ -723,6 +828,76 @@ int num_sms() {
     return sms;
 }
 
+// Stream-K plan: when the last wave of whole tiles would leave pairs idle,
+// that wave and the full wave before it are cut into equal runs of k-blocks,
+// one run per pair. Not when the last wave is nearly full (the partial sums
+// cost more than the idle pairs), nor for runs under 4 k-blocks. Off unless
+// ZEST_GEMM_SK=1: measured on the configs' shapes, the extra epilogues of
+// the split tiles cost more than the idle pairs of the last wave (only the
+// K >= 9728 launches gained, by 3-7 %).
+bool plan_stream_k(pair_params &pp, int64_t tiles, int pairs) {
+    static const bool on = [] {
+        const char *s = getenv("ZEST_GEMM_SK");
+        return s && s[0] == '1';
+    }();
+    const int64_t full = tiles / pairs, rem = tiles % pairs;
+    if (!on || rem == 0 || 2 * pairs > SK_SLOTS || rem > (pairs * 7) / 8) return false;
+    if (full == 0 && rem < 2) return false;
+    const int64_t sk_tiles = rem + (full >= 1 ? pairs : 0);
+    const int64_t q = (sk_tiles * pp.num_k + pairs - 1) / pairs;
+    if (q < 4) return false;
+    pp.dp_tiles = (int) ((full >= 1 ? full - 1 : 0) * pairs);
+    pp.sk_tiles = (int) sk_tiles;
+    pp.sk_q = q;
+    return true;
+}
+
+// The stream-K workspace is one per device, so launches that may use it run
+// one at a time: a launch on another stream than the last one waits for it
+// (and inside a stream capture, where it cannot wait on outside work, runs
+// without stream-K).
+struct sk_owner {
+    cudaStream_t last = nullptr;
+    cudaEvent_t done = nullptr;
+    bool recorded = false;
+    int epoch = 0;
+};
+std::mutex g_sk_mu;
+sk_owner g_sk_owner[64];
+
+bool sk_claim(cudaStream_t st, int *epoch) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return false;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) return false;
+    const bool capturing = cs != cudaStreamCaptureStatusNone;
+    std::lock_guard<std::mutex> lk(g_sk_mu);
+    sk_owner &o = g_sk_owner[dev];
+    if (!o.done && cudaEventCreateWithFlags(&o.done, cudaEventDisableTiming) != cudaSuccess) return false;
+    if (o.recorded && o.last != st) {
+        if (capturing) {
+            o.last = st;  // later launches in this capture follow this one in stream order
+            o.recorded = false;
+            return false;
+        }
+        if (cudaStreamWaitEvent(st, o.done, 0) != cudaSuccess) return false;
+    }
+    o.last = st;
+    o.epoch = o.epoch == 0x7fffffff ? 1 : o.epoch + 1;
+    *epoch = o.epoch;
+    return true;
+}
+
+void sk_release(cudaStream_t st) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    std::lock_guard<std::mutex> lk(g_sk_mu);
+    sk_owner &o = g_sk_owner[dev];
+    if (cs == cudaStreamCaptureStatusNone) o.recorded = cudaEventRecord(o.done, st) == cudaSuccess;
+}
+
 // The pair kernel for an N tile of BN_T over a group of weights sharing A:
 // B's tensor maps (BN_T/2-row boxes, one per CTA), the outputs' for TMA
 // stores, a cluster-of-2 launch.
@@ -785,7 +960,19 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
         attr_set = true;
     }
     const int64_t tiles = (int64_t) pp.num_m * pp.num_n;
-    const int pairs = (int) (tiles < num_sms() / 2 ? tiles : num_sms() / 2);
+    const int max_pairs = num_sms() / 2;
+    pp.dp_tiles = (int) tiles;
+    pp.sk_tiles = 0;
+    pp.sk_q = 0;
+    pp.sk_epoch = 0;
+    const bool sk = plan_stream_k(pp, tiles, max_pairs) && sk_claim(st, &pp.sk_epoch);
+    if (!sk) {
+        pp.dp_tiles = (int) tiles;
+        pp.sk_tiles = 0;
+        pp.sk_q = 0;
+    }
+    // stream-K spreads even a small launch over every pair
+    const int pairs = sk ? max_pairs : (int) (tiles < max_pairs ? tiles : max_pairs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) (2 * pairs));
     cfg.blockDim = dim3(NUM_THREADS);
@@ -799,6 +986,7 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T>, ta, maps, pp);
+    if (sk) sk_release(st);
     return check_launch("gemm");
 }
 

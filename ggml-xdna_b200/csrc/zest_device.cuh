@@ -247,6 +247,32 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     }
 }
 
+// Spins until *flag == want (acquire, GPU scope) or limit_ns passes (false).
+__device__ __forceinline__ bool flag_wait_bounded(const int *flag, int want, volatile int *abort, uint64_t limit_ns) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v == want) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 0;; it++) {
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v == want) return true;
+        if ((it & 15u) == 15u) {
+            if (abort && *abort) return false;
+            if (global_ns() - t0 > limit_ns) return false;
+        }
+        __nanosleep(64);
+    }
+}
+
+__device__ __forceinline__ void flag_release(int *flag, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+
+// A barrier among the `n` threads (a multiple of 32) that name barrier `id`.
+__device__ __forceinline__ void named_barrier(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // 2D TMA tile load into shared memory, completing on `bar` (no multicast).
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int32_t c0, int32_t c1) {
     asm volatile(
