@@ -270,27 +270,35 @@ __global__ void __launch_bounds__(128) convert_weight_kernel(row_source src, int
             }
         }
         __syncthreads();
-        for (int b = tid; b < 16 * W / 8; b += 128) {
-            const int kt = b / 128, p = b % 128, c = p / 16, row = p % 16;
-            const int col = kt * TILE_K + c * 8;
+        // a warp per row, a lane per 8-value block: each warp's bf16 store is
+        // one contiguous run of the row (512 bytes when W = 256)
+        const int warp = tid / 32, lane = tid % 32;
+        for (int row = warp; row < 16; row += 4) {
             int64_t limit;
             const uint8_t *base;
             const bool real = source_row(src, r0 + row, limit, base) != nullptr;
-            float v[8];
-            if (real) {
-                dequant8<TYPE>(raw + row * SLOT + head[row], col, v);
-            } else {
+            for (int cb = lane; cb < W / 8; cb += 32) {
+                const int col = cb * 8, kt = col / TILE_K, c = (col % TILE_K) / 8;
+                float v[8];
+                if (real) {
+                    dequant8<TYPE>(raw + row * SLOT + head[row], col, v);
+                } else {
 #pragma unroll
-                for (int i = 0; i < 8; i++) v[i] = 0.0f;  // padding rows (xdna-npu.cpp:372, pad_n)
+                    for (int i = 0; i < 8; i++) v[i] = 0.0f;  // padding rows (xdna-npu.cpp:372, pad_n)
+                }
+                uint8_t enc[9];
+                uint32_t bf[4];
+                encode_block(v, enc, bf);
+                if (b_bf16)
+                    *reinterpret_cast<uint4 *>(b_bf16 + (r0 + row) * K + w0 + col) =
+                        make_uint4(bf[0], bf[1], bf[2], bf[3]);
+                if (b_bytes) {
+                    // the tile's order: 16-row pair, then block column, then row
+                    uint8_t *s = stage + kt * SUB_BYTES + (c * 16 + row) * BLOCK_BYTES;
+#pragma unroll
+                    for (int i = 0; i < 9; i++) s[i] = enc[i];
+                }
             }
-            uint8_t enc[9];
-            uint32_t bf[4];
-            encode_block(v, enc, bf);
-            if (b_bf16)
-                *reinterpret_cast<uint4 *>(b_bf16 + (r0 + row) * K + w0 + col) = make_uint4(bf[0], bf[1], bf[2], bf[3]);
-            uint8_t *s = stage + kt * SUB_BYTES + p * BLOCK_BYTES;
-#pragma unroll
-            for (int i = 0; i < 9; i++) s[i] = enc[i];
         }
         __syncthreads();
         if (b_bytes)
@@ -346,7 +354,7 @@ int set_iq3s_grid(const uint32_t *grid512) {
 template <int TYPE, int W>
 static void launch_convert_t(const row_source &s, int64_t n_pad, int64_t K, uint8_t *b, uint16_t *h, cudaStream_t st) {
     const int64_t units = (n_pad / 16) * (K / W);
-    convert_weight_kernel<TYPE, W><<<grid_for(units, 8), 128, 0, st>>>(s, n_pad, K, b, h);
+    convert_weight_kernel<TYPE, W><<<grid_for(units, 16), 128, 0, st>>>(s, n_pad, K, b, h);
 }
 
 int launch_convert_weight(int type, const void *src0, const void *src1, int fused, int64_t n_rows, int64_t src_row0,
