@@ -458,6 +458,8 @@ struct context {
     size_t stage_next = 0;
     float *rope_table = nullptr;
     size_t rope_cap = 0;
+    void *a_next = nullptr;  // a SwiGLU's packed result on its way to the next matmul
+    size_t a_next_cap = 0;
     // where the time goes, printed with GGML_XDNA_TRACE=1
     double compute_ms = 0, copy_ms = 0;
     int64_t matmuls = 0, pieces = 0, late_copies = 0, small_ops = 0, fused = 0, grouped = 0;
@@ -477,6 +479,7 @@ struct context {
     }
 
     ~context() {
+        cudaFree(a_next);
         if (npu) zest_close(npu);
         cudaFree(stage_x);
         cudaFree(stage_y);
@@ -786,6 +789,287 @@ bool small_op(context &ctx, ggml_tensor *n, std::string &err) {
     return true;
 }
 
+// ---------------------------------------------------------------------------
+// a piece's plan: which matmuls run together and which small ops ride along
+// ---------------------------------------------------------------------------
+
+// GGML_ZEST_FUSE=0 runs the block executor's ops one by one.
+bool fuse_on() {
+    static const bool v = env_int("GGML_ZEST_FUSE", 1) != 0;
+    return v;
+}
+
+// One call of the matmul service: a group of matmuls on one input (or a
+// fused SwiGLU), with what it folds in from the nodes around it (the
+// reference folds the same ops into its passes over the rows, run_pass,
+// src/xdna-exec.cpp:368-388):
+//   norm/mul   the RMS_NORM (and its MUL by a weight row) that makes the
+//              input: normalised inside the pack, never written out
+//   add[i]     the residual ADD that reads matmul i's result and nothing
+//              else does: added in the GEMM epilogue, written to the ADD
+//   a_next     a SwiGLU whose result only the next matmul reads: written as
+//              that matmul's packed operand, not as f32 (packed_in there)
+struct mm_job {
+    std::vector<ggml_tensor *> mms;
+    const fusion *glu = nullptr;
+    ggml_tensor *norm = nullptr, *mul = nullptr;
+    std::vector<ggml_tensor *> add;
+    bool a_next = false, packed_in = false;
+};
+
+// RMS_NORM -> MUL (a weight row) -> ROPE of the same rows: one kernel.
+struct rope_job {
+    ggml_tensor *norm, *mul, *rope;
+};
+
+struct piece_plan {
+    std::vector<fusion> fusions;  // the fused SwiGLUs (jobs point into it)
+    std::vector<mm_job> jobs;
+    std::vector<rope_job> ropes;
+    std::unordered_map<const ggml_tensor *, int> job_at, rope_at;  // anchor node -> job
+    std::unordered_map<const ggml_tensor *, bool> skip;            // run inside another node's job
+    int counts[6] = {};  // SwiGLU fusions, groups, norm prologues, ADD epilogues, packed hand-offs, norm+rope
+};
+
+template <typename Set>
+piece_plan plan_piece(const std::vector<ggml_tensor *> &nodes, const Set &in_piece) {
+    piece_plan pl;
+    std::unordered_map<const ggml_tensor *, int> idx;
+    for (size_t i = 0; i < nodes.size(); i++) idx[nodes[i]] = (int) i;
+    // in-piece readers of a tensor's storage
+    std::unordered_map<const ggml_tensor *, std::vector<ggml_tensor *>> readers;
+    for (ggml_tensor *m : nodes)
+        for (int j = 0; j < GGML_MAX_SRC; j++)
+            if (m->src[j]) readers[owner(m->src[j])].push_back(m);
+    auto only_read_by = [&](const ggml_tensor *t, const std::vector<ggml_tensor *> &by) {
+        if (read_outside(t, in_piece)) return false;
+        auto it = readers.find(t);
+        if (it == readers.end()) return false;
+        for (ggml_tensor *r : it->second)
+            if (std::find(by.begin(), by.end(), r) == by.end()) return false;
+        return true;
+    };
+    auto pos = [&](const ggml_tensor *t) { auto it = idx.find(t); return it == idx.end() ? -1 : it->second; };
+    auto dev = [](const ggml_tensor *t) { return t && t->data && !is_host(t); };
+
+    if (blocks()) {
+        pl.fusions = find_fusions(nodes, in_piece);
+        for (const fusion &f : pl.fusions) {
+            mm_job j;
+            j.mms = { f.gate };
+            if (f.up) j.mms.push_back(f.up);
+            j.glu = &f;
+            pl.job_at[f.gate] = (int) pl.jobs.size();
+            pl.jobs.push_back(j);
+            if (f.up) pl.skip[f.up] = true;
+            pl.skip[f.glu] = true;
+            pl.counts[0]++;
+        }
+    }
+    std::unordered_map<const ggml_tensor *, bool> taken;
+    for (const auto &kv : pl.job_at) taken[kv.first] = true;
+    for (const auto &kv : pl.skip) taken[kv.first] = true;
+    const auto groups = groups_on() ? find_groups(nodes, taken) : std::vector<std::vector<ggml_tensor *>>();
+    for (const auto &g : groups) {
+        mm_job j;
+        j.mms = g;
+        pl.job_at[g[0]] = (int) pl.jobs.size();
+        pl.jobs.push_back(j);
+        for (size_t k = 1; k < g.size(); k++) pl.skip[g[k]] = true;
+        for (ggml_tensor *m : g) taken[m] = true;
+        pl.counts[1]++;
+    }
+    for (ggml_tensor *m : nodes)
+        if (op_is(m, "MUL_MAT") && !taken.count(m)) {
+            mm_job j;
+            j.mms = { m };
+            pl.job_at[m] = (int) pl.jobs.size();
+            pl.jobs.push_back(j);
+        }
+    for (mm_job &j : pl.jobs) j.add.assign(j.mms.size(), nullptr);
+    if (!blocks() || !fuse_on()) return pl;
+
+    for (mm_job &j : pl.jobs) {
+        const int at = pos(j.mms[0]);
+        ggml_tensor *x = j.mms[0]->src[1];
+        const ggml_tensor *out0 = j.glu ? j.glu->glu : j.mms[0];
+        bool all_dev = dev(x) && dev(out0);
+        for (ggml_tensor *m : j.mms) all_dev = all_dev && dev(m->src[1]);
+        if (!all_dev) continue;
+        // prologue: x = MUL(RMS_NORM(y), w) or RMS_NORM(y), just before the job
+        ggml_tensor *mul = op_is(x, "MUL") ? x : nullptr;
+        ggml_tensor *nrm = mul ? mul->src[0] : x;
+        if (op_is(nrm, "RMS_NORM") && pos(nrm) >= 0 && f32_contig(nrm->src[0]) && dev(nrm->src[0]) &&
+            nrm->src[0]->ne[0] == x->ne[0] && (!mul || (pos(mul) == pos(nrm) + 1 && is_row_of(mul->src[1], mul) &&
+                                                        dev(mul->src[1]) && mul->src[0] == nrm)) &&
+            pos(x) + 1 == at && only_read_by(x, j.mms) && (!mul || only_read_by(nrm, { mul })) &&
+            !pl.skip.count(nrm) && !pl.job_at.count(nrm)) {
+            j.norm = nrm;
+            j.mul = mul;
+            pl.skip[nrm] = true;
+            if (mul) pl.skip[mul] = true;
+            pl.counts[2]++;
+        }
+        // epilogue: a plain matmul whose only reader is the ADD right after it
+        if (!j.glu && j.mms.size() == 1) {
+            ggml_tensor *m = j.mms[0];
+            const int after = pos(m) + 1;
+            if (after < (int) nodes.size()) {
+                ggml_tensor *a = nodes[after];
+                if (op_is(a, "ADD") && (a->src[0] == m || a->src[1] == m) && only_read_by(m, { a })) {
+                    const ggml_tensor *r = a->src[0] == m ? a->src[1] : a->src[0];
+                    if (r && f32_contig(r) && same_shape(r, a) && same_shape(m, a) && f32_contig(a) && dev(r) &&
+                        dev(a) && pos(owner(r)) < pos(m)) {
+                        j.add[0] = a;
+                        pl.skip[a] = true;
+                        pl.counts[3]++;
+                    }
+                }
+            }
+        }
+    }
+    // a SwiGLU whose only reader is the matmul right after it hands over its packed result
+    for (mm_job &j : pl.jobs) {
+        if (!j.glu) continue;
+        ggml_tensor *g = j.glu->glu;
+        const int after = pos(g) + 1;
+        if (after >= (int) nodes.size()) continue;
+        auto it = pl.job_at.find(nodes[after]);
+        if (it == pl.job_at.end()) continue;
+        mm_job &k = pl.jobs[it->second];
+        if (k.glu || k.norm || k.mms.size() != 1 || k.mms[0]->src[1] != g || !only_read_by(g, k.mms)) continue;
+        if (!f32_contig(g) || g->ne[0] % 64) continue;
+        j.a_next = true;
+        k.packed_in = true;
+        pl.counts[4]++;
+    }
+    // norm + rope of a head-shaped view: RMS_NORM -> MUL(w) -> ROPE, consecutive
+    for (size_t i = 0; i + 2 < nodes.size(); i++) {
+        ggml_tensor *nrm = nodes[i], *mul = nodes[i + 1], *rope = nodes[i + 2];
+        if (!op_is(nrm, "RMS_NORM") || !op_is(mul, "MUL") || !op_is(rope, "ROPE")) continue;
+        if (pl.skip.count(nrm) || pl.skip.count(mul) || mul->src[0] != nrm || rope->src[0] != mul) continue;
+        const ggml_tensor *a = nrm->src[0];
+        const int mode = param_i32(rope, 2);
+        if (!f32_contig(a) || !f32_contig(rope) || !same_shape(a, rope) || a->ne[0] > 256 || a->ne[3] != 1 ||
+            !is_row_of(mul->src[1], mul) || (mode != ZEST_ROPE_NORMAL && mode != ZEST_ROPE_NEOX))
+            continue;
+        if (!dev(a) || !dev(rope) || !dev(mul->src[1]) || !only_read_by(nrm, { mul }) || !only_read_by(mul, { rope }))
+            continue;
+        pl.rope_at[rope] = (int) pl.ropes.size();
+        pl.ropes.push_back({ nrm, mul, rope });
+        pl.skip[nrm] = true;
+        pl.skip[mul] = true;
+        pl.counts[5]++;
+    }
+    return pl;
+}
+
+// The rope table of a ROPE node's positions, in the context's table.
+const float *rope_table_of(context &ctx, const ggml_tensor *n, cudaStream_t st, std::string &err) {
+    const int n_dims = param_i32(n, 1), n_ctx_orig = param_i32(n, 4);
+    const int64_t T = n->src[0]->ne[2];
+    const float par[6] = { param_f32(n, 5), param_f32(n, 6), param_f32(n, 7),
+                           param_f32(n, 8), param_f32(n, 9), param_f32(n, 10) };
+    const size_t tb = (size_t) (T * n_dims) * sizeof(float);
+    if (tb > ctx.rope_cap) {
+        cudaFree(ctx.rope_table);
+        ctx.rope_table = nullptr;
+        ctx.rope_cap = 0;
+        if (cudaMalloc(&ctx.rope_table, tb) != cudaSuccess) {
+            err = "cannot allocate the rope table";
+            return nullptr;
+        }
+        ctx.rope_cap = tb;
+    }
+    const int32_t *pos = (const int32_t *) device_in(ctx, n->src[1], st);
+    const float *ff = (const float *) device_in(ctx, n->src[2], st);
+    if (zest_rope_table(pos, T, n_dims, n_ctx_orig, par, ff, ctx.rope_table, st)) {
+        err = std::string(n->name) + ": " + zest_last_error();
+        return nullptr;
+    }
+    return ctx.rope_table;
+}
+
+bool run_rope_job(context &ctx, const rope_job &r, std::string &err) {
+    cudaStream_t st = (cudaStream_t) zest_stream(ctx.npu);
+    const float *table = rope_table_of(ctx, r.rope, st, err);
+    if (!table) return false;
+    const ggml_tensor *a = r.norm->src[0];
+    if (zest_norm_rope((const float *) a->data, a->ne[2], a->ne[1], a->ne[0], param_f32(r.norm, 0),
+                       (const float *) r.mul->src[1]->data, param_i32(r.rope, 1), param_i32(r.rope, 2), table,
+                       (float *) r.rope->data, nullptr, st)) {
+        err = std::string(r.rope->name) + ": " + zest_last_error();
+        return false;
+    }
+    ctx.small_ops += 3;
+    return true;
+}
+
+// One job through zest_mul_mat_group_ex (device memory throughout).
+bool run_mm_job(context &ctx, const mm_job &j, std::string &err) {
+    std::vector<zest_wkey> keys;
+    std::vector<int> fused;
+    std::vector<zest_mm_out> outs;
+    if (j.glu) {
+        zest_wkey key;
+        if (!ensure_fused(ctx, *j.glu, key, err)) return false;
+        keys.push_back(key);
+        fused.push_back(1);
+        ggml_tensor *g = j.glu->glu;
+        uint16_t *an = nullptr;
+        if (j.a_next) {
+            const size_t need = (size_t) ((g->ne[1] + 127) / 128 * 128) * (size_t) g->ne[0] * 2;
+            if (need > ctx.a_next_cap) {
+                cudaFree(ctx.a_next);
+                ctx.a_next = nullptr;
+                ctx.a_next_cap = 0;
+                if (cudaMalloc(&ctx.a_next, need) != cudaSuccess) {
+                    err = "cannot allocate the packed hand-off";
+                    return false;
+                }
+                ctx.a_next_cap = need;
+            }
+            an = (uint16_t *) ctx.a_next;
+        }
+        outs.push_back({ j.a_next ? nullptr : (float *) g->data, nullptr, an });
+        ctx.matmuls += j.glu->up ? 2 : 1;
+        ctx.fused++;
+    } else {
+        for (size_t i = 0; i < j.mms.size(); i++) {
+            const ggml_tensor *w = j.mms[i]->src[0];
+            if (!ensure_weight(ctx, w, err)) return false;
+            keys.push_back({ w->buffer, w->data, (int) w->type, w->ne[0], w->ne[1] });
+            fused.push_back(0);
+            const ggml_tensor *a = j.add[i];
+            const ggml_tensor *r = a ? (a->src[0] == j.mms[i] ? a->src[1] : a->src[0]) : nullptr;
+            outs.push_back({ (float *) (a ? a->data : j.mms[i]->data), r ? (const float *) r->data : nullptr, nullptr });
+        }
+        ctx.matmuls += (int64_t) j.mms.size();
+        ctx.grouped += (int64_t) j.mms.size() - 1;
+    }
+    const ggml_tensor *x = j.mms[0]->src[1];
+    const float *xin = j.norm ? (const float *) j.norm->src[0]->data : (const float *) x->data;
+    const float eps = j.norm ? param_f32(j.norm, 0) : -1.0f;
+    const float *nw = j.mul ? (const float *) j.mul->src[1]->data : nullptr;
+    const uint16_t *a = j.packed_in ? (const uint16_t *) ctx.a_next : nullptr;
+    if (zest_mul_mat_group_ex(ctx.npu, (int) keys.size(), keys.data(), fused.data(), j.packed_in ? nullptr : xin,
+                              eps, nw, nullptr, a, x->ne[1], outs.data())) {
+        err = std::string(j.mms[0]->name) + ": " + zest_last_error();
+        return false;
+    }
+    if (j.norm) ctx.small_ops += j.mul ? 2 : 1;
+    for (const ggml_tensor *ad : j.add)
+        if (ad) ctx.small_ops++;
+    return true;
+}
+
+// Whether a job must take the one-op-at-a-time route: any of its tensors in
+// host memory (staged by mul_mat / mul_mat_group), and nothing fused.
+bool plain_job(const mm_job &j) {
+    return !j.glu && !j.norm && !j.a_next && !j.packed_in &&
+           std::all_of(j.add.begin(), j.add.end(), [](const ggml_tensor *a) { return a == nullptr; });
+}
+
 enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgraph) {
     context &ctx = *(context *) backend->context;
     {
@@ -812,48 +1096,30 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
         const std::unordered_map<const ggml_tensor *, int> &m;
         size_t count(const ggml_tensor *t) const { return m.count(t); }
     } in_piece{ in_piece_map };
-    const std::vector<fusion> fusions = blocks() ? find_fusions(nodes, in_piece) : std::vector<fusion>();
-    std::unordered_map<const ggml_tensor *, const fusion *> fused_gate;
-    std::unordered_map<const ggml_tensor *, bool> fused_skip;
-    for (const fusion &f : fusions) {
-        fused_gate[f.gate] = &f;
-        if (f.up) fused_skip[f.up] = true;
-        fused_skip[f.glu] = true;
-    }
-    std::unordered_map<const ggml_tensor *, bool> unfused;
-    for (const auto &kv : fused_gate) unfused[kv.first] = true;
-    for (const auto &kv : fused_skip) unfused[kv.first] = true;
-    const auto groups = groups_on() ? find_groups(nodes, unfused) : std::vector<std::vector<ggml_tensor *>>();
-    std::unordered_map<const ggml_tensor *, const std::vector<ggml_tensor *> *> group_first;
-    for (const auto &g : groups) {
-        group_first[g[0]] = &g;
-        for (size_t j = 1; j < g.size(); j++) fused_skip[g[j]] = true;
-    }
+    const piece_plan plan = plan_piece(nodes, in_piece);
     cudaStream_t st = (cudaStream_t) zest_stream(ctx.npu);
     for (ggml_tensor *node : nodes) {
         if (status != GGML_STATUS_SUCCESS) break;
         std::string err;
-        bool ok;
-        if (fused_skip.count(node)) continue;
-        if (auto it = fused_gate.find(node); it != fused_gate.end()) {
-            const fusion &f = *it->second;
-            zest_wkey key;
-            const ggml_tensor *x = f.gate->src[1];
-            ok = ensure_fused(ctx, f, key, err);
-            if (ok && (is_host(x) || is_host(f.glu))) {
-                err = "a fused SwiGLU with host-memory operands";
-                ok = false;
+        bool ok = true;
+        if (plan.skip.count(node)) continue;
+        if (auto it = plan.job_at.find(node); it != plan.job_at.end()) {
+            const mm_job &j = plan.jobs[it->second];
+            if (j.glu) {
+                const ggml_tensor *x = j.glu->gate->src[1];
+                if (is_host(x) || is_host(j.glu->glu)) {
+                    err = "a fused SwiGLU with host-memory operands";
+                    ok = false;
+                } else {
+                    ok = run_mm_job(ctx, j, err);
+                }
+            } else if (plain_job(j)) {
+                ok = j.mms.size() > 1 ? mul_mat_group(ctx, j.mms, err) : mul_mat(ctx, j.mms[0], err);
+            } else {
+                ok = run_mm_job(ctx, j, err);
             }
-            if (ok && zest_mul_mat(ctx.npu, &key, 1, (const float *) x->data, x->ne[1], (float *) f.glu->data, 1)) {
-                err = std::string(f.glu->name) + ": " + zest_last_error();
-                ok = false;
-            }
-            ctx.matmuls += f.up ? 2 : 1;
-            ctx.fused++;
-        } else if (auto gi = group_first.find(node); gi != group_first.end()) {
-            ok = mul_mat_group(ctx, *gi->second, err);
-        } else if (op_is(node, "MUL_MAT")) {
-            ok = mul_mat(ctx, node, err);
+        } else if (auto ri = plan.rope_at.find(node); ri != plan.rope_at.end()) {
+            ok = run_rope_job(ctx, plan.ropes[ri->second], err);
         } else {
             ok = small_op(ctx, node, err);
         }
@@ -1075,6 +1341,26 @@ int ggml_zest_piece_groups(ggml_cgraph *cgraph, int *sizes, int max_groups) {
     const auto groups = find_groups(nodes, none);
     for (int i = 0; i < (int) groups.size() && i < max_groups; i++) sizes[i] = (int) groups[i].size();
     return (int) groups.size();
+}
+
+int ggml_zest_piece_plan(ggml_cgraph *cgraph, int *counts) {
+    std::vector<ggml_tensor *> nodes;
+    std::unordered_map<const ggml_tensor *, int> in_piece_map;
+    const int n = ggml_graph_n_nodes(cgraph);
+    for (int i = 0; i < n; i++) {
+        ggml_tensor *node = ggml_graph_node(cgraph, i);
+        in_piece_map[node] = i;
+        if (!(op_is(node, "NONE") || op_is(node, "RESHAPE") || op_is(node, "VIEW") || op_is(node, "PERMUTE") ||
+              op_is(node, "TRANSPOSE")))
+            nodes.push_back(node);
+    }
+    struct piece_set {
+        const std::unordered_map<const ggml_tensor *, int> &m;
+        size_t count(const ggml_tensor *t) const { return m.count(t); }
+    } in_piece{ in_piece_map };
+    const piece_plan pl = plan_piece(nodes, in_piece);
+    for (int i = 0; i < 6; i++) counts[i] = pl.counts[i];
+    return (int) pl.jobs.size();
 }
 
 int ggml_zest_piece_fusions(ggml_cgraph *cgraph) {

@@ -529,6 +529,66 @@ int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *f
     return 0;
 }
 
+int zest_mul_mat_group_ex(zest_npu *npu, int n, const zest_wkey *keys, const int *fused, const float *x,
+                          float norm_eps, const float *norm_w, float *x_normed, const uint16_t *a_bf16, int64_t T,
+                          const zest_mm_out *outs) {
+    if (!npu || !keys || !outs || n <= 0 || n > 4) return set_error("zest_mul_mat_group_ex: no service, or not 1 to 4 weights");
+    const zest_npu::weight *w[4];
+    for (int i = 0; i < n; i++) {
+        w[i] = npu->find(&keys[i], fused ? fused[i] : 0);
+        if (!w[i]) return set_error("zest_mul_mat_group_ex: weight not added");
+        if (w[i]->K != w[0]->K) return set_error("zest_mul_mat_group_ex: a group's weights differ in K");
+    }
+    if (!a_bf16 && !x) return set_error("zest_mul_mat_group_ex: no input");
+    if (T <= 0) return 0;
+    if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_mul_mat_group_ex: cannot select the device");
+    if (npu->inject && injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
+    const int64_t K = w[0]->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
+    cudaStream_t st = npu->st;
+    const bool nan = npu->inject && injected_nan();
+    cudaEventRecord(npu->t_pack[0], st);
+    cudaMemsetAsync(npu->err_dev, 0, sizeof(unsigned), st);
+    int rc = 0;
+    const uint16_t *a = a_bf16;
+    if (!a) {
+        if (!grow((void **) &npu->a_bf16, &npu->a_cap, (size_t) (m_pad * K) * 2))
+            return set_error("zest_mul_mat_group_ex: out of GPU memory for the packed input");
+        rc = norm_eps >= 0.0f ? zest_pack_rms_norm(x, T, K, K, norm_eps, norm_w, x_normed, K, m_pad, npu->a_bf16, K, st)
+                              : launch_pack_activations(x, T, K, K, m_pad, nullptr, npu->a_bf16, K, st);
+        a = npu->a_bf16;
+    }
+    cudaEventRecord(npu->t_gemm[0], st);
+    gemm_seg segs[4];
+    for (int i = 0; i < n; i++) {
+        segs[i] = { w[i]->bf16, K, w[i]->n_pad, w[i]->n_out, w[i]->n_out, w[i]->mode, outs[i].y };
+        segs[i].resid = outs[i].residual;
+        segs[i].ldr = w[i]->n_out;
+        segs[i].a_next = outs[i].a_next;
+        segs[i].lda_next = w[i]->n_out;
+    }
+    if (!rc) rc = launch_gemm_group(a, K, T, K, n, segs, npu->err_dev, st);
+    if (!rc && nan)
+        for (int i = 0; i < n; i++)
+            if (outs[i].y) {
+                cudaMemsetAsync(outs[i].y, 0xff, (size_t) (T * w[i]->n_out) * 4, st);
+                check_finite_kernel<<<148, 256, 0, st>>>(outs[i].y, T * w[i]->n_out, npu->err_dev);
+            }
+    cudaEventRecord(npu->t_end[0], st);
+    cudaMemcpyAsync(npu->err_host, npu->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail("zest_mul_mat_group_ex", e);
+    float pa = 0, gm = 0;
+    cudaEventElapsedTime(&pa, npu->t_pack[0], npu->t_gemm[0]);
+    cudaEventElapsedTime(&gm, npu->t_gemm[0], npu->t_end[0]);
+    npu->times.encode_ms += pa;
+    npu->times.gemm_ms += gm;
+    npu->times.calls += n;
+    if (*npu->err_host & ERR_TIMEOUT) return set_error("a GPU kernel's bounded wait ran out");
+    if (*npu->err_host & ERR_NOT_FINITE) return set_error("the GPU's results held NaN or infinity");
+    return 0;
+}
+
 int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x, int64_t T, float *y, int on_device) {
     if (!key) return set_error("zest_mul_mat: no service or key");
     float *ys[1] = { y };

@@ -45,6 +45,11 @@ class GemmSeg(ctypes.Structure):
                 ("residual", _vp), ("ldr", _i64), ("a_next", _vp), ("lda_next", _i64)]
 
 
+class MmOut(ctypes.Structure):
+    """zest_mm_out: where one weight's result of zest_mul_mat_group_ex goes."""
+    _fields_ = [("y", _vp), ("residual", _vp), ("a_next", _vp)]
+
+
 class Times(ctypes.Structure):
     _fields_ = [("encode_ms", ctypes.c_double), ("gemm_ms", ctypes.c_double), ("copy_ms", ctypes.c_double),
                 ("pack_ms", ctypes.c_double), ("calls", _int)]
@@ -94,6 +99,8 @@ def lib() -> ctypes.CDLL:
         "zest_weight_bf16": (_vp, [_vp, ctypes.POINTER(WKey), _int, ctypes.POINTER(_i64)]),
         "zest_mul_mat": (_int, [_vp, ctypes.POINTER(WKey), _int, _vp, _i64, _vp, _int]),
         "zest_mul_mat_group": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, _i64, _vpp, _int]),
+        "zest_mul_mat_group_ex": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, ctypes.c_float, _vp, _vp, _vp,
+                                         _i64, ctypes.POINTER(MmOut)]),
         "zest_stream": (_vp, [_vp]),
         "zest_take_times": (_int, [_vp, ctypes.POINTER(Times)]),
     }
@@ -114,7 +121,7 @@ def exported_symbols() -> list[str]:
                         "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
                         "zest_add_weight_values",
                         "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_mul_mat",
-                        "zest_mul_mat_group", "zest_stream", "zest_take_times")]
+                        "zest_mul_mat_group", "zest_mul_mat_group_ex", "zest_stream", "zest_take_times")]
 
 
 def _check(rc: int, what: str) -> None:
@@ -293,6 +300,17 @@ class Npu:
         _check(lib().zest_mul_mat_group(self.h, n, (WKey * n)(*keys), (_int * n)(*[int(f) for f in fused]),
                                         ctypes.c_void_p(x_ptr), T, (_vp * n)(*y_ptrs), int(on_device)),
                "zest_mul_mat_group")
+
+    def mul_mat_group_ex(self, keys, outs, T: int, x_ptr: int = 0, a_ptr: int = 0, norm_eps: float = -1.0,
+                         norm_w_ptr: int = 0, x_normed_ptr: int = 0, fused=None):
+        """Device buffers; outs: [(y, residual, a_next)] pointers (0 for none)."""
+        n = len(keys)
+        fused = fused or [False] * n
+        _check(lib().zest_mul_mat_group_ex(self.h, n, (WKey * n)(*keys), (_int * n)(*[int(f) for f in fused]),
+                                           ctypes.c_void_p(x_ptr), ctypes.c_float(norm_eps),
+                                           ctypes.c_void_p(norm_w_ptr), ctypes.c_void_p(x_normed_ptr),
+                                           ctypes.c_void_p(a_ptr), T, (MmOut * n)(*[MmOut(*o) for o in outs])),
+               "zest_mul_mat_group_ex")
 
     def stream(self) -> int:
         return int(lib().zest_stream(self.h) or 0)

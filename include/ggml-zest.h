@@ -46,6 +46,13 @@ __attribute__((visibility("default"))) int ggml_zest_piece_fusions(struct ggml_c
 __attribute__((visibility("default"))) int ggml_zest_piece_groups(struct ggml_cgraph *cgraph, int *sizes,
                                                                   int max_groups);
 
+/* The plan graph_compute makes for this piece: returns the number of matmul
+ * service calls and writes counts[0..5]: fused SwiGLUs, grouped matmul
+ * calls, RMS_NORMs folded into a pack, residual ADDs folded into a GEMM
+ * epilogue, SwiGLU results handed to the next matmul packed, and
+ * RMS_NORM + MUL + ROPE runs done as one kernel. Host logic only; for tests. */
+__attribute__((visibility("default"))) int ggml_zest_piece_plan(struct ggml_cgraph *cgraph, int *counts);
+
 #ifdef __cplusplus
 }
 #endif

@@ -284,6 +284,27 @@ int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x,
 int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *fused, const float *x, int64_t T,
                        float *const *y, int on_device);
 
+/* Where one weight's result of zest_mul_mat_group_ex goes. */
+typedef struct {
+    float *y;               /* [T][out_width]; may be NULL for a fused gate/up weight that gives a_next */
+    const float *residual;  /* NULL, or the ADD that follows: y = residual + result ([T][out_width], may be y) */
+    uint16_t *a_next;       /* NULL, or (a fused gate/up weight) the SwiGLU result's K2 operand,
+                               [roundup(T,128)][out_width], the next matmul's a_bf16 */
+} zest_mm_out;
+
+/* zest_mul_mat_group on device buffers, with the block executor's ops next
+ * to the matmuls folded in. The input is one of: a_bf16 (an operand already
+ * packed, [roundup(T,128)][K], e.g. another call's a_next); x after
+ * RMS_NORM(norm_eps) and a MUL by norm_w (may be NULL) when norm_eps >= 0,
+ * the f32 normalised rows going to x_normed unless it is NULL; or x as is.
+ * Each weight's result goes where outs[i] says.
+ * Replaces: a piece's run_rows passes around its matmuls (RMS_NORM, MUL,
+ * ADD, GLU; src/xdna-exec.cpp:253-346,368-388) together with the group's
+ * encode / submit / decode (src/xdna-npu.cpp:476-551). */
+int zest_mul_mat_group_ex(zest_npu *npu, int n, const zest_wkey *keys, const int *fused, const float *x,
+                          float norm_eps, const float *norm_w, float *x_normed, const uint16_t *a_bf16, int64_t T,
+                          const zest_mm_out *outs);
+
 /* The service's CUDA stream (a cudaStream_t). */
 void *zest_stream(zest_npu *npu);
 

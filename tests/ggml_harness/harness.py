@@ -98,6 +98,7 @@ class Harness:
         self.plugin.ggml_backend_score.restype = _int
         self.plugin.ggml_zest_policy_supports.argtypes = [ctypes.POINTER(Tensor)]
         self.plugin.ggml_zest_piece_fusions.argtypes = [_vp]
+        self.plugin.ggml_zest_piece_plan.argtypes = [_vp, ctypes.POINTER(ctypes.c_int)]
         self.plugin.ggml_zest_piece_groups.argtypes = [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
         # ctypes objects the C side points at, kept for the whole process: the
         # plugin remembers who read each tensor by address (as the reference
@@ -109,6 +110,14 @@ class Harness:
         arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])
         self.keep.append(arr)
         return self.plugin.ggml_zest_piece_fusions(self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp)))
+
+    def piece_plan(self, nodes: list[Tensor]) -> dict:
+        """graph_compute's plan for a piece: its service calls and what it folds in."""
+        arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])
+        self.keep.append(arr)
+        c = (ctypes.c_int * 6)()
+        jobs = self.plugin.ggml_zest_piece_plan(self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp)), c)
+        return dict(jobs=jobs, swiglu=c[0], groups=c[1], norm=c[2], add=c[3], handoff=c[4], rope=c[5])
 
     def piece_groups(self, nodes: list[Tensor]) -> list[int]:
         arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])

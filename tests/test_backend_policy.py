@@ -232,3 +232,57 @@ def test_matmul_groups(h):
     assert piece(alias=True) == [2], "k's bytes are q_norm's, live between q and k: k runs at its own turn"
     assert piece(host_out=True) == [2], "an output in host memory with the input on the device"
     assert piece(n_extra=2) == [4], "at most 4 to a group"
+
+
+def test_piece_plan_folds_the_block_ops(h):
+    # what graph_compute folds into its matmul calls: the RMS_NORM (and MUL)
+    # before a matmul into the pack, the residual ADD after o/down into the
+    # GEMM epilogue, a SwiGLU whose only reader is down into down's packed
+    # input, and RMS_NORM -> MUL -> ROPE into one kernel
+    k, f, t, hd, heads = 2048, 5632, 2048, 128, 16
+    C, W = h.buffer(USAGE_COMPUTE), h.buffer(USAGE_WEIGHTS)
+    base = 0x7e0000000000
+    addr = iter(range(base, base + (256 << 30), 1 << 30))
+
+    def T(type_, ne, name, buf=C, **kw):
+        return h.tensor(type_, ne, name, buf, next(addr), **kw)
+
+    def ffn(extra_norm_reader=False):
+        x = T(F32, [k, t], "x")
+        nrm = h.rms_norm(x, name="ffn_norm", buffer=C, data=next(addr))
+        m = h.mul(nrm, T(F32, [k], "ffn_norm.weight", W), name="ffn_inp", buffer=C, data=next(addr))
+        g = h.mul_mat(T(Q4_K, [k, f], "ffn_gate.weight", W), m, "gate", C, next(addr))
+        u = h.mul_mat(T(Q4_K, [k, f], "ffn_up.weight", W), m, "up", C, next(addr))
+        s = h.glu(g, u, kind=2, name="swiglu", buffer=C, data=next(addr))
+        d = h.mul_mat(T(Q4_K, [f, k], "ffn_down.weight", W), s, "down", C, next(addr))
+        out = h.add(d, x, name="ffn_out", buffer=C, data=next(addr))
+        nodes = [nrm, m, g, u, s, d, out]
+        if extra_norm_reader:
+            nodes.append(h.scale(nrm, 2.0, name="other", buffer=C, data=next(addr)))
+        for nd in nodes:
+            h.supports_op(nd)
+        return h.piece_plan(nodes)
+
+    p = ffn()
+    assert (p["swiglu"], p["norm"], p["add"], p["handoff"]) == (1, 1, 1, 1), p
+    assert p["jobs"] == 2  # gate/up and down: two service calls for the whole block
+    p = ffn(extra_norm_reader=True)
+    assert p["norm"] == 0 and p["swiglu"] == 1, "a norm read by another op is computed on its own"
+
+    x = T(F32, [k, t], "x")
+    nrm = h.rms_norm(x, name="attn_norm", buffer=C, data=next(addr))
+    m = h.mul(nrm, T(F32, [k], "attn_norm.weight", W), name="attn_inp", buffer=C, data=next(addr))
+    q = h.mul_mat(T(Q4_K, [k, heads * hd], "attn_q.weight", W), m, "q", C, next(addr))
+    kk = h.mul_mat(T(Q4_K, [k, 4 * hd], "attn_k.weight", W), m, "k", C, next(addr))
+    v = h.mul_mat(T(Q4_K, [k, 4 * hd], "attn_v.weight", W), m, "v", C, next(addr))
+    q3 = h.tensor(F32, [hd, heads, t], "q3", C, q.data, op="RESHAPE", src=(q,), view_src=q)
+    qn = h.rms_norm(q3, name="q_norm", buffer=C, data=next(addr))
+    qm = h.mul(qn, T(F32, [hd], "attn_q_norm.weight", W), name="q_normed", buffer=C, data=next(addr))
+    pos = h.tensor(26, [t], "pos", h.buffer(USAGE_COMPUTE), next(addr))
+    qr = h.rope(qm, pos, hd, 2, name="q_rope", buffer=C, data=next(addr))
+    nodes = [nrm, m, q, kk, v, q3, qn, qm, qr]
+    for nd in nodes:
+        h.supports_op(nd)
+    p = h.piece_plan(nodes)
+    assert (p["groups"], p["norm"], p["rope"]) == (1, 1, 1), p
+    assert p["jobs"] == 1

@@ -48,7 +48,13 @@ class Buffers:
         return t
 
 
-def test_ffn_piece_with_fused_swiglu(h):
+@pytest.mark.parametrize("keep", [False, True])
+def test_ffn_piece_with_fused_swiglu(h, keep):
+    # keep=False: only the block's output is read outside the piece, so the
+    # norm rides in the pack, gate/up in one SwiGLU GEMM that hands down its
+    # packed result, and the residual ADD in down's epilogue: the
+    # intermediates are never written. keep=True: they are graph outputs, so
+    # each is computed and written.
     K, F, T = 1024, 2816, 1024
     rng = np.random.default_rng(1)
     x = (rng.standard_normal((T, K)) * 1.5).astype(np.float32)
@@ -72,14 +78,19 @@ def test_ffn_piece_with_fused_swiglu(h):
     u = h.mul_mat(uw, n2, "up", C, u_out.data_ptr())
     s_out = B.out(T, F)
     s = h.glu(g, u, kind=2, name="swiglu", buffer=C, data=s_out.data_ptr())
-    dn = h.mul_mat(dw, s, "down", C, B.out(T, K).data_ptr())
+    d_out = B.out(T, K)
+    dn = h.mul_mat(dw, s, "down", C, d_out.data_ptr())
     y = B.out(T, K)
     out = h.add(dn, xt, name="ffn_out", buffer=C, data=y.data_ptr())
     out.flags = 2  # GGML_TENSOR_FLAG_OUTPUT
+    if keep:
+        n2.flags = s.flags = dn.flags = 2
     nodes = [n1, n2, g, u, s, dn, out]
     for nd in nodes:  # the scheduler asks about every op: this records who reads what
         h.supports_op(nd)
     assert h.supports_op(s) and h.supports_op(out)
+    plan = h.piece_plan(nodes)
+    assert (plan["norm"], plan["handoff"], plan["add"]) == ((0, 0, 0) if keep else (1, 1, 1)), plan
     b, _ = h.init_backend()
     torch.cuda.synchronize()
     h.graph_optimize(b, nodes)
@@ -88,13 +99,17 @@ def test_ffn_piece_with_fused_swiglu(h):
     # the gate and up results were never written: one fused GEMM produced the SwiGLU
     assert torch.isnan(g_out).all() and torch.isnan(u_out).all()
     xm = O.mul_row(O.rms_norm(x, K, 1e-6), wn)
-    assert O.nrmse(m.cpu().numpy(), xm) <= 1e-5
     gv = O.mul_mat(dec(O.dequant(Q4_K, g_raw, F, K)), dec(xm))
     uv = O.mul_mat(dec(O.dequant(Q4_K, u_raw, F, K)), dec(xm))
     sv = O.swiglu_bf16(gv, uv)
-    assert O.nrmse(s_out.cpu().numpy(), sv) <= 1e-3
     want = O.add(mm_bf16(O.dequant(Q8_0, d_raw, K, F), sv), x)
     assert O.nrmse(y.cpu().numpy(), want) <= 1e-3
+    if keep:
+        assert O.nrmse(m.cpu().numpy(), xm) <= 1e-5
+        assert O.nrmse(s_out.cpu().numpy(), sv) <= 1e-3
+        assert O.nrmse(d_out.cpu().numpy(), mm_bf16(O.dequant(Q8_0, d_raw, K, F), sv)) <= 1e-3
+    else:
+        assert torch.isnan(m).all() and torch.isnan(s_out).all() and torch.isnan(d_out).all()
     h.backend_free(b)
 
 
@@ -124,6 +139,8 @@ def test_attention_input_piece_with_rope(h):
     nodes = [n1, n2, q, q3, qn, qm, qr]
     for nd in nodes:
         h.supports_op(nd)
+    plan = h.piece_plan(nodes)
+    assert (plan["norm"], plan["rope"]) == (1, 1), plan  # the norms ride in the pack and in the rope kernel
     b, _ = h.init_backend()
     torch.cuda.synchronize()
     assert h.graph_compute(b, nodes) == STATUS_SUCCESS
