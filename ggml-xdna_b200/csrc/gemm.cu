@@ -487,7 +487,9 @@ __device__ __forceinline__ void pair_tile_coords(int t, const pair_params &pp, i
     }
 }
 
-template <int BN_T>
+// SK: whether this instance walks stream-K runs (a separate instance, so the
+// whole-tile kernel carries none of that code or its registers).
+template <int BN_T, bool SK>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ pair_maps maps,
                              const __grid_constant__ pair_params pp) {
@@ -660,7 +662,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tc_fence_after();
             // stream-K: this run stops inside the tile (its sum goes to the
             // workspace), or finishes a tile that earlier runs started
-            const bool part = kb1 < pp.num_k, fin = !part && kb0 > 0;
+            const bool part = SK && kb1 < pp.num_k, fin = SK && !part && kb0 > 0;
             const int j0 = fin ? (int) ((int64_t) (t - pp.dp_tiles) * pp.num_k / pp.sk_q) : 0;
             if (fin && !dead)
                 for (int j = j0; j < pair; j++)
@@ -952,12 +954,21 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
         const int f = atoi(force);
         if (f >= RASTER_GROUPS && f <= RASTER_COLS) pp.raster = f;
     }
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 C::P_SMEM_BYTES) != cudaSuccess)
-            return check_launch("gemm (shared memory size)");
-        attr_set = true;
+    {
+        // a function attribute holds per device: set it once on each
+        static std::mutex mu;
+        static uint64_t set_on = 0;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev >= 64 || !((set_on >> dev) & 1)) {
+            if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::P_SMEM_BYTES) != cudaSuccess ||
+                cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::P_SMEM_BYTES) != cudaSuccess)
+                return check_launch("gemm (shared memory size)");
+            if (dev < 64) set_on |= 1ull << dev;
+        }
     }
     const int64_t tiles = (int64_t) pp.num_m * pp.num_n;
     const int max_pairs = num_sms() / 2;
@@ -985,7 +996,10 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T>, ta, maps, pp);
+    if (sk)
+        cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T, true>, ta, maps, pp);
+    else
+        cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T, false>, ta, maps, pp);
     if (sk) sk_release(st);
     return check_launch("gemm");
 }
@@ -1012,12 +1026,18 @@ int launch_single(const CUtensorMap &ta, int64_t M, int64_t K, const gemm_seg &g
     p.num_n = (int) ((g.N + BN - 1) / BN);
     p.num_k = (int) ((K + BK - 1) / BK);
     p.tma_store = 0;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess)
-            return check_launch("gemm (shared memory size)");
-        attr = true;
+    {
+        static std::mutex mu;
+        static uint64_t set_on = 0;  // per device, as the attribute holds
+        int dev = 0;
+        cudaGetDevice(&dev);
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev >= 64 || !((set_on >> dev) & 1)) {
+            if (cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+                cudaSuccess)
+                return check_launch("gemm (shared memory size)");
+            if (dev < 64) set_on |= 1ull << dev;
+        }
     }
     const int64_t tiles = (int64_t) p.num_m * p.num_n;
     const int grid = (int) (tiles < num_sms() ? tiles : num_sms());
