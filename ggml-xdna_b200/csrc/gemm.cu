@@ -86,15 +86,30 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb
     nb = r / gsz;
 }
 
-__device__ __forceinline__ float bf16_round(float x) {
-    uint32_t u = __float_as_uint(x);
-    if ((u & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(u | 0x00400000u);
-    u += 0x7fffu + ((u >> 16) & 1u);
-    return __uint_as_float(u & 0xffff0000u);
-}
-
 __device__ __forceinline__ uint32_t not_finite(float v) {
     return (__float_as_uint(v) & 0x7f800000u) == 0x7f800000u;
+}
+
+// Two floats rounded to bf16, nearest even, by the hardware's paired
+// conversion (a NaN comes back as a NaN), and widened back to floats.
+__device__ __forceinline__ void bf16_round2(float &x, float &y) {
+    uint32_t p;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(y), "f"(x));
+    x = __uint_as_float(p << 16);
+    y = __uint_as_float(p & 0xffff0000u);
+}
+
+// Whether any of 32 values is NaN or infinite, without a branch: x * 0 is 0
+// for every finite x and NaN otherwise.
+__device__ __forceinline__ uint32_t any_not_finite(const float (&o)[32]) {
+    float c0 = 0.0f, c1 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+        c0 = __fmaf_rn(o[i], 0.0f, c0);
+        c1 = __fmaf_rn(o[i + 1], 0.0f, c1);
+    }
+    const float c = c0 + c1;
+    return c != c;
 }
 
 // o[i] = resid[row][col0 + i] + o[i] for the columns the output holds (the
@@ -132,8 +147,10 @@ __device__ __forceinline__ uint32_t store_chunk(const gemm_params &p, const uint
             for (int i = 0; i < 8; i++) {
                 const float g = __uint_as_float(r[h * 16 + i]), u = __uint_as_float(r[h * 16 + 8 + i]);
                 const float s = 1.0f / (1.0f + expf(-g));
-                o[h * 8 + i] = bf16_round((g * u) * s);
+                o[h * 8 + i] = (g * u) * s;
             }
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) bf16_round2(o[i], o[i + 1]);
         const int64_t oc0 = col0 / 2;
         if (p.a_next) {
             // two aligned 8-value blocks (oc0 is a multiple of 16), encoded
@@ -174,18 +191,17 @@ __device__ __forceinline__ uint32_t store_chunk(const gemm_params &p, const uint
     }
     float o[32];
 #pragma unroll
-    for (int i = 0; i < 32; i++) {
-        const float v = __uint_as_float(r[i]);
-        o[i] = p.mode == MODE_BF16 ? bf16_round(v) : v;
-    }
+    for (int i = 0; i < 32; i++) o[i] = __uint_as_float(r[i]);
+    if (p.mode == MODE_BF16)
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) bf16_round2(o[i], o[i + 1]);
     if (p.resid) add_residual(p, o, row, col0);
     float *dst = p.c + row * p.ldc + col0;
-    if (col0 + 32 <= p.n_out && (p.ldc % 4) == 0) {
+    if (col0 + 32 <= p.n_out && (p.ldc % 4) == 0 && ((uintptr_t) dst & 15) == 0) {
+        bad |= any_not_finite(o);
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
+        for (int i = 0; i < 32; i += 4)
             *reinterpret_cast<float4 *>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-            bad |= not_finite(o[i]) | not_finite(o[i + 1]) | not_finite(o[i + 2]) | not_finite(o[i + 3]);
-        }
     } else {
 #pragma unroll
         for (int i = 0; i < 32; i++)
@@ -717,14 +733,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 __syncwarp();
                 float o[32];
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const float v = __uint_as_float(r[i]);
-                    o[i] = p.mode == MODE_BF16 ? bf16_round(v) : v;
-                }
-                if (p.resid && row < p.M) add_residual(p, o, row, col0);
+                for (int i = 0; i < 32; i++) o[i] = __uint_as_float(r[i]);
+                if (p.mode == MODE_BF16)
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    if (row < p.M && col0 + i < p.n_out) bad |= not_finite(o[i]);
+                    for (int i = 0; i < 32; i += 2) bf16_round2(o[i], o[i + 1]);
+                if (p.resid && row < p.M) add_residual(p, o, row, col0);
+                // rows past M and columns past the output hold the operands' zero
+                // fill (TMA's out-of-bounds fill, the weights' zero padding rows),
+                // so the whole chunk can be checked without a branch
+                bad |= any_not_finite(o);
 #pragma unroll
                 for (int j = 0; j < 8; j++)
                     *reinterpret_cast<float4 *>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
