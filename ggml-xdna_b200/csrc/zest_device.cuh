@@ -77,6 +77,31 @@ __device__ __forceinline__ void encode_block(const float (&x)[8], uint8_t (&out)
         any |= u & 0x7fffffffu;
     }
     int q[8];
+    if (mx >= 6 && mx <= 200) {
+        // every value finite and the block's quantum Q = 2^(e - 133) in the
+        // normal or subnormal range: rounding x * 2^(133 - e) to an integer,
+        // nearest even, is rounding x to a multiple of Q, which one add and
+        // one subtract of C = 1.5 * 2^23 * Q do exactly (|x| < 2^7 Q, far
+        // inside the 2^22 Q the method needs); then q <= 127 is d <= 127 Q
+        // (x / Q > -128 always, so -128 never clamps). d is q * Q exactly,
+        // the decoded value, and has at most 8 significant bits.
+        const float C = u2f(((mx + 17u) << 23) | 0x400000u);  // 1.5 * 2^(mx - 110)
+        const float top = u2f((mx << 23) | 0x7E0000u);        // 127 * 2^(mx - 133)
+        const float scale = u2f((260u - mx) << 23);           // 2^(133 - mx)
+        uint32_t h[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float d = fminf(__fsub_rn(__fadd_rn(x[i], C), C), top);
+            h[i] = f2u(d) >> 16;
+            q[i] = __float2int_rz(__fmul_rn(d, scale));
+        }
+        out[0] = (uint8_t) mx;
+#pragma unroll
+        for (int i = 0; i < 8; i++) out[1 + i] = (uint8_t) (int8_t) q[i];
+#pragma unroll
+        for (int i = 0; i < 4; i++) bf[i] = h[2 * i] | (h[2 * i + 1] << 16);
+        return;
+    }
     if (mx >= 6) {
         const float scale = u2f((260u - mx) << 23);
 #pragma unroll
