@@ -732,7 +732,26 @@ class Prefill:
             with torch.cuda.graph(g):
                 self.claimed_chunk(p0, T)
             self.graphs[ci] = g
+        # the unclaimed tail and the LM head as one more graph (torch ops only)
+        self.tail_graph = None
+        p0, T = self.chunks[-1]
+        if T < self.c["min_batch"]:
+            self.head_out = torch.empty(self.c["vocab"], dtype=torch.float32, device="cuda")
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self._tail_and_head(p0, T)
+            torch.cuda.current_stream().wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._tail_and_head(p0, T)
+            self.tail_graph = g
         torch.cuda.synchronize()
+
+    def _tail_and_head(self, p0, T):
+        torch = self.torch
+        last = self.unclaimed_chunk(p0, T)[-1:]
+        h = last * torch.rsqrt(last.pow(2).mean(-1, keepdim=True) + self.c["eps"]) * self.out_norm
+        self.head_out.copy_((h.to(torch.bfloat16) @ self.lm_head.T).float()[0])
 
     def _segs(self, K, T, items, ev):
         """One zest_gemm_segs launch: items = [(weight, N, mode, c, residual, a_next)]."""
@@ -857,13 +876,19 @@ class Prefill:
             xt = xt + mm(torch.nn.functional.silu(gu[:, self.gi]) * gu[:, self.gi + 8], d["down"], H)
         return xt
 
-    def run(self, ids_host, evs=None, claim=True, graphs=False, att_evs=None):
+    def run(self, ids_host, evs=None, claim=True, graphs=False, att_evs=None, tail_ev=None):
         """One prefill: token ids (pinned host) in, last-token logits (pinned
         host) out. claim=False runs every chunk as an unclaimed one;
-        graphs=True replays the captured claimed chunks."""
+        graphs=True replays the captured claimed chunks (and the tail)."""
         torch = self.torch
         self.ids.copy_(ids_host, non_blocking=True)
         last = None
+        if graphs and claim and self.tail_graph is not None:
+            for ci in range(len(self.chunks) - 1):
+                self.graphs[ci].replay()
+            self.tail_graph.replay()
+            self.logits.copy_(self.head_out, non_blocking=True)
+            return self.logits
         for ci, (p0, T) in enumerate(self.chunks):
             if claim and T >= self.c["min_batch"]:
                 if graphs:
@@ -873,9 +898,13 @@ class Prefill:
                     last = self.claimed_chunk(p0, T, evs[ci] if evs is not None else None,
                                               att_evs[ci] if att_evs is not None else None)[-1:]
             else:
+                if tail_ev is not None:
+                    tail_ev[0].record()
                 last = self.unclaimed_chunk(p0, T)[-1:]
         h = last * torch.rsqrt(last.pow(2).mean(-1, keepdim=True) + self.c["eps"]) * self.out_norm
         self.logits.copy_((h.to(torch.bfloat16) @ self.lm_head.T).float()[0], non_blocking=True)
+        if tail_ev is not None:
+            tail_ev[1].record()
         return self.logits
 
 
@@ -915,11 +944,12 @@ def run_model(args, w: dict) -> None:
     n_prof = 2
     evs = [[[[mk() for _ in range(4)] for _ in range(nL)] for _ in m.chunks] for _ in range(n_prof)]
     aevs = [[[mk() for _ in range(nL)] for _ in m.chunks] for _ in range(n_prof)]
+    tevs = [mk() for _ in range(n_prof)]
     e0, e1 = mk()
     torch.cuda.synchronize()
     e0.record()
     for si in range(n_prof):
-        m.run(ids_host, evs[si], att_evs=aevs[si])
+        m.run(ids_host, evs[si], att_evs=aevs[si], tail_ev=tevs[si])
     e1.record()
     torch.cuda.synchronize()
     eager_ms = e0.elapsed_time(e1) / n_prof
@@ -957,6 +987,7 @@ def run_model(args, w: dict) -> None:
                 per_launch[names[j]] += e / (nL * len(claimed))
             att_ms += sum(aevs[si][ci][li][0].elapsed_time(aevs[si][ci][li][1]) for si in range(n_prof)) / n_prof
         per_chunk.append(tot)
+    tail_ms = sum(a.elapsed_time(b) for a, b in tevs) / n_prof if m.chunks[-1][1] < c["min_batch"] else 0.0
     per_token_fl = 2.0 * nL * sum(N * K for N, K in m.shapes.values())
     claimed_fl = per_token_fl * sum(m.chunks[ci][1] for ci in claimed)
     mm_ms = sum(per_chunk)
@@ -984,7 +1015,7 @@ def run_model(args, w: dict) -> None:
                                   "eighth, every third between). One seeded set of raw bytes per type, converted "
                                   "into every layer's own device copy",
                        "attention": m.attn_impl + " (outside the path)",
-                       "graphs": "each claimed chunk replayed from its CUDA graph",
+                       "graphs": "each claimed chunk, and the tail with the LM head, replayed from CUDA graphs",
                        "fused": "norm in the pack, q/k norm with rope, residual ADDs and SwiGLU's packed output in "
                                 "the GEMM epilogues" if m.fused else "every op its own kernel",
                        "unclaimed": f"the {m.chunks[-1][1]}-token tail (< {c['min_batch']} tokens) in torch ops",
@@ -999,8 +1030,8 @@ def run_model(args, w: dict) -> None:
                         "share_of_prefill": mm_ms / ms_max,
                         "per_launch_us": {n: round(v * 1e3, 1) for n, v in per_launch.items()}},
             "breakdown_ms": {"prefill_graphs": ms_max, "prefill_eager": eager_ms, "mul_mat": mm_ms,
-                             "attention_claimed_chunks": att_ms,
-                             "rest": eager_ms - mm_ms - att_ms,
+                             "attention_claimed_chunks": att_ms, "tail_and_head_eager": tail_ms,
+                             "rest": eager_ms - mm_ms - att_ms - tail_ms,
                              "note": "eager prefills with events around each launch; the rest is the small ops, "
                                      "packs, cache writes, the unclaimed tail, the LM head and the host gaps"},
             "load": {"weight_conversion_s": m.load_s, "layers": nL},
