@@ -850,17 +850,20 @@ int num_sms() {
 // Stream-K plan: when the last wave of whole tiles would leave pairs idle,
 // that wave and the full wave before it are cut into equal runs of k-blocks,
 // one run per pair. Not when the last wave is nearly full (the partial sums
-// cost more than the idle pairs), nor for runs under 4 k-blocks. Off unless
-// ZEST_GEMM_SK=1: measured on the configs' shapes, the extra epilogues of
-// the split tiles cost more than the idle pairs of the last wave (only the
-// K >= 9728 launches gained, by 3-7 %).
+// cost more than the idle pairs), nor for runs under 4 k-blocks, and by
+// default only for K >= 8192: measured on the configs' shapes, a split
+// tile's extra epilogue costs more than the idle pairs save at K <= 4096
+// (C1 53 -> 61 us, C3 q+k+v 55 -> 63 us), while the long-K down projections
+// gain (C3 down 112 -> 93 us, C2 down 295 -> 277 us). ZEST_GEMM_SK=1 splits
+// at any K, ZEST_GEMM_SK=0 never.
 bool plan_stream_k(pair_params &pp, int64_t tiles, int pairs) {
-    static const bool on = [] {
+    static const int mode = [] {
         const char *s = getenv("ZEST_GEMM_SK");
-        return s && s[0] == '1';
+        return s && s[0] == '1' ? 1 : (s && s[0] == '0' ? 0 : 2);
     }();
     const int64_t full = tiles / pairs, rem = tiles % pairs;
-    if (!on || rem == 0 || 2 * pairs > SK_SLOTS || rem > (pairs * 7) / 8) return false;
+    if (mode == 0 || (mode == 2 && pp.num_k < 128)) return false;
+    if (rem == 0 || 2 * pairs > SK_SLOTS || rem > (pairs * 7) / 8) return false;
     if (full == 0 && rem < 2) return false;
     const int64_t sk_tiles = rem + (full >= 1 ? pairs : 0);
     const int64_t q = (sk_tiles * pp.num_k + pairs - 1) / pairs;
