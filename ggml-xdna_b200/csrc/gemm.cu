@@ -671,6 +671,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             pair_tile_coords(t, pp, mb, nbg);
             locate(nbg, seg, nb);
             const gemm_params &p = pp.seg[seg];
+            if (p.resid) {
+                // bring this row's residual into L2 while the tile's MMAs run
+                const int64_t prow = (int64_t) mb * P_BM + rank * 128 + q * 32 + lane;
+                const int64_t pc0 = (int64_t) nb * P_BN;
+                if (prow < p.M)
+                    for (int c = 0; c < P_BN && pc0 + c < p.n_out; c += 32)
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.resid + prow * p.ldr + pc0 + c));
+            }
             if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, WAIT_LIMIT_NS)) {
                 fail();
                 break;
@@ -692,6 +700,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t tbase = tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * ACC_COLS);
             uint32_t r[32];
             for (int ch = 0; ch < P_BN / 32; ch++) {
+                // the residual's loads go out before the TMEM load, so their
+                // latency overlaps it (the aligned, full-width case)
+                float4 rr[8];
+                const int64_t rcol0 = (int64_t) nb * P_BN + ch * 32;
+                const bool rfast = p.resid && p.tma_store && row < p.M && rcol0 + 32 <= p.n_out &&
+                                   (p.ldr % 4) == 0 && ((uintptr_t) p.resid & 15) == 0;
+                if (rfast) {
+                    const float4 *src = reinterpret_cast<const float4 *>(p.resid + row * p.ldr + rcol0);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) rr[i] = src[i];
+                }
                 tmem_ld_32x32b_x32(tbase + (uint32_t) (ch * 32), r);
                 tmem_ld_wait();
                 if (ch == P_BN / 32 - 1) {
@@ -737,7 +756,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (p.mode == MODE_BF16)
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) bf16_round2(o[i], o[i + 1]);
-                if (p.resid && row < p.M) add_residual(p, o, row, col0);
+                if (rfast) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        o[4 * i] = __fadd_rn(rr[i].x, o[4 * i]);
+                        o[4 * i + 1] = __fadd_rn(rr[i].y, o[4 * i + 1]);
+                        o[4 * i + 2] = __fadd_rn(rr[i].z, o[4 * i + 2]);
+                        o[4 * i + 3] = __fadd_rn(rr[i].w, o[4 * i + 3]);
+                    }
+                } else if (p.resid && row < p.M) {
+                    add_residual(p, o, row, col0);
+                }
                 // rows past M and columns past the output hold the operands' zero
                 // fill (TMA's out-of-bounds fill, the weights' zero padding rows),
                 // so the whole chunk can be checked without a branch
