@@ -1056,6 +1056,228 @@ def run_model(args, w: dict) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# tensor-parallel layer (--mode tp)
+# ---------------------------------------------------------------------------
+
+TP_KSHARDED = ("o", "down")  # inputs the block leaves split by columns: attention heads, the SwiGLU
+
+
+def run_tp(args, w: dict) -> None:
+    """The layer's MUL_MATs as one tensor-parallel block on N GPUs: q/k/v and
+    gate/up N-sharded (each rank its slab of output columns, left where they
+    are, as a head-parallel attention and the FFN's SwiGLU consume them);
+    o and down K-sharded (each rank multiplies its column slab of their input
+    by the same slab of the weight), and their partial products summed by
+    one NCCL all-reduce per row chunk, issued as each chunk's GEMMs finish so
+    it overlaps the next chunk's. Strong scaling: the job is one layer of M
+    tokens however many GPUs share it."""
+    import torch
+    import torch.distributed as dist
+
+    import zest_b200 as Z
+    from zest_b200.shard import all_reduce_rows, shard_cols, shard_rows
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    from datetime import timedelta
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    threads = max(1, (os.cpu_count() or 1) // max(1, world))
+    if w["qtype"] == IQ3_S:
+        Z.load_iq3s_grid()
+    M, qt = w["M"], w["qtype"]
+    kinds = {}
+    for name, N, K, kind in w["proj"]:
+        kinds.setdefault(kind, K)
+    ksh = {kind for kind in kinds if kind in TP_KSHARDED}
+
+    # weights: N-sharded projections convert their row slab; K-sharded ones
+    # convert whole and multiply the column slab of the bf16 copy in place
+    bh, n_of, kcols = {}, {}, {}
+    for name, N, K, kind in w["proj"]:
+        raw = torch.from_numpy(weight_raw(qt, name, N, K, threads)).cuda()
+        if kind in ksh:
+            _, bh[name] = Z.convert_weight(qt, raw, N, K, want_bytes=False)
+            n_of[name] = N
+            kcols[kind] = shard_cols(K, world, rank)
+        else:
+            row0, n = shard_rows(N, world, rank)
+            _, bh[name] = Z.convert_weight(qt, raw, N, K, row0=row0, n_rows=n, want_bytes=False)
+            n_of[name] = n
+        del raw
+    for kind in kinds:
+        kcols.setdefault(kind, (0, kinds[kind]))
+    torch.cuda.synchronize()
+
+    gen = torch.Generator("cuda").manual_seed(1234)  # the same layer input on every rank
+    x, ah = {}, {}
+    mp = Z.pad_to(M, 128)
+    for kind, K in kinds.items():
+        x[kind] = torch.randn(M, K, device="cuda", generator=gen)
+        ah[kind] = torch.empty((mp, kcols[kind][1]), dtype=torch.int16, device="cuda")
+    out = {name: torch.zeros((M, max(1, n_of[name])), dtype=torch.float32, device="cuda")
+           for name, N, K, kind in w["proj"]}
+    # the K-sharded partials summed by the GEMM itself: its epilogue adds them
+    # into a symmetric buffer bound to an NVLink multicast object (every rank
+    # a copy), the NVSwitch doing the reduction, when the box supports it
+    mc = {}
+    reduce_how = "NCCL all-reduce"
+    if world > 1 and args.tp_reduce == "multicast":
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            for name, N, K, kind in w["proj"]:
+                if kind in ksh:
+                    t = symm_mem.empty((M, N), dtype=torch.float32, device="cuda")
+                    hdl = symm_mem.rendezvous(t, dist.group.WORLD)
+                    if not hdl.multicast_ptr:
+                        raise RuntimeError("no multicast support")
+                    out[name] = t
+                    mc[name] = (hdl, int(hdl.multicast_ptr))
+            reduce_how = "multimem.red into an NVLink multicast buffer from the GEMM epilogue"
+        except Exception as e:  # fall back to NCCL
+            mc = {}
+            reduce_how = f"NCCL all-reduce (multicast unavailable: {type(e).__name__}: {e})"
+    tick = torch.zeros(1, dtype=torch.float32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+    L = Z.lib()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    groups = launch_groups(w)
+    CH = Z.pad_to(max(128, M // (1 if mc else args.tp_chunks)), 128)
+    chunks = [(r0, min(CH, M - r0)) for r0 in range(0, M, CH)]
+
+    def ok(rc):
+        if rc:
+            raise Z.ZestError(L.zest_last_error().decode())
+
+    def step(events=None):
+        works = []
+        if mc:
+            # zero this rank's copies, and no rank adds before every rank has
+            # (a one-float all-reduce as the group's stream-ordered fence)
+            for name in mc:
+                out[name].zero_()
+            dist.all_reduce(tick)
+        for ci, (r0, m) in enumerate(chunks):
+            for kind, K in kinds.items():
+                k0, k = kcols[kind]
+                ok(L.zest_pack_activations(ctypes.c_void_p(x[kind][r0:].data_ptr() + 4 * k0), m, k, K,
+                                           Z.pad_to(m, 128), None, ctypes.c_void_p(ah[kind][r0:].data_ptr()), k,
+                                           sp))
+            for gi, (kind, members) in enumerate(groups):
+                k0, k = kcols[kind]
+                n = len(members)
+                partial = kind in ksh
+                if events is not None:
+                    events[gi][ci][0].record(stream)
+                if partial and mc:
+                    segs = (Z.GemmSeg * n)(*[Z.GemmSeg(bh[nm].data_ptr() + 2 * k0, K, n_of[nm], Z.MODE_F32, None,
+                                                       out[nm].shape[1], None, 0, None, 0,
+                                                       mc[nm][1] + 4 * r0 * out[nm].shape[1])
+                                             for nm, _, _ in members])
+                    ok(L.zest_gemm_segs(ctypes.c_void_p(ah[kind][r0:].data_ptr()), k, m, k, n, segs,
+                                        ctypes.c_void_p(err.data_ptr()), sp))
+                else:
+                    ok(L.zest_gemm_group(
+                        ctypes.c_void_p(ah[kind][r0:].data_ptr()), k, m, k, n,
+                        (ctypes.c_void_p * n)(*[bh[nm].data_ptr() + 2 * k0 for nm, _, _ in members]),
+                        (ctypes.c_int64 * n)(*[K for _, _, K in members]),
+                        (ctypes.c_int64 * n)(*[n_of[nm] for nm, _, _ in members]),
+                        (ctypes.c_int * n)(*[Z.MODE_F32 if partial else Z.MODE_BF16] * n),
+                        (ctypes.c_void_p * n)(*[out[nm][r0:].data_ptr() for nm, _, _ in members]),
+                        (ctypes.c_int64 * n)(*[out[nm].shape[1] for nm, _, _ in members]),
+                        ctypes.c_void_p(err.data_ptr()), sp))
+                if events is not None:
+                    events[gi][ci][1].record(stream)
+                if partial and world > 1 and not mc:
+                    for nm, _, _ in members:
+                        works.append(all_reduce_rows(out[nm], r0, m))
+        for wk in works:
+            wk.wait()  # the stream waits for the reductions, not the host
+        if mc:
+            dist.all_reduce(tick)  # every rank's reductions are in before anyone reads the sums
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if int(err.item()):
+        raise Z.ZestError(f"device error bits {int(err.item()):#x} during warm-up")
+    check = None
+    if mc:
+        # the multicast sums against the same partials summed by NCCL
+        worst = 0.0
+        for kind in ksh:
+            k0, k = kcols[kind]
+            for nm, N, K in dict(groups)[kind]:
+                part = torch.empty((M, n_of[nm]), dtype=torch.float32, device="cuda")
+                ok(L.zest_gemm(ctypes.c_void_p(ah[kind].data_ptr()), k, ctypes.c_void_p(bh[nm].data_ptr() + 2 * k0),
+                               K, M, n_of[nm], k, Z.MODE_F32, ctypes.c_void_p(part.data_ptr()), n_of[nm],
+                               ctypes.c_void_p(err.data_ptr()), sp))
+                dist.all_reduce(part)
+                worst = max(worst, ((out[nm] - part).abs().max() / part.abs().max()).item())
+        check = {"max_rel_diff_vs_nccl": worst}
+        if not worst <= 1e-5:
+            raise Z.ZestError(f"multicast sums differ from NCCL's by {worst}")
+    mk = lambda: [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+    ev = [[[mk() for _ in chunks] for _ in groups] for _ in range(args.steps)]
+    t0, t1 = mk()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t0.record(stream)
+        for s in range(args.steps):
+            step(ev[s])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if int(err.item()):
+        raise Z.ZestError(f"device error bits {int(err.item()):#x} in the timed region")
+    ms = t0.elapsed_time(t1) / args.steps
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    gemm_ms = [sum(ev[s][gi][ci][0].elapsed_time(ev[s][gi][ci][1]) for s in range(args.steps)
+                   for ci in range(len(chunks))) / args.steps for gi in range(len(groups))]
+    peaks = measured_peaks()
+    if rank == 0:
+        value = flops(w) / (ms_max * 1e-3) / 1e12
+        names = ["+".join(nm for nm, _, _ in members) for _, members in groups]
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "none", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "desc": w["config"], "M": M, "weights": QNAME[qt],
+                       "parallelism": f"tp{world}: q/k/v and gate/up N-sharded, o/down K-sharded, their partials "
+                                      f"summed by {reduce_how}" + (f", per {CH}-row chunk" if len(chunks) > 1 else ""),
+                       "outputs": "N-sharded projections: bf16-rounded slabs left on their rank; K-sharded: the "
+                                  "f32 sums of the partials on every rank",
+                       "global_tokens_per_step": M},
+            "tokens_per_s": M / (ms_max * 1e-3),
+            "pct_of_bf16_peak": 100.0 * value / (world * peaks["tflops_sustained"]),
+            "per_rank_gemm_us": {nm: round(v * 1e3, 1) for nm, v in zip(names, gemm_ms)},
+            "reduce_check": check,
+            "gpu_launches": args.steps * len(chunks) * (len(kinds) + len(groups)),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        # every rank is done with the multicast buffers before any releases them
+        torch.cuda.synchronize()
+        dist.barrier()
+        mc.clear()
+        out.clear()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1064,9 +1286,14 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--mode", choices=["tokens", "nshard", "nshard-nogather"], default="tokens",
-                    help="N>1: each GPU its own token chunk (default, no collective), or N-slabs of every weight "
-                         "with (nshard) or without the NCCL all-gather of the output slabs")
+    ap.add_argument("--mode", choices=["tokens", "nshard", "nshard-nogather", "tp"], default="tokens",
+                    help="N>1: each GPU its own token chunk (default, no collective), N-slabs of every weight "
+                         "with (nshard) or without the NCCL all-gather of the output slabs, or the layer as "
+                         "one tensor-parallel block (tp: o/down K-sharded, one all-reduce per row chunk)")
+    ap.add_argument("--tp-chunks", type=int, default=1, help="tp with NCCL: row chunks whose all-reduce overlaps the next")
+    ap.add_argument("--tp-reduce", choices=["multicast", "nccl"], default="nccl",
+                    help="tp: K-sharded partials summed by NCCL, or in the GEMM epilogue through NVLink multicast "
+                         "(multimem.red; exact, faster at 2 GPUs, slower at 8)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
     w = WORKLOADS[args.workload]
@@ -1074,6 +1301,8 @@ def main() -> None:
         run_reference(args, w)
     elif w.get("model"):
         run_model(args, w)
+    elif args.mode == "tp":
+        run_tp(args, w)
     else:
         run_ours(args, w)
 

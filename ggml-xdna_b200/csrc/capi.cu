@@ -606,6 +606,7 @@ int zest_gemm_segs(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, in
         g[i].ldr = z.ldr;
         g[i].a_next = z.a_next;
         g[i].lda_next = z.lda_next;
+        g[i].c_mc = z.c_multicast;
     }
     return launch_gemm_group(a_bf16, lda, M, K, n, g, err, (cudaStream_t) stream);
 }

@@ -75,6 +75,7 @@ struct gemm_params {
     int64_t ldr;
     uint16_t *a_next;    // SwiGLU: the result's bfp16-rounded bf16 copy, the next GEMM's A, or null
     int64_t lda_next;
+    float *c_mc;         // or null: the results added (multimem.red) into a multicast buffer [M][ldc]
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
@@ -196,6 +197,23 @@ __device__ __forceinline__ uint32_t store_chunk(const gemm_params &p, const uint
 #pragma unroll
         for (int i = 0; i < 32; i += 2) bf16_round2(o[i], o[i + 1]);
     if (p.resid) add_residual(p, o, row, col0);
+    if (p.c_mc) {
+        // a tensor-parallel partial product: summed into every rank's copy
+        float *dst = p.c_mc + row * p.ldc + col0;
+        if (col0 + 32 <= p.n_out && (p.ldc % 4) == 0 && ((uintptr_t) dst & 15) == 0) {
+            bad |= any_not_finite(o);
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) multimem_red_add_v4(dst + i, o[i], o[i + 1], o[i + 2], o[i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                if (col0 + i < p.n_out) {
+                    multimem_red_add(dst + i, o[i]);
+                    bad |= not_finite(o[i]);
+                }
+        }
+        return bad;
+    }
     float *dst = p.c + row * p.ldc + col0;
     if (col0 + 32 <= p.n_out && (p.ldc % 4) == 0 && ((uintptr_t) dst & 15) == 0) {
         bad |= any_not_finite(o);
@@ -361,6 +379,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 acc_phase ^= 1;
             }
         }
+        if (p.c_mc) asm volatile("fence.acq_rel.sys;" ::: "memory");  // the reductions are performed before we exit
         if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.err, ERR_NOT_FINITE);
     }
 
@@ -741,7 +760,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                 const int64_t col0 = (int64_t) nb * P_BN + ch * 32;
                 if (col0 >= p.N) continue;
-                if (!p.tma_store) {
+                if (!p.tma_store && !p.c_mc) {
                     bad |= store_chunk(p, r, row, col0);
                     continue;
                 }
@@ -775,6 +794,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int j = 0; j < 8; j++)
                     *reinterpret_cast<float4 *>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
                         make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                if (p.c_mc) {
+                    // a tensor-parallel partial: read the staged 32 x 32 back by
+                    // rows (8 lanes a row, 4 rows an instruction) and add each
+                    // 512-byte run into every rank's copy through the NVSwitch
+                    __syncwarp();
+#pragma unroll
+                    for (int it = 0; it < 8; it++) {
+                        const int rl = it * 4 + lane / 8, u = lane % 8;
+                        const float4 v = *reinterpret_cast<const float4 *>(buf + rl * 128 + ((u ^ (rl & 7)) << 4));
+                        const int64_t grow = row0 + rl, gcol = col0 + u * 4;
+                        if (grow < p.M) {
+                            float *dst = p.c_mc + grow * p.ldc + gcol;
+                            if (gcol + 4 <= p.n_out && ((uintptr_t) dst & 15) == 0) {
+                                multimem_red_add_v4(dst, v.x, v.y, v.z, v.w);
+                            } else {
+                                const float e[4] = { v.x, v.y, v.z, v.w };
+                                for (int i = 0; i < 4; i++)
+                                    if (gcol + i < p.n_out) multimem_red_add(dst + i, e[i]);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    continue;
+                }
                 fence_proxy_async_shared();
                 __syncwarp();
                 if (lane == 0) {
@@ -802,6 +845,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
         }
         if (stored) bulk_wait_all();  // every store has landed before the block exits
+        bool mc = false;
+        for (int sg = 0; sg < pp.nseg; sg++) mc = mc || pp.seg[sg].c_mc != nullptr;
+        if (mc) asm volatile("fence.acq_rel.sys;" ::: "memory");  // the reductions are performed before we exit
         if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(pp.err, ERR_NOT_FINITE);
     }
 
@@ -865,6 +911,9 @@ bool make_tmap_out(CUtensorMap *m, void *base, int64_t rows, int64_t cols, int64
            CUDA_SUCCESS;
 }
 
+// The SMs the persistent GEMM spreads over: all of them, or at most
+// ZEST_GEMM_MAX_SMS (even), leaving the rest to kernels that must run beside
+// it, such as a collective overlapping the next row chunk's GEMMs.
 int num_sms() {
     static int sms = 0;
     if (!sms) {
@@ -872,6 +921,10 @@ int num_sms() {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
+        if (const char *cap = getenv("ZEST_GEMM_MAX_SMS")) {
+            const int c = atoi(cap) & ~1;
+            if (c >= 2 && c < sms) sms = c;
+        }
     }
     return sms;
 }
@@ -983,6 +1036,7 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
         p.ldr = g.ldr;
         p.a_next = g.a_next;
         p.lda_next = g.lda_next;
+        p.c_mc = g.c_mc;
         // TMA stores need 16-byte aligned rows; SwiGLU halves the width and keeps direct stores
         p.tma_store = g.mode != MODE_SWIGLU && g.c && g.ldc % 4 == 0 && ((uintptr_t) g.c & 15) == 0 &&
                       make_tmap_out(&maps.c[s], g.c, M, g.n_out, g.ldc);
@@ -1071,6 +1125,7 @@ int launch_single(const CUtensorMap &ta, int64_t M, int64_t K, const gemm_seg &g
     p.ldr = g.ldr;
     p.a_next = g.a_next;
     p.lda_next = g.lda_next;
+    p.c_mc = g.c_mc;
     p.num_m = (int) ((M + BM - 1) / BM);
     p.num_n = (int) ((g.N + BN - 1) / BN);
     p.num_k = (int) ((K + BK - 1) / BK);
@@ -1110,7 +1165,9 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
             return set_error("gemm: bad output mode");
         const int64_t width = g.mode == MODE_SWIGLU ? g.N / 2 : g.N;
         if (g.n_out <= 0 || g.n_out > width) g.n_out = width;
-        if (!g.c && !g.a_next) return set_error("gemm: no output");
+        if (!g.c && !g.a_next && !g.c_mc) return set_error("gemm: no output");
+        if (g.c_mc && (g.c || g.mode == MODE_SWIGLU || g.resid || g.a_next || g.ldc < g.n_out))
+            return set_error("gemm: a multicast output takes fp32 or bf16 results alone, rows of ldc >= the width");
         if (g.c && g.ldc < g.n_out) return set_error("gemm: ldc smaller than the output width");
         if (g.resid && (g.mode == MODE_SWIGLU || !g.c || g.ldr < g.n_out))
             return set_error("gemm: a residual needs an fp32 or bf16 output of its width");

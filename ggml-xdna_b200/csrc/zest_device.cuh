@@ -293,6 +293,18 @@ __device__ __forceinline__ void flag_release(int *flag, int v) {
     asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
 }
 
+// Adds to the value at a multicast address in every GPU bound to it: the
+// NVSwitch performs the reduction (NVLink SHARP). Relaxed, system scope.
+__device__ __forceinline__ void multimem_red_add_v4(float *mc, float a, float b, float c, float d) {
+    asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b),
+                 "f"(c), "f"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ void multimem_red_add(float *mc, float a) {
+    asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(mc), "f"(a) : "memory");
+}
+
 // A barrier among the `n` threads (a multiple of 32) that name barrier `id`.
 __device__ __forceinline__ void named_barrier(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

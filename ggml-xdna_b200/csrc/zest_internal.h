@@ -50,6 +50,7 @@ struct gemm_seg {
     int64_t ldr = 0;
     uint16_t *a_next = nullptr;
     int64_t lda_next = 0;
+    float *c_mc = nullptr;       // multicast address: results added into every GPU's copy (NVSwitch reduction)
 };
 
 // Up to 4 weights sharing one A (q, k and v; gate and up) in one launch.

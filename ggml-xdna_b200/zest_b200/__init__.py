@@ -42,7 +42,7 @@ class WKey(ctypes.Structure):
 class GemmSeg(ctypes.Structure):
     """zest_gemm_seg: one weight of zest_gemm_segs with its fused epilogue."""
     _fields_ = [("b", _vp), ("ldb", _i64), ("N", _i64), ("mode", _int), ("c", _vp), ("ldc", _i64),
-                ("residual", _vp), ("ldr", _i64), ("a_next", _vp), ("lda_next", _i64)]
+                ("residual", _vp), ("ldr", _i64), ("a_next", _vp), ("lda_next", _i64), ("c_multicast", _vp)]
 
 
 class MmOut(ctypes.Structure):

@@ -1,9 +1,17 @@
-"""N-sharding of a MUL_MAT across GPUs: each rank converts and multiplies
-its slab of weight rows (output columns); an all-gather of the slab outputs
-over NCCL (gloo on CPU) rebuilds ggml's row-major [M][N] on every rank.
+"""Partitioning a layer's MUL_MATs across GPUs.
 
-The reference runs on one NPU and has no counterpart; this is the
-partitioning its GEMM admits (output columns are independent).
+N-sharding: each rank converts and multiplies its slab of weight rows
+(output columns); an all-gather of the slab outputs over NCCL (gloo on CPU)
+rebuilds ggml's row-major [M][N] on every rank.
+
+K-sharding (the tensor-parallel block): a projection whose input is already
+split by columns across the ranks (the FFN's down projection after N-sharded
+gate/up) multiplies each rank's column slab of the input by the same column
+slab of the weight; the ranks' partial products add up to the full product
+in one all-reduce, of [M][N] instead of the gather of every projection.
+
+The reference runs on one NPU and has no counterpart; these are the
+partitionings its GEMM admits.
 """
 from __future__ import annotations
 
@@ -40,3 +48,20 @@ def gather_slabs(slab_out, full_out, world: int, N: int, group=None, granule: in
         if n:
             full_out[:, lo:lo + n].copy_(gathered[r, :, :n])
     return full_out
+
+
+K_GRANULE = 64  # columns per K-shard granule: the GEMM's k-block and the pack's tile
+
+
+def shard_cols(K: int, world: int, rank: int, granule: int = K_GRANULE) -> tuple[int, int]:
+    """This rank's slab [k0, k0 + k) of K reduction columns, in whole
+    granules spread as evenly as they go."""
+    return shard_rows(K, world, rank, granule)
+
+
+def all_reduce_rows(partial, row0: int, rows: int, group=None, async_op: bool = True):
+    """Sums rows [row0, row0 + rows) of every rank's partial [M][N] product
+    in place (NCCL, or gloo on CPU). Collective: every rank calls it, in
+    order; returns the work handle when async_op."""
+    import torch.distributed as dist
+    return dist.all_reduce(partial[row0:row0 + rows], op=dist.ReduceOp.SUM, group=group, async_op=async_op)

@@ -126,6 +126,11 @@ typedef struct {
     uint16_t *a_next;     /* NULL, or (ZEST_MODE_SWIGLU) the result's K2 operand: the bf16 copy of
                              its bfp16 rounding, [M][lda_next], the next GEMM's A */
     int64_t lda_next;
+    float *c_multicast;   /* NULL, or (with c NULL) a multicast address of a buffer [M][ldc] that every
+                             GPU of a tensor-parallel group holds: the results are added into all the
+                             copies through the NVSwitch (multimem.red), so when every rank's launch has
+                             finished each copy holds the sum of the ranks' partial products. The
+                             caller zeroes the copies and fences the group before and after */
 } zest_gemm_seg;
 
 /* zest_gemm_group with fused epilogues: per weight a residual ADD, or for a

@@ -75,3 +75,64 @@ def test_gather_rebuilds_row_major_product_gloo():
     results = dict(q.get(timeout=10) for _ in range(world))
     assert all(p.exitcode == 0 for p in procs)
     assert results == {0: True, 1: True}
+
+
+def test_k_shards_cover_columns_exactly():
+    from zest_b200.shard import shard_cols
+    for K in (64, 2560, 9728, 17408):
+        for world in (1, 2, 4, 8):
+            spans = [shard_cols(K, world, r) for r in range(world)]
+            covered = []
+            for k0, k in spans:
+                covered.extend(range(k0, k0 + k))
+            assert covered == list(range(K)), (K, world)
+            assert all(k0 % 64 == 0 and k % 64 == 0 for k0, k in spans if k)
+
+
+def _tp_rank(rank: int, world: int, port: int, q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root), str(root / "ggml-xdna_b200")]
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+    from zest_b200.shard import all_reduce_rows, shard_cols
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        # the down projection of a tensor-parallel FFN: each rank holds a column
+        # slab of the input (the N-sharded SwiGLU) and the same slab of the
+        # weight; the row chunks of the partial products are all-reduced one by one
+        M, N, K, chunk = 96, 320, 1024, 32
+        W = O.dequant(O.Q8_0, O.quantize(O.Q8_0, O.weights_f32(N, K, 3)), N, K)
+        X = O.activations(M, K, 4)
+        k0, k = shard_cols(K, world, rank)
+        part = torch.from_numpy(O.mul_mat(W[:, k0:k0 + k], X[:, k0:k0 + k]))
+        works = [all_reduce_rows(part, r0, min(chunk, M - r0)) for r0 in range(0, M, chunk)]
+        for w in works:
+            w.wait()
+        want = O.mul_mat(W, X)
+        err = float(np.max(np.abs(part.numpy() - want)) / np.max(np.abs(want)))
+        q.put((rank, err < 1e-5))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_k_sharded_partials_sum_to_the_product_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    results = dict(q.get(timeout=10) for _ in range(world))
+    assert all(p.exitcode == 0 for p in procs)
+    assert results == {0: True, 1: True}
