@@ -4,12 +4,21 @@
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--workload NAME]
 
 One step = one prefill chunk through every projection of a layer: the
-activation pack (K2) of each distinct input, then each projection's GEMM
-(K3), weights converted once beforehand (K1), as the reference converts them
-at load. Inputs are seeded synthetic tensors with the configs' shapes and
-distributions (no model files exist here). Multi-GPU: one process per GPU,
-each converting and multiplying its N-slab of every weight, then an NCCL
-all-gather of the output slabs.
+activation pack (K2) of each distinct input, then one grouped GEMM launch
+(K3) per input (q+k+v, o, gate+up, down), weights converted once beforehand
+(K1), as the reference converts them at load. Inputs are seeded synthetic
+tensors with the configs' shapes and distributions (no model files exist
+here). --workload picks BASELINE's configs: qwen3-4b-layer (the default,
+configs[1]), single-q8_0, qwen3-4b-model (configs[2], a whole
+36-layer prefill in tok/s), 27b-layer-m8192/m2048 and
+lfm-m1024..16384 (configs[4]).
+
+Multi-GPU (one process per GPU under torchrun, NCCL): --mode tokens (the
+default) gives every rank its own prompt chunk, no collective; nshard /
+nshard-nogather split every weight's rows with / without the all-gather of
+the output slabs; tp runs the layer as one tensor-parallel block (o/down
+K-sharded, one all-reduce of their partials, by NCCL or by the GEMM itself
+through NVLink multicast).
 
 --impl reference times the reference's own CPU path (xdna_ref_mul_mat,
 oracle/_ref, compiled from the reference sources) on the host cores.

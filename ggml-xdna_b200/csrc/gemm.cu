@@ -27,6 +27,13 @@
 //               output rows)
 // The tile loop walks up to 4 weights sharing A (q, k, v; gate, up) as one
 // space of N tiles: a grouped launch is one kernel, no tails between them.
+// The walk's order (rows, columns or groups of 8 M blocks) is chosen per
+// launch to keep the re-read operand in L2. A second instance,
+// <BN_T, true>, adds stream-K: the last wave's tiles cut into runs of
+// k-blocks across all pairs, partial sums through a per-CTA workspace
+// (used by default for K >= 8192). The epilogue also fuses the residual ADD,
+// SwiGLU's packed output for the next GEMM, and, for tensor-parallel
+// partials, multimem.red into an NVLink multicast buffer.
 //
 // gemm_bf16_tc_kernel (M <= 128, and ZEST_GEMM_PAIR=0): one CTA on a 128x256
 // tile, 192 threads: warp 0 TMA, warp 1 TMEM + MMA (M=128, N=256), warps 2-5
