@@ -286,3 +286,53 @@ def test_piece_plan_folds_the_block_ops(h):
     p = h.piece_plan(nodes)
     assert (p["groups"], p["norm"], p["rope"]) == (1, 1, 1), p
     assert p["jobs"] == 1
+
+
+def test_piece_plan_leaves_unsafe_folds_alone(h):
+    # what the plan must NOT fold: a residual ADD that is not the matmul's
+    # next node, or whose other operand is a bias row, or is computed after
+    # the matmul; a norm feeding a matmul in host memory; a SwiGLU whose
+    # result another op reads too
+    k, n, t = 2048, 2048, 2048
+    C, W, Hm = h.buffer(USAGE_COMPUTE), h.buffer(USAGE_WEIGHTS), h.buffer(USAGE_COMPUTE, host=True)
+    base = 0x7d0000000000
+    addr = iter(range(base, base + (256 << 30), 1 << 30))
+
+    def T(type_, ne, name, buf=C, **kw):
+        return h.tensor(type_, ne, name, buf, next(addr), **kw)
+
+    def plan(nodes):
+        for nd in nodes:
+            h.supports_op(nd)
+        return h.piece_plan(nodes)
+
+    x = T(F32, [k, t], "x")
+    r = T(F32, [n, t], "resid")
+    mm = h.mul_mat(T(Q4_K, [k, n], "w", W), x, "mm", C, next(addr))
+    other = h.scale(x, 2.0, name="between", buffer=C, data=next(addr))
+    add = h.add(mm, r, name="out", buffer=C, data=next(addr))
+    assert plan([mm, other, add])["add"] == 0, "a node between the matmul and its ADD"
+    assert plan([mm, add])["add"] == 1
+
+    mm2 = h.mul_mat(T(Q4_K, [k, n], "w2", W), x, "mm2", C, next(addr))
+    bias = h.add(mm2, T(F32, [n], "bias", W), name="biased", buffer=C, data=next(addr))
+    assert plan([mm2, bias])["add"] == 0, "a bias row is a small op of its own"
+
+    mm3 = h.mul_mat(T(Q4_K, [k, n], "w3", W), x, "mm3", C, next(addr))
+    late = h.scale(T(F32, [n, t], "y"), 1.0, name="late", buffer=C, data=next(addr))
+    add3 = h.add(mm3, late, name="out3", buffer=C, data=next(addr))
+    assert plan([mm3, late, add3])["add"] == 0, "a residual computed after the matmul"
+
+    xh = T(F32, [k, t], "x_host", Hm)
+    nrm = h.rms_norm(xh, name="norm_h", buffer=Hm, data=next(addr))
+    mmh = h.mul_mat(T(Q4_K, [k, n], "w4", W), nrm, "mm_h", C, next(addr))
+    assert plan([nrm, mmh])["norm"] == 0, "operands in host memory take the staged route"
+
+    f = 5632
+    g = h.mul_mat(T(Q4_K, [k, f], "gate", W), x, "g", C, next(addr))
+    u = h.mul_mat(T(Q4_K, [k, f], "up", W), x, "u", C, next(addr))
+    s = h.glu(g, u, kind=2, name="s", buffer=C, data=next(addr))
+    d = h.mul_mat(T(Q4_K, [f, k], "down", W), s, "d", C, next(addr))
+    extra = h.scale(s, 0.5, name="s_read_too", buffer=C, data=next(addr))
+    p = plan([g, u, s, d, extra])
+    assert p["swiglu"] == 1 and p["handoff"] == 0, "the SwiGLU is read by another op: written in f32"
