@@ -201,12 +201,8 @@ struct budget_t {
 };
 budget_t g_budget;
 
-bool budget_takes(const ggml_tensor *w) {
-    if (!w->buffer || !w->data || ggml_backend_buffer_get_usage(w->buffer) != GGML_BACKEND_BUFFER_USAGE_WEIGHTS)
-        return true;
-    budget_t &b = g_budget;
-    std::lock_guard<std::mutex> lk(b.mu);
-    if (b.contexts == 0) return true;
+// The decision for one weight against budget b (its lock held).
+bool budget_decide(budget_t &b, const ggml_tensor *w) {
     const wkey key = { w->buffer, w->data, (int) w->type, w->ne[0], w->ne[1] };
     if (b.in.count(key)) return true;
     if (b.out.count(key)) return false;
@@ -251,6 +247,14 @@ bool budget_takes(const ggml_tensor *w) {
     }
     b.out[key] = e;
     return false;
+}
+
+bool budget_takes(const ggml_tensor *w) {
+    if (!w->buffer || !w->data || ggml_backend_buffer_get_usage(w->buffer) != GGML_BACKEND_BUFFER_USAGE_WEIGHTS)
+        return true;
+    std::lock_guard<std::mutex> lk(g_budget.mu);
+    if (g_budget.contexts == 0) return true;
+    return budget_decide(g_budget, w);
 }
 
 // ---------------------------------------------------------------------------
@@ -1341,6 +1345,27 @@ int ggml_zest_piece_groups(ggml_cgraph *cgraph, int *sizes, int max_groups) {
     const auto groups = find_groups(nodes, none);
     for (int i = 0; i < (int) groups.size() && i < max_groups; i++) sizes[i] = (int) groups[i].size();
     return (int) groups.size();
+}
+
+int ggml_zest_budget_plan(double limit_gb, const ggml_tensor *const *weights, int n, int *taken) {
+    budget_t b;
+    b.started = true;
+    b.limit = limit_gb * GB;
+    int count = 0;
+    for (int i = 0; i < n; i++) {
+        taken[i] = budget_decide(b, weights[i]) ? 1 : 0;
+        count += taken[i];
+    }
+    // a weight taken before the cut but whose layer the cut gave back
+    for (int i = 0; i < n; i++) {
+        const ggml_tensor *w = weights[i];
+        const wkey key = { w->buffer, w->data, (int) w->type, w->ne[0], w->ne[1] };
+        if (taken[i] && !b.in.count(key)) {
+            taken[i] = 0;
+            count--;
+        }
+    }
+    return count;
 }
 
 int ggml_zest_piece_plan(ggml_cgraph *cgraph, int *counts) {

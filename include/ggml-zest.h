@@ -46,6 +46,16 @@ __attribute__((visibility("default"))) int ggml_zest_piece_fusions(struct ggml_c
 __attribute__((visibility("default"))) int ggml_zest_piece_groups(struct ggml_cgraph *cgraph, int *sizes,
                                                                   int max_groups);
 
+/* The weight-copy budget's answers for these weights asked in this order
+ * under a limit of limit_gb (GGML_XDNA_MAX_COPY_GB): taken[i] = 1 where the
+ * weight's copy is made. Once a weight does not fit, its whole layer (by the
+ * "blk.N." name) stays on the GPU backend with every later one
+ * (src/ggml-zest.cpp:466-564). Returns how many are taken. Host logic only;
+ * for tests. */
+__attribute__((visibility("default"))) int ggml_zest_budget_plan(double limit_gb,
+                                                                 const struct ggml_tensor *const *weights, int n,
+                                                                 int *taken);
+
 /* The plan graph_compute makes for this piece: returns the number of matmul
  * service calls and writes counts[0..5]: fused SwiGLUs, grouped matmul
  * calls, RMS_NORMs folded into a pack, residual ADDs folded into a GEMM

@@ -99,6 +99,7 @@ class Harness:
         self.plugin.ggml_zest_policy_supports.argtypes = [ctypes.POINTER(Tensor)]
         self.plugin.ggml_zest_piece_fusions.argtypes = [_vp]
         self.plugin.ggml_zest_piece_plan.argtypes = [_vp, ctypes.POINTER(ctypes.c_int)]
+        self.plugin.ggml_zest_budget_plan.argtypes = [ctypes.c_double, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         self.plugin.ggml_zest_piece_groups.argtypes = [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
         # ctypes objects the C side points at, kept for the whole process: the
         # plugin remembers who read each tensor by address (as the reference
@@ -118,6 +119,14 @@ class Harness:
         c = (ctypes.c_int * 6)()
         jobs = self.plugin.ggml_zest_piece_plan(self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp)), c)
         return dict(jobs=jobs, swiglu=c[0], groups=c[1], norm=c[2], add=c[3], handoff=c[4], rope=c[5])
+
+    def budget_plan(self, limit_gb: float, weights: list[Tensor]) -> list[int]:
+        """The weight-copy budget's answers for these weights, asked in order."""
+        arr = (ctypes.POINTER(Tensor) * len(weights))(*[ctypes.pointer(w) for w in weights])
+        self.keep.append(arr)
+        taken = (ctypes.c_int * len(weights))()
+        self.plugin.ggml_zest_budget_plan(limit_gb, ctypes.cast(arr, _vp), len(weights), taken)
+        return list(taken)
 
     def piece_groups(self, nodes: list[Tensor]) -> list[int]:
         arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])

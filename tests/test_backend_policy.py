@@ -336,3 +336,21 @@ def test_piece_plan_leaves_unsafe_folds_alone(h):
     extra = h.scale(s, 0.5, name="s_read_too", buffer=C, data=next(addr))
     p = plan([g, u, s, d, extra])
     assert p["swiglu"] == 1 and p["handoff"] == 0, "the SwiGLU is read by another op: written in f32"
+
+
+def test_budget_cuts_whole_layers(h):
+    # the reference's tests/test-memory-budget.cpp: weight copies fill the
+    # budget in the order they are asked for; the first weight that does not
+    # fit sends its whole layer back, and every later weight stays on the GPU
+    # backend. Each 2048 x 2048 copy takes 2048 * 2048 * (9/8 + 2) bytes = 13.1 MB.
+    W = h.buffer(USAGE_WEIGHTS)
+    base = 0x7c0000000000
+    ws = [h.tensor(Q4_K, [2048, 2048], f"blk.{i // 3}.ffn_{('gate', 'up', 'down')[i % 3]}.weight", W,
+                   base + (i << 30)) for i in range(12)]
+    # 7 copies fit in 0.1 GB: layer 2 is cut at its second weight, and its first goes back
+    assert h.budget_plan(0.1, ws) == [1] * 6 + [0] * 6
+    assert h.budget_plan(1.0, ws) == [1] * 12
+    assert h.budget_plan(0.0, ws) == [0] * 12
+    # a weight without a layer in its name (the output head) is cut alone
+    head = h.tensor(Q4_K, [2048, 2048], "output.weight", W, base + (40 << 30))
+    assert h.budget_plan(0.03, [ws[0], ws[1], head]) == [1, 1, 0]
