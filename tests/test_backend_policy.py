@@ -106,7 +106,8 @@ def test_mul_mat_id_not_claimed(h):
 
 def test_supports_op_needs_a_usable_gpu(h):
     # supports_op = a usable GPU (start-up self-test) and the policy; without
-    # a GPU no device is offered and nothing is claimed
+    # a GPU the plugin still registers but no device is offered and nothing
+    # is claimed (tests/test-safe-start.cpp:20-38, its --no-driver case)
     try:
         import torch
         gpu = torch.cuda.is_available()

@@ -131,3 +131,30 @@ def test_failure_is_sticky():
     assert f"status {STATUS_FAILED}" in r.stdout
     assert "after False" in r.stdout, "after a failure the backend claims nothing"
     assert "claiming nothing from now on" in r.stderr
+
+
+def test_no_device_when_the_gpu_cannot_run():
+    """tests/test-safe-start.cpp:20-38: when the device cannot run the path,
+    the plugin still registers but offers no device, so it claims nothing.
+    The reference simulates it with a kernel path that names nothing; here
+    the CUDA device index names no device, which fails the same start-up
+    check a missing GPU or a non-B200 one does."""
+    here = os.path.dirname(__file__)
+    code = textwrap.dedent(f"""
+        import sys
+        sys.path[:0] = [{os.path.join(here, 'ggml_harness')!r}, {os.path.dirname(here)!r}]
+        from harness import *
+        h = Harness()
+        print("reg", h.reg_name())
+        print("devices", h.device_count())
+        x = h.tensor(F32, [2048, 2048], buffer=h.buffer(USAGE_COMPUTE))
+        w = h.tensor(Q4_K, [2048, 2048], buffer=h.buffer(USAGE_WEIGHTS))
+        print("policy", h.policy(h.mul_mat(w, x)))
+    """)
+    env = dict(os.environ, GGML_ZEST_CUDA_DEVICE="64")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "reg XDNA" in r.stdout, "the plugin loads"
+    assert "devices 0" in r.stdout, "no device offered"
+    assert "policy True" in r.stdout, "the host-side policy alone would take the matmul"
+    assert "not offering" in r.stderr and "no such CUDA device" in r.stderr
