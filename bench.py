@@ -485,7 +485,7 @@ def run_ours(args, w: dict) -> None:
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["tflops_sustained"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["tflops_sustained"],
                          "traffic": traffic,
-                         "kernel": "k3 gemm_bf16_tc_pair_kernel<256> (the stream-K instance when K >= 8192)",
+                         "kernel": "k3 gemm_bf16_tc_pair_kernel<256> (the stream-K instance at K >= 8192 with a full wave, or a quarter of the pair-slots idle at K >= 4096)",
                          "launch": f"{top_desc}: {top_flops / 1e9:.1f} GFLOP, {gemm_ms[top] * 1e3:.1f} us avg",
                          "peak_kind": f"bf16 sustained ({peaks['source']})", "peak_burst": peaks["tflops_burst"],
                          "all_gemms": {"ms_per_step": gemm_total_ms,

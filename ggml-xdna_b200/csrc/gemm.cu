@@ -451,6 +451,7 @@ struct pair_params {
     int tile0[MAX_SEG + 1];    // first N tile of each segment; tile0[nseg] = all N tiles
     int nseg, num_m, num_n, num_k;
     int raster;                // RASTER_*
+    int stream_hint;           // the streamed operand's loads carry an evict-first L2 hint
     // stream-K: tiles [0, dp_tiles) run whole, one per pair per wave; the
     // sk_tiles after them are cut into runs of sk_q k-blocks, pair p taking
     // [p * sk_q, (p + 1) * sk_q) of their (tile, k-block) space
@@ -468,17 +469,29 @@ struct pair_params {
 // across streams by the launcher.
 constexpr int SK_SLOTS = 160;
 constexpr int SK_SLOT_FLOATS = 128 * 256;
+// A CTA's partial tile in the workspace, in the order the epilogue holds it:
+// warp q, 32-column chunk ch, 4-column group g, then the warp's 32 lanes (one
+// row each), four floats apiece. Each float4 access of a warp is then 512
+// contiguous bytes; the writer and the reader of a slot share (q, lane) for
+// every row, as both are the same rank of their pair.
+__device__ __forceinline__ size_t sk_off(int q, int ch, int g, int lane) {
+    return ((size_t) ((q * 8 + ch) * 8 + g) * 32 + lane) * 4;
+}
 __device__ float g_sk_part[SK_SLOTS * SK_SLOT_FLOATS];
 __device__ int g_sk_flag[SK_SLOTS];
 
-// The runs of one pair: its whole tiles, then its stretch of the stream-K
-// space one (tile, k-block range) at a time, from the END of the stretch
-// back to its start. So a pair first computes the run that stops inside a
-// tile (whose partial sum another pair waits for) and publishes it, and only
-// then the run that finishes a tile started by the pair before it: no pair
-// waits on a pair that is itself waiting.
+// The runs of one pair. Its stretch of the stream-K space is walked one
+// (tile, k-block range) at a time from the END back to its start, so the
+// run that stops inside a tile (whose partial sum another pair waits for)
+// comes before the run that finishes a tile started by the pair before it:
+// no pair waits on a pair that is itself waiting. That first stream-K run
+// goes ahead of the pair's whole tiles, so every partial is published at the
+// start of the launch and a short run never follows a whole tile directly
+// (the MMAs of the run after it would wait for that tile's epilogue to free
+// its accumulator).
 struct unit_iter {
     int i = 0;
+    bool lead = true;        // the stretch's first run is still to come, ahead of the whole tiles
     int64_t u0 = 0, u1 = 0;  // the stretch still to walk, [u0, u1)
     __device__ unit_iter(const pair_params &pp, int pair) {
         const int64_t end = (int64_t) pp.sk_tiles * pp.num_k;
@@ -487,6 +500,10 @@ struct unit_iter {
         if (u0 > u1) u0 = u1;
     }
     __device__ bool next(const pair_params &pp, int pair, int npairs, int &t, int &kb0, int &kb1) {
+        if (lead) {
+            lead = false;
+            if (u1 > u0) return take(pp, t, kb0, kb1);
+        }
         const int td = pair + i * npairs;
         if (td < pp.dp_tiles) {
             i++;
@@ -496,6 +513,10 @@ struct unit_iter {
             return true;
         }
         if (u1 <= u0) return false;
+        return take(pp, t, kb0, kb1);
+    }
+    // the last (tile, k-block range) of what is left of the stretch
+    __device__ bool take(const pair_params &pp, int &t, int &kb0, int &kb1) {
         const int64_t st = (u1 - 1) / pp.num_k, ts = st * pp.num_k;
         const int64_t start = u0 > ts ? u0 : ts;
         t = pp.dp_tiles + (int) st;
@@ -596,6 +617,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t armed = 0, armed_phase = 0;
             bool ok = true;
             const uint64_t pol = l2_evict_first_policy();
+            const bool hint_a = pp.stream_hint && pp.raster == RASTER_ROWS;
+            const bool hint_b = pp.stream_hint && pp.raster != RASTER_ROWS;
             unit_iter it(pp, pair);
             int t, kb0, kb1;
             while (ok && it.next(pp, pair, npairs, t, kb0, kb1)) {
@@ -612,11 +635,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t bar = map_to_rank(&full[stage], 0);
                     uint8_t *sa = smem + stage * P_STAGE_BYTES;
                     // the operand this raster streams is read once: evict-first
-                    if (pp.raster == RASTER_ROWS)
+                    if (hint_a)
                         tma_load_2d_pair_hint(sa, &tmA, bar, kb * BK, mb * P_BM + (int) rank * 128, pol);
                     else
                         tma_load_2d_pair(sa, &tmA, bar, kb * BK, mb * P_BM + (int) rank * 128);
-                    if (pp.raster != RASTER_ROWS)
+                    if (hint_b)
                         tma_load_2d_pair_hint(sa + P_A_BYTES, &maps.b[seg], bar, kb * BK,
                                               nb * P_BN + (int) rank * (P_BN / 2), pol);
                     else
@@ -726,13 +749,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t tbase = tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * ACC_COLS);
             uint32_t r[32];
             for (int ch = 0; ch < P_BN / 32; ch++) {
-                // the residual's loads go out before the TMEM load, so their
-                // latency overlaps it (the aligned, full-width case)
+                // the residual's loads (or, finishing a stream-K tile, the
+                // first partial's) go out before the TMEM load, so their
+                // latency overlaps it
                 float4 rr[8];
                 const int64_t rcol0 = (int64_t) nb * P_BN + ch * 32;
                 const bool rfast = p.resid && p.tma_store && row < p.M && rcol0 + 32 <= p.n_out &&
                                    (p.ldr % 4) == 0 && ((uintptr_t) p.resid & 15) == 0;
-                if (rfast) {
+                const bool sum_in = fin && !dead;
+                if (sum_in) {
+                    const float *src = g_sk_part + (size_t) (2 * j0 + rank) * SK_SLOT_FLOATS;
+#pragma unroll
+                    for (int g = 0; g < 8; g++) rr[g] = *reinterpret_cast<const float4 *>(src + sk_off(q, ch, g, lane));
+                } else if (rfast) {
                     const float4 *src = reinterpret_cast<const float4 *>(p.resid + row * p.ldr + rcol0);
 #pragma unroll
                     for (int i = 0; i < 8; i++) rr[i] = src[i];
@@ -744,27 +773,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     mbar_arrive_cluster(tempty_leader[acc]);
                 }
                 if (part) {
-                    float *dst = g_sk_part + (size_t) blockIdx.x * SK_SLOT_FLOATS + row_local * 256 + ch * 32;
+                    float *dst = g_sk_part + (size_t) blockIdx.x * SK_SLOT_FLOATS;
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4 *>(dst + i) = make_float4(
-                            __uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
-                            __uint_as_float(r[i + 3]));
+                    for (int g = 0; g < 8; g++)
+                        *reinterpret_cast<float4 *>(dst + sk_off(q, ch, g, lane)) = make_float4(
+                            __uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]), __uint_as_float(r[4 * g + 2]),
+                            __uint_as_float(r[4 * g + 3]));
                     continue;
                 }
-                if (fin && !dead)
+                if (sum_in) {
                     for (int j = j0; j < pair; j++) {
-                        const float *src =
-                            g_sk_part + (size_t) (2 * j + rank) * SK_SLOT_FLOATS + row_local * 256 + ch * 32;
+                        if (j > j0) {
+                            const float *src = g_sk_part + (size_t) (2 * j + rank) * SK_SLOT_FLOATS;
 #pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            const float4 v = *reinterpret_cast<const float4 *>(src + i);
-                            r[i] = __float_as_uint(__uint_as_float(r[i]) + v.x);
-                            r[i + 1] = __float_as_uint(__uint_as_float(r[i + 1]) + v.y);
-                            r[i + 2] = __float_as_uint(__uint_as_float(r[i + 2]) + v.z);
-                            r[i + 3] = __float_as_uint(__uint_as_float(r[i + 3]) + v.w);
+                            for (int g = 0; g < 8; g++)
+                                rr[g] = *reinterpret_cast<const float4 *>(src + sk_off(q, ch, g, lane));
+                        }
+#pragma unroll
+                        for (int g = 0; g < 8; g++) {
+                            r[4 * g] = __float_as_uint(__uint_as_float(r[4 * g]) + rr[g].x);
+                            r[4 * g + 1] = __float_as_uint(__uint_as_float(r[4 * g + 1]) + rr[g].y);
+                            r[4 * g + 2] = __float_as_uint(__uint_as_float(r[4 * g + 2]) + rr[g].z);
+                            r[4 * g + 3] = __float_as_uint(__uint_as_float(r[4 * g + 3]) + rr[g].w);
                         }
                     }
+                    if (rfast) {
+                        // the residual after the partials (it is in L2: prefetched at the tile's start)
+                        const float4 *src = reinterpret_cast<const float4 *>(p.resid + row * p.ldr + rcol0);
+#pragma unroll
+                        for (int i = 0; i < 8; i++) rr[i] = src[i];
+                    }
+                }
                 const int64_t col0 = (int64_t) nb * P_BN + ch * 32;
                 if (col0 >= p.N) continue;
                 if (!p.tma_store && !p.c_mc) {
@@ -938,20 +977,31 @@ int num_sms() {
 
 // Stream-K plan: when the last wave of whole tiles would leave pairs idle,
 // that wave and the full wave before it are cut into equal runs of k-blocks,
-// one run per pair. Not when the last wave is nearly full (the partial sums
-// cost more than the idle pairs), nor for runs under 4 k-blocks, and by
-// default only for K >= 8192: measured on the configs' shapes, a split
-// tile's extra epilogue costs more than the idle pairs save at K <= 4096
-// (C1 53 -> 61 us, C3 q+k+v 55 -> 63 us), while the long-K down projections
-// gain (C3 down 112 -> 93 us, C2 down 295 -> 277 us). ZEST_GEMM_SK=1 splits
-// at any K, ZEST_GEMM_SK=0 never.
+// one run per pair. By default only where a quarter or more of the launch's
+// pair-slots would sit idle and K is 4096 or more, or K is 8192 or more and
+// there is at least one full wave: measured on the configs' shapes (device
+// time per launch, whole tiles -> stream-K), C3 o 51 -> 46 us (idle 0.46, 64
+// k-blocks), C3 down 104 -> 80 (0.46), C5 M=1024 down 61 -> 54 (0.57), C4
+// M=2048 down 327 -> 281 (0.28), C2 down about 330 -> 292 (0.14, 152
+// k-blocks, mean of 5 runs); while C1 (0.32 idle but 40 k-blocks) 51 -> 54,
+// C5 M=2048 down (one wave of 64 tiles, 0.14 idle) 66 -> 74, and the shorter
+// launches with less idle lose 2-10 %: each split tile adds an exposed
+// epilogue, and under the power cap the busy pairs of a ragged wave run at
+// higher clocks.
+// ZEST_GEMM_SK=1 splits whenever the shape allows, ZEST_GEMM_SK=0 never.
 bool plan_stream_k(pair_params &pp, int64_t tiles, int pairs) {
     static const int mode = [] {
         const char *s = getenv("ZEST_GEMM_SK");
         return s && s[0] == '1' ? 1 : (s && s[0] == '0' ? 0 : 2);
     }();
+    if (mode == 0) return false;
+    if (mode == 2) {
+        const int64_t slots = (tiles + pairs - 1) / pairs * pairs;
+        const bool ragged = pp.num_k >= 64 && 4 * (slots - tiles) >= slots;
+        const bool long_k = pp.num_k >= 128 && tiles >= pairs;
+        if (!ragged && !long_k) return false;
+    }
     const int64_t full = tiles / pairs, rem = tiles % pairs;
-    if (mode == 0 || (mode == 2 && pp.num_k < 128)) return false;
     if (rem == 0 || 2 * pairs > SK_SLOTS || rem > (pairs * 7) / 8) return false;
     if (full == 0 && rem < 2) return false;
     const int64_t sk_tiles = rem + (full >= 1 ? pairs : 0);
@@ -1092,6 +1142,11 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
         pp.sk_tiles = 0;
         pp.sk_q = 0;
     }
+    // A stream-K launch's runs start at staggered k offsets, so a panel of
+    // the streamed operand is read by its tiles at different times: it stays
+    // in L2 without the evict-first hint (ZEST_GEMM_HINT=0/1 forces it).
+    pp.stream_hint = !sk;
+    if (const char *h = getenv("ZEST_GEMM_HINT")) pp.stream_hint = h[0] == '1';
     // stream-K spreads even a small launch over every pair
     const int pairs = sk ? max_pairs : (int) (tiles < max_pairs ? tiles : max_pairs);
     cudaLaunchConfig_t cfg = {};

@@ -232,6 +232,22 @@ got = host(Z.gemm(ah, gu, M, n, 2))
 idx = np.arange(F)
 at = (idx // 8) * 16 + idx % 8
 ok &= same_up_to_sum_order(got[:, :F], O.swiglu_bf16(acc[:, at], acc[:, at + 8]), rounded=True)
+# the residual ADD on completed sums: the same split as the plain launch, so
+# the sum order matches and the result is the plain one plus the residual
+import ctypes
+M, N, K = 2048, 2560, 4096
+_, bh = Z.convert_weight(O.Q8_0, dev(O.quantize(O.Q8_0, O.weights_f32(N, K, 14))), N, K)
+_, ah = Z.pack_activations(dev(O.activations(M, K, 15)))
+resid = torch.randn((M, N), device="cuda", generator=torch.Generator("cuda").manual_seed(16))
+c = torch.empty((M, N), device="cuda")
+err = torch.zeros(1, dtype=torch.int32, device="cuda")
+seg = (Z.GemmSeg * 1)(Z.GemmSeg(bh.data_ptr(), K, N, Z.MODE_BF16, c.data_ptr(), N, resid.data_ptr(), N, None, 0))
+L = Z.lib()
+rc = L.zest_gemm_segs(ctypes.c_void_p(ah.data_ptr()), K, M, K, 1, seg, ctypes.c_void_p(err.data_ptr()),
+                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+assert rc == 0, L.zest_last_error().decode()
+plain = host(Z.gemm(ah, bh, M, N, Z.MODE_BF16))
+ok &= bool(np.array_equal(host(c), host(resid) + plain)) and int(err.item()) == 0
 print("STREAMK", "OK" if ok else "DIFFER")
 """
 
