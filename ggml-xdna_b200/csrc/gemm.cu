@@ -747,11 +747,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int row_local = q * 32 + lane;
             const int64_t row0 = (int64_t) mb * P_BM + rank * 128 + q * 32, row = row0 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * ACC_COLS);
-            uint32_t r[32];
+            // each chunk's TMEM load goes out while the chunk before it is
+            // stored, so its latency overlaps that work
+            uint32_t r[32], nx[32];
+            tmem_ld_32x32b_x32(tbase, nx);
             for (int ch = 0; ch < P_BN / 32; ch++) {
                 // the residual's loads (or, finishing a stream-K tile, the
-                // first partial's) go out before the TMEM load, so their
-                // latency overlaps it
+                // first partial's) go out before the wait for this chunk
                 float4 rr[8];
                 const int64_t rcol0 = (int64_t) nb * P_BN + ch * 32;
                 const bool rfast = p.resid && p.tma_store && row < p.M && rcol0 + 32 <= p.n_out &&
@@ -766,8 +768,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int i = 0; i < 8; i++) rr[i] = src[i];
                 }
-                tmem_ld_32x32b_x32(tbase + (uint32_t) (ch * 32), r);
-                tmem_ld_wait();
+                tmem_ld_wait(nx);
+#pragma unroll
+                for (int i = 0; i < 32; i++) r[i] = nx[i];
+                if (ch + 1 < P_BN / 32) tmem_ld_32x32b_x32(tbase + (uint32_t) ((ch + 1) * 32), nx);
                 if (ch == P_BN / 32 - 1) {
                     tc_fence_before();
                     mbar_arrive_cluster(tempty_leader[acc]);
