@@ -595,6 +595,28 @@ int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x,
     return zest_mul_mat_group(npu, 1, key, &fused, x, T, ys, on_device);
 }
 
+int zest_plan_gemm(int64_t M, int64_t K, int n, const int64_t *N, int sms, zest_gemm_plan *out) {
+    if (!out || !N || n <= 0 || n > 4 || M <= 0 || K <= 0)
+        return set_error("zest_plan_gemm: 1 to 4 weights, M and K positive, and an output");
+    for (int i = 0; i < n; i++)
+        if (N[i] <= 0) return set_error("zest_plan_gemm: every weight needs rows");
+    gemm_plan gp;
+    plan_gemm(M, K, n, N, sms, gp);
+    out->pair_kernel = gp.pair;
+    out->tile_n = gp.bn;
+    out->tiles_m = gp.num_m;
+    out->tiles_n = gp.num_n;
+    out->k_blocks = gp.num_k;
+    out->tiles = gp.tiles;
+    out->ctas = gp.ctas;
+    out->raster = gp.raster;
+    out->stream_k = gp.stream_k;
+    out->whole_tiles = gp.dp_tiles;
+    out->split_tiles = gp.sk_tiles;
+    out->run_k_blocks = gp.sk_q;
+    return 0;
+}
+
 int zest_gemm_segs(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int n, const zest_gemm_seg *segs,
                    unsigned *err, void *stream) {
     if (n <= 0 || n > 4 || !segs) return set_error("zest_gemm_segs: 1 to 4 weights");

@@ -993,7 +993,8 @@ int num_sms() {
 // epilogue, and under the power cap the busy pairs of a ragged wave run at
 // higher clocks.
 // ZEST_GEMM_SK=1 splits whenever the shape allows, ZEST_GEMM_SK=0 never.
-bool plan_stream_k(pair_params &pp, int64_t tiles, int pairs) {
+bool plan_stream_k(gemm_plan &gp, int pairs) {
+    const int64_t tiles = gp.tiles;
     static const int mode = [] {
         const char *s = getenv("ZEST_GEMM_SK");
         return s && s[0] == '1' ? 1 : (s && s[0] == '0' ? 0 : 2);
@@ -1001,19 +1002,19 @@ bool plan_stream_k(pair_params &pp, int64_t tiles, int pairs) {
     if (mode == 0) return false;
     if (mode == 2) {
         const int64_t slots = (tiles + pairs - 1) / pairs * pairs;
-        const bool ragged = pp.num_k >= 64 && 4 * (slots - tiles) >= slots;
-        const bool long_k = pp.num_k >= 128 && tiles >= pairs;
+        const bool ragged = gp.num_k >= 64 && 4 * (slots - tiles) >= slots;
+        const bool long_k = gp.num_k >= 128 && tiles >= pairs;
         if (!ragged && !long_k) return false;
     }
     const int64_t full = tiles / pairs, rem = tiles % pairs;
     if (rem == 0 || 2 * pairs > SK_SLOTS || rem > (pairs * 7) / 8) return false;
     if (full == 0 && rem < 2) return false;
     const int64_t sk_tiles = rem + (full >= 1 ? pairs : 0);
-    const int64_t q = (sk_tiles * pp.num_k + pairs - 1) / pairs;
+    const int64_t q = (sk_tiles * gp.num_k + pairs - 1) / pairs;
     if (q < 4) return false;
-    pp.dp_tiles = (int) ((full >= 1 ? full - 1 : 0) * pairs);
-    pp.sk_tiles = (int) sk_tiles;
-    pp.sk_q = q;
+    gp.dp_tiles = (int) ((full >= 1 ? full - 1 : 0) * pairs);
+    gp.sk_tiles = (int) sk_tiles;
+    gp.sk_q = q;
     return true;
 }
 
@@ -1067,8 +1068,8 @@ void sk_release(cudaStream_t st) {
 // B's tensor maps (BN_T/2-row boxes, one per CTA), the outputs' for TMA
 // stores, a cluster-of-2 launch.
 template <int BN_T>
-int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, const gemm_seg *segs, unsigned *err_flag,
-                      cudaStream_t st) {
+int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, const gemm_seg *segs, const gemm_plan &gp,
+                      unsigned *err_flag, cudaStream_t st) {
     using C = pair_cfg<BN_T>;
     pair_maps maps;
     pair_params pp;
@@ -1077,8 +1078,8 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
     pp.nseg = nseg;
     pp.M = M;
     pp.err = err_flag;
-    pp.num_m = (int) ((M + P_BM - 1) / P_BM);
-    pp.num_k = (int) ((K + BK - 1) / BK);
+    pp.num_m = gp.num_m;
+    pp.num_k = gp.num_k;
     int tiles_n = 0;
     for (int s = 0; s < nseg; s++) {
         const gemm_seg &g = segs[s];
@@ -1106,18 +1107,7 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
     }
     pp.tile0[nseg] = tiles_n;
     pp.num_n = tiles_n;
-    // keep the re-read operand within about half of the 126 MB L2 (the rest
-    // holds the streamed operand's tiles and the outputs on their way out)
-    const double l2_budget = 60e6, a_bytes = 2.0 * (double) M * (double) K;
-    double b_bytes = 0;
-    for (int s = 0; s < nseg; s++) b_bytes += 2.0 * (double) segs[s].N * (double) K;
-    pp.raster = b_bytes <= l2_budget && b_bytes <= a_bytes ? RASTER_ROWS
-                : a_bytes <= l2_budget                     ? RASTER_COLS
-                                                           : RASTER_GROUPS;
-    if (const char *force = getenv("ZEST_GEMM_RASTER")) {
-        const int f = atoi(force);
-        if (f >= RASTER_GROUPS && f <= RASTER_COLS) pp.raster = f;
-    }
+    pp.raster = gp.raster;
     {
         // a function attribute holds per device: set it once on each
         static std::mutex mu;
@@ -1134,17 +1124,15 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
             if (dev < 64) set_on |= 1ull << dev;
         }
     }
-    const int64_t tiles = (int64_t) pp.num_m * pp.num_n;
-    const int max_pairs = num_sms() / 2;
-    pp.dp_tiles = (int) tiles;
+    pp.dp_tiles = (int) gp.tiles;
     pp.sk_tiles = 0;
     pp.sk_q = 0;
     pp.sk_epoch = 0;
-    const bool sk = plan_stream_k(pp, tiles, max_pairs) && sk_claim(st, &pp.sk_epoch);
-    if (!sk) {
-        pp.dp_tiles = (int) tiles;
-        pp.sk_tiles = 0;
-        pp.sk_q = 0;
+    const bool sk = gp.stream_k && sk_claim(st, &pp.sk_epoch);
+    if (sk) {
+        pp.dp_tiles = gp.dp_tiles;
+        pp.sk_tiles = gp.sk_tiles;
+        pp.sk_q = gp.sk_q;
     }
     // A stream-K launch's runs start at staggered k offsets, so a panel of
     // the streamed operand is read by its tiles at different times: it stays
@@ -1152,7 +1140,8 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
     pp.stream_hint = !sk;
     if (const char *h = getenv("ZEST_GEMM_HINT")) pp.stream_hint = h[0] == '1';
     // stream-K spreads even a small launch over every pair
-    const int pairs = sk ? max_pairs : (int) (tiles < max_pairs ? tiles : max_pairs);
+    const int max_pairs = num_sms() / 2;
+    const int pairs = sk ? max_pairs : (int) (gp.tiles < max_pairs ? gp.tiles : max_pairs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) (2 * pairs));
     cfg.blockDim = dim3(NUM_THREADS);
@@ -1241,30 +1230,83 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
                          ((uintptr_t) g.a_next & 15)))
             return set_error("gemm: the next operand needs SwiGLU, a width of 8s and 16-byte aligned rows");
     }
-    // The CTA-pair kernel unless ZEST_GEMM_PAIR=0 or the rows fit one 128-row tile.
-    const char *pair_env = getenv("ZEST_GEMM_PAIR");
-    const bool pair = M > BM && !(pair_env && pair_env[0] == '0');
+    int64_t Ns[MAX_SEG];
+    for (int s = 0; s < nseg; s++) Ns[s] = segs[s].N;
+    gemm_plan gp;
+    plan_gemm(M, K, nseg, Ns, 0, gp);
     CUtensorMap ta;
     if (!make_tmap(&ta, a_bf16, M, K, lda, BM)) return set_error("gemm: cannot build the TMA descriptors");
-    if (!pair) {
+    if (!gp.pair) {
         for (int s = 0; s < nseg; s++)
             if (launch_single(ta, M, K, segs[s], err_flag, st)) return -1;
         return 0;
     }
+    switch (gp.bn) {
+        case 192: return launch_pair_group<192>(ta, M, K, nseg, segs, gp, err_flag, st);
+        case 160: return launch_pair_group<160>(ta, M, K, nseg, segs, gp, err_flag, st);
+        case 128: return launch_pair_group<128>(ta, M, K, nseg, segs, gp, err_flag, st);
+        default: return launch_pair_group<256>(ta, M, K, nseg, segs, gp, err_flag, st);
+    }
+}
+
+void plan_gemm(int64_t M, int64_t K, int nseg, const int64_t *Ns, int sms, gemm_plan &gp) {
+    gp = gemm_plan{};
+    if (sms <= 0) sms = num_sms();
+    gp.num_k = (int) ((K + BK - 1) / BK);
+    // The CTA-pair kernel unless ZEST_GEMM_PAIR=0 or the rows fit one 128-row tile.
+    const char *pair_env = getenv("ZEST_GEMM_PAIR");
+    gp.pair = M > BM && !(pair_env && pair_env[0] == '0');
+    if (!gp.pair) {
+        // one launch per weight, each its own tiles in groups of 8 tile rows
+        gp.bn = BN;
+        gp.num_m = (int) ((M + BM - 1) / BM);
+        int64_t widest = 0;
+        for (int s = 0; s < nseg; s++) {
+            const int64_t n = (Ns[s] + BN - 1) / BN;
+            gp.num_n += (int) n;
+            widest = n > widest ? n : widest;
+        }
+        gp.tiles = (int64_t) gp.num_m * gp.num_n;
+        const int64_t most = (int64_t) gp.num_m * widest;
+        gp.ctas = (int) (most < sms ? most : sms);
+        gp.raster = RASTER_GROUPS;
+        gp.dp_tiles = (int) gp.tiles;
+        return;
+    }
     // 256-wide N tiles: measured on every shape of the configs, narrower
     // tiles lose 15-45 % per flop, more than they win back by rounding to
     // fewer waves. Narrower ones stay selectable for tests and tuning.
-    int bn = 256;
+    gp.bn = 256;
     if (const char *force = getenv("ZEST_GEMM_BN")) {
         const int f = atoi(force);
-        if (f == 192 || f == 160 || f == 128) bn = f;
+        if (f == 192 || f == 160 || f == 128) gp.bn = f;
     }
-    switch (bn) {
-        case 192: return launch_pair_group<192>(ta, M, K, nseg, segs, err_flag, st);
-        case 160: return launch_pair_group<160>(ta, M, K, nseg, segs, err_flag, st);
-        case 128: return launch_pair_group<128>(ta, M, K, nseg, segs, err_flag, st);
-        default: return launch_pair_group<256>(ta, M, K, nseg, segs, err_flag, st);
+    gp.num_m = (int) ((M + P_BM - 1) / P_BM);
+    for (int s = 0; s < nseg; s++) gp.num_n += (int) ((Ns[s] + gp.bn - 1) / gp.bn);
+    gp.tiles = (int64_t) gp.num_m * gp.num_n;
+    // keep the re-read operand within about half of the 126 MB L2 (the rest
+    // holds the streamed operand's tiles and the outputs on their way out)
+    const double l2_budget = 60e6, a_bytes = 2.0 * (double) M * (double) K;
+    double b_bytes = 0;
+    for (int s = 0; s < nseg; s++) b_bytes += 2.0 * (double) Ns[s] * (double) K;
+    gp.raster = b_bytes <= l2_budget && b_bytes <= a_bytes ? RASTER_ROWS
+                : a_bytes <= l2_budget                     ? RASTER_COLS
+                                                           : RASTER_GROUPS;
+    if (const char *force = getenv("ZEST_GEMM_RASTER")) {
+        const int f = atoi(force);
+        if (f >= RASTER_GROUPS && f <= RASTER_COLS) gp.raster = f;
     }
+    const int max_pairs = sms / 2;
+    gp.dp_tiles = (int) gp.tiles;
+    gp.stream_k = plan_stream_k(gp, max_pairs) ? 1 : 0;
+    if (!gp.stream_k) {
+        gp.dp_tiles = (int) gp.tiles;
+        gp.sk_tiles = 0;
+        gp.sk_q = 0;
+    }
+    // stream-K spreads even a small launch over every pair
+    const int64_t pairs = gp.stream_k ? max_pairs : (gp.tiles < max_pairs ? gp.tiles : max_pairs);
+    gp.ctas = (int) (2 * pairs);
 }
 
 int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,

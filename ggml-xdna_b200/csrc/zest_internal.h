@@ -53,6 +53,25 @@ struct gemm_seg {
     float *c_mc = nullptr;       // multicast address: results added into every GPU's copy (NVSwitch reduction)
 };
 
+// How K3 runs one launch: the kernel, its tiles, the order the persistent
+// CTAs walk them in, and the stream-K split of the last waves.
+struct gemm_plan {
+    int pair;                // 1: CTA pairs on 256-row tiles; 0: one CTA per 128-row tile
+    int bn;                  // output tile width
+    int num_m, num_n, num_k; // tile rows, tile columns (all weights end to end), 64-wide k-blocks
+    int64_t tiles;
+    int ctas;                // CTAs launched (the one-CTA kernel: per weight, at most)
+    int raster;              // 0: groups of 8 tile rows, 1: rows (A streamed), 2: columns (B streamed)
+    int stream_k;            // 1: the last waves are cut into runs of k-blocks
+    int dp_tiles, sk_tiles;  // tiles run whole; tiles cut into runs
+    int64_t sk_q;            // k-blocks per pair over the cut tiles
+};
+
+// The plan of a launch of A [M][K] against nseg weights of Ns rows each on
+// `sms` SMs (<= 0: this device's, capped by ZEST_GEMM_MAX_SMS). Reads the
+// tuning variables (ZEST_GEMM_PAIR, _BN, _RASTER, _SK) as the launch does.
+void plan_gemm(int64_t M, int64_t K, int nseg, const int64_t *Ns, int sms, gemm_plan &gp);
+
 // Up to 4 weights sharing one A (q, k and v; gate and up) in one launch.
 int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int nseg, gemm_seg *segs,
                       unsigned *err_flag, cudaStream_t st);

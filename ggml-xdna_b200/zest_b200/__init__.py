@@ -45,6 +45,13 @@ class GemmSeg(ctypes.Structure):
                 ("residual", _vp), ("ldr", _i64), ("a_next", _vp), ("lda_next", _i64), ("c_multicast", _vp)]
 
 
+class GemmPlan(ctypes.Structure):
+    """zest_gemm_plan: how K3 runs a launch."""
+    _fields_ = [("pair_kernel", _int), ("tile_n", _int), ("tiles_m", _int), ("tiles_n", _int), ("k_blocks", _int),
+                ("tiles", _i64), ("ctas", _int), ("raster", _int), ("stream_k", _int), ("whole_tiles", _int),
+                ("split_tiles", _int), ("run_k_blocks", _i64)]
+
+
 class MmOut(ctypes.Structure):
     """zest_mm_out: where one weight's result of zest_mul_mat_group_ex goes."""
     _fields_ = [("y", _vp), ("residual", _vp), ("a_next", _vp)]
@@ -76,6 +83,7 @@ def lib() -> ctypes.CDLL:
         "zest_gemm": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
         "zest_gemm_group": (_int, [_vp, _i64, _i64, _i64, _int, _vpp, _i64p, _i64p, _intp, _vpp, _i64p, _vp, _vp]),
         "zest_gemm_segs": (_int, [_vp, _i64, _i64, _i64, _int, ctypes.POINTER(GemmSeg), _vp, _vp]),
+        "zest_plan_gemm": (_int, [_i64, _i64, _int, _i64p, _int, ctypes.POINTER(GemmPlan)]),
         "zest_pack_rms_norm": (_int, [_vp, _i64, _i64, _i64, ctypes.c_float, _vp, _vp, _i64, _i64, _vp, _i64, _vp]),
         "zest_norm_rope": (_int, [_vp, _i64, _i64, _i64, ctypes.c_float, _vp, _int, _int, _vp, _vp, _vp, _vp]),
         "zest_mul_mat_noalloc": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _int, _vp, _i64, _vp, _vp]),
@@ -114,7 +122,7 @@ def lib() -> ctypes.CDLL:
 def exported_symbols() -> list[str]:
     return [n for n in ("zest_version", "zest_last_error", "zest_load_iq3s_grid", "zest_pack_activations",
                         "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_gemm_group",
-                        "zest_gemm_segs", "zest_mul_mat_noalloc",
+                        "zest_gemm_segs", "zest_plan_gemm", "zest_mul_mat_noalloc",
                         "zest_rms_norm", "zest_mul_row", "zest_add", "zest_scale", "zest_glu", "zest_rope_table",
                         "zest_rope", "zest_pack_rms_norm", "zest_norm_rope",
                         "zest_usable", "zest_open",
@@ -240,6 +248,14 @@ def gemm_group(a_bf16, bs, M: int, Ns, modes, outs=None, err=None):
         if e:
             raise ZestError(f"zest_gemm_group raised device error bits {e:#x}")
     return outs
+
+
+def plan_gemm(M: int, K: int, Ns, sms: int = 0) -> dict:
+    """How K3 would run A [M][K] against weights of Ns rows (no GPU needed)."""
+    n = len(Ns)
+    out = GemmPlan()
+    _check(lib().zest_plan_gemm(M, K, n, (_i64 * n)(*Ns), sms, ctypes.byref(out)), "zest_plan_gemm")
+    return {name: getattr(out, name) for name, _ in GemmPlan._fields_}
 
 
 # --- the matmul service -------------------------------------------------------

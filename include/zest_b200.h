@@ -142,6 +142,29 @@ typedef struct {
 int zest_gemm_segs(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, int n, const zest_gemm_seg *segs,
                    unsigned *err, void *stream);
 
+/* How K3 runs a launch: its kernel, tiles, tile order and stream-K split. */
+typedef struct zest_gemm_plan {
+    int pair_kernel;      /* 1: CTA pairs on 256-row tiles; 0: one CTA per 128-row tile (M <= 128) */
+    int tile_n;           /* output tile width */
+    int tiles_m, tiles_n; /* tile rows; tile columns of all the weights end to end */
+    int k_blocks;         /* 64-wide k-blocks */
+    int64_t tiles;
+    int ctas;             /* CTAs launched (the one-CTA kernel: per weight, at most) */
+    int raster;           /* order the persistent CTAs walk the tiles in: 0 groups of 8 tile rows,
+                             1 rows (A streamed, B re-read from L2), 2 columns (B streamed) */
+    int stream_k;         /* 1: the last waves are cut into equal runs of k-blocks, one per pair */
+    int whole_tiles;      /* tiles run whole */
+    int split_tiles;      /* tiles cut into runs */
+    int64_t run_k_blocks; /* k-blocks per pair over the split tiles */
+} zest_gemm_plan;
+
+/* The plan zest_gemm_group / zest_gemm_segs make for A [M][K] and n weights
+ * of N[i] rows, on `sms` SMs (<= 0: this device's), with the same tuning
+ * variables. Host only: needs no GPU. The reference's NPU calls have a fixed
+ * design per shape (kernels/bfp16_gemm/whole_array_bfp_rtp.py:61-377); this
+ * reports the choices the B200 launch makes instead. */
+int zest_plan_gemm(int64_t M, int64_t K, int n, const int64_t *N, int sms, zest_gemm_plan *out);
+
 /* K2 + K3 without allocating anything: y[T][ldy] = x[T][K] * W^T, where w_bf16
  * is a weight's bf16 B operand (zest_convert_weight / zest_weight_bf16) of N
  * rows and the same mode and err word as zest_gemm. No counterpart in the
