@@ -30,6 +30,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #define ZEST_DESCRIPTION "NVIDIA B200 tensor cores (prompt work, next to the CUDA GPU backend)"
@@ -450,8 +451,22 @@ bool policy(const ggml_tensor *op, int depth = 0) {
 // the backend context (src/ggml-zest.cpp:184-423)
 // ---------------------------------------------------------------------------
 
+// The CUDA backend's own instance, for a piece that failed here, and its
+// buffer for the piece's host-memory inputs (grown as needed).
+struct sibling_run {
+    ggml_backend_t backend = nullptr;
+    ggml_backend_buffer_t in = nullptr;
+    size_t in_size = 0;
+    int64_t runs = 0;
+    ~sibling_run() {
+        if (in) ggml_backend_buffer_free(in);
+        if (backend) ggml_backend_free(backend);
+    }
+};
+
 struct context {
     zest_npu *npu = nullptr;
+    sibling_run again;  // failed pieces run again on the CUDA backend
     std::vector<float> host_values;  // a weight of a type without a GPU converter, dequantised
     std::vector<uint8_t> host_raw;
     float *stage_x = nullptr, *stage_y = nullptr;
@@ -603,6 +618,125 @@ void backend_free(ggml_backend_t backend) {
 const ggml_tensor *owner(const ggml_tensor *t) {
     while (t->view_src) t = t->view_src;
     return t;
+}
+
+// ---------------------------------------------------------------------------
+// a failed piece, run again on the CUDA backend (src/ggml-zest.cpp:709-755,
+// 887-891: the reference runs it again on its Vulkan sibling)
+// ---------------------------------------------------------------------------
+
+// GGML_ZEST_RERUN=0 leaves a failed piece failed (GGML_STATUS_FAILED).
+bool rerun_on() {
+    static const bool v = env_int("GGML_ZEST_RERUN", 1) != 0;
+    return v;
+}
+
+// Whether running the piece again reads what its first run read. The
+// reference's piece writes nothing back until it has finished; here results
+// go to their tensors as each op runs, and ggml's allocator may have put a
+// result on the memory of a piece input it outlives. So: no result the first
+// run may have written (the compute nodes up to the one that failed, and
+// every result folded into an earlier node's job) may overlap an input.
+bool rerun_safe(const std::vector<ggml_tensor *> &nodes, size_t failed_at,
+                const std::unordered_map<const ggml_tensor *, bool> &folded) {
+    struct range {
+        uintptr_t lo, hi;
+    };
+    auto span = [](const ggml_tensor *t) {
+        const uintptr_t lo = (uintptr_t) t->data;
+        return range{ lo, lo + ggml_nbytes(t) };
+    };
+    const std::unordered_set<const ggml_tensor *> made(nodes.begin(), nodes.end());
+    std::vector<range> written, inputs;
+    for (size_t k = 0; k < nodes.size(); k++)
+        if ((k <= failed_at || folded.count(nodes[k])) && nodes[k]->data) written.push_back(span(nodes[k]));
+    for (const ggml_tensor *n : nodes)
+        for (int j = 0; j < GGML_MAX_SRC; j++) {
+            const ggml_tensor *src = n->src[j];
+            if (!src || !src->data || made.count(src) || made.count(owner(src))) continue;
+            inputs.push_back(span(src));
+        }
+    for (const range &w : written)
+        for (const range &in : inputs)
+            if (w.lo < in.hi && in.lo < w.hi) return false;
+    return true;
+}
+
+// The piece on the CUDA backend; inputs in host memory (rotary positions)
+// move into CUDA memory for the call, and the tensors point back after it.
+bool sibling_compute(sibling_run &sr, ggml_cgraph *g, std::string &err) {
+    const sibling_t &sb = sibling();
+    if (!sb.dev || !sb.buft) {
+        err = "no CUDA backend to run it";
+        return false;
+    }
+    if (!sr.backend && !(sr.backend = ggml_backend_dev_init(sb.dev, nullptr))) {
+        err = "cannot start the CUDA backend";
+        return false;
+    }
+    std::vector<ggml_tensor *> owners, views;
+    std::unordered_set<const ggml_tensor *> seen;
+    const int n = ggml_graph_n_nodes(g);
+    for (int i = 0; i < n; i++) {
+        ggml_tensor *node = ggml_graph_node(g, i);
+        for (int j = 0; j < GGML_MAX_SRC; j++) {
+            ggml_tensor *src = node->src[j];
+            if (!src || !is_host(src) || !seen.insert(src).second) continue;
+            if (!src->view_src) {
+                owners.push_back(src);
+                continue;
+            }
+            views.push_back(src);
+            ggml_tensor *root = src;
+            while (root->view_src) root = root->view_src;
+            if (seen.insert(root).second) owners.push_back(root);
+        }
+    }
+    const size_t align = ggml_backend_buft_get_alignment(sb.buft);
+    auto padded = [align](size_t b) { return (b + align - 1) / align * align; };
+    size_t need = 0;
+    for (const ggml_tensor *o : owners) need += padded(ggml_nbytes(o));
+    if (need > sr.in_size) {
+        if (sr.in) ggml_backend_buffer_free(sr.in);
+        sr.in = ggml_backend_buft_alloc_buffer(sb.buft, need);
+        sr.in_size = sr.in ? need : 0;
+        if (!sr.in) {
+            err = "cannot hold the piece's host-memory inputs in CUDA memory";
+            return false;
+        }
+    }
+    // each view's place in its owner, taken before the owners move
+    std::vector<size_t> view_off;
+    for (const ggml_tensor *v : views) view_off.push_back((size_t) ((const char *) v->data - (const char *) owner(v)->data));
+    struct place {
+        ggml_tensor *t;
+        ggml_backend_buffer_t buffer;
+        void *data;
+    };
+    std::vector<place> moved;
+    char *base = owners.empty() ? nullptr : (char *) ggml_backend_buffer_get_base(sr.in);
+    size_t off = 0;
+    for (ggml_tensor *o : owners) {
+        moved.push_back({ o, o->buffer, o->data });
+        o->buffer = sr.in;
+        o->data = base + off;
+        ggml_backend_tensor_set(o, moved.back().data, 0, ggml_nbytes(o));
+        off += padded(ggml_nbytes(o));
+    }
+    for (size_t i = 0; i < views.size(); i++) {
+        ggml_tensor *v = views[i];
+        moved.push_back({ v, v->buffer, v->data });
+        v->buffer = sr.in;
+        v->data = (char *) owner(v)->data + view_off[i];
+    }
+    const bool ok = ggml_backend_graph_compute(sr.backend, g) == GGML_STATUS_SUCCESS;
+    for (auto it = moved.rbegin(); it != moved.rend(); ++it) {
+        it->t->buffer = it->buffer;
+        it->t->data = it->data;
+    }
+    sr.runs++;
+    if (!ok) err = "the CUDA backend failed it too";
+    return ok;
 }
 
 // SiLU(gate) * up as one GEMM (output mode 2): a SwiGLU whose gate and up are
@@ -1102,7 +1236,9 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
     } in_piece{ in_piece_map };
     const piece_plan plan = plan_piece(nodes, in_piece);
     cudaStream_t st = (cudaStream_t) zest_stream(ctx.npu);
-    for (ggml_tensor *node : nodes) {
+    size_t failed_at = nodes.size();  // the compute node that failed, if one did
+    for (size_t k = 0; k < nodes.size(); k++) {
+        ggml_tensor *node = nodes[k];
         if (status != GGML_STATUS_SUCCESS) break;
         std::string err;
         bool ok = true;
@@ -1130,11 +1266,25 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
         if (!ok) {
             failed(err);
             status = GGML_STATUS_FAILED;
+            failed_at = k;
         }
     }
     if (cudaStreamSynchronize(st) != cudaSuccess && status == GGML_STATUS_SUCCESS) {
         failed(std::string("a kernel failed: ") + cudaGetErrorString(cudaGetLastError()));
         status = GGML_STATUS_FAILED;
+        failed_at = nodes.size() - 1;
+    }
+    if (status != GGML_STATUS_SUCCESS && rerun_on()) {
+        // the failure is sticky (nothing is claimed from now on); this piece
+        // runs again on the CUDA backend when its inputs are intact
+        std::string err;
+        if (!rerun_safe(nodes, failed_at, plan.skip))
+            log_line("", "the failed piece does not run again: a result it wrote lies on one of its inputs");
+        else if (sibling_compute(ctx.again, cgraph, err)) {
+            log_line("", std::string("the failed piece ran again on ") + ggml_backend_dev_name(sibling().dev));
+            status = GGML_STATUS_SUCCESS;
+        } else
+            log_line("", "the failed piece could not run again: " + err);
     }
     cudaSetDevice(prev);
     ctx.compute_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -1386,6 +1536,34 @@ int ggml_zest_piece_plan(ggml_cgraph *cgraph, int *counts) {
     const piece_plan pl = plan_piece(nodes, in_piece);
     for (int i = 0; i < 6; i++) counts[i] = pl.counts[i];
     return (int) pl.jobs.size();
+}
+
+int ggml_zest_rerun_safe(ggml_cgraph *cgraph, int failed_at) {
+    std::vector<ggml_tensor *> nodes;
+    std::unordered_map<const ggml_tensor *, int> in_piece_map;
+    const int n = ggml_graph_n_nodes(cgraph);
+    for (int i = 0; i < n; i++) {
+        ggml_tensor *node = ggml_graph_node(cgraph, i);
+        in_piece_map[node] = i;
+        if (!(op_is(node, "NONE") || op_is(node, "RESHAPE") || op_is(node, "VIEW") || op_is(node, "PERMUTE") ||
+              op_is(node, "TRANSPOSE")))
+            nodes.push_back(node);
+    }
+    struct piece_set {
+        const std::unordered_map<const ggml_tensor *, int> &m;
+        size_t count(const ggml_tensor *t) const { return m.count(t); }
+    } in_piece{ in_piece_map };
+    const piece_plan pl = plan_piece(nodes, in_piece);
+    const size_t at = failed_at < 0 || (size_t) failed_at >= nodes.size() ? nodes.size() - 1 : (size_t) failed_at;
+    return rerun_safe(nodes, at, pl.skip) ? 1 : 0;
+}
+
+int ggml_zest_rerun(ggml_cgraph *cgraph) {
+    sibling_run sr;
+    std::string err;
+    if (sibling_compute(sr, cgraph, err)) return GGML_STATUS_SUCCESS;
+    log_line("", "the piece could not run on the CUDA backend: " + err);
+    return GGML_STATUS_FAILED;
 }
 
 int ggml_zest_piece_fusions(ggml_cgraph *cgraph) {

@@ -63,6 +63,18 @@ __attribute__((visibility("default"))) int ggml_zest_budget_plan(double limit_gb
  * RMS_NORM + MUL + ROPE runs done as one kernel. Host logic only; for tests. */
 __attribute__((visibility("default"))) int ggml_zest_piece_plan(struct ggml_cgraph *cgraph, int *counts);
 
+/* The failure path's host side (src/ggml-zest.cpp:709-755,887-891). After a
+ * failed piece, graph_compute runs it again on the CUDA backend and returns
+ * its status, unless GGML_ZEST_RERUN=0 or a result the first run may have
+ * written (the compute nodes up to the failing one, failed_at; -1 for all,
+ * and every result folded into an earlier node's job) overlaps one of the
+ * piece's inputs. ggml_zest_rerun_safe answers that check (1: safe to run
+ * again); ggml_zest_rerun runs the piece on the CUDA backend as graph_compute
+ * does, moving host-memory inputs into CUDA memory for the call. Host logic
+ * only; for tests. */
+__attribute__((visibility("default"))) int ggml_zest_rerun_safe(struct ggml_cgraph *cgraph, int failed_at);
+__attribute__((visibility("default"))) int ggml_zest_rerun(struct ggml_cgraph *cgraph);
+
 #ifdef __cplusplus
 }
 #endif

@@ -101,6 +101,11 @@ class Harness:
         self.plugin.ggml_zest_piece_plan.argtypes = [_vp, ctypes.POINTER(ctypes.c_int)]
         self.plugin.ggml_zest_budget_plan.argtypes = [ctypes.c_double, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         self.plugin.ggml_zest_piece_groups.argtypes = [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+        self.plugin.ggml_zest_rerun_safe.argtypes = [_vp, ctypes.c_int]
+        self.plugin.ggml_zest_rerun.argtypes = [_vp]
+        self.fake.fake_sibling_set.argtypes = [_int, _int]
+        self.fake.fake_sibling_stats.argtypes = [ctypes.POINTER(ctypes.c_long)]
+        self.fake.fake_sibling_stats.restype = ctypes.c_ulonglong
         # ctypes objects the C side points at, kept for the whole process: the
         # plugin remembers who read each tensor by address (as the reference
         # does), and a freed tensor's address reused by a later test's tensor
@@ -134,6 +139,31 @@ class Harness:
         sizes = (ctypes.c_int * 16)()
         n = self.plugin.ggml_zest_piece_groups(self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp)), sizes, 16)
         return list(sizes[:n])
+
+    def graph(self, nodes: list[Tensor]):
+        arr = (ctypes.POINTER(Tensor) * len(nodes))(*[ctypes.pointer(n) for n in nodes])
+        self.keep.append(arr)
+        return self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp))
+
+    def rerun_safe(self, nodes: list[Tensor], failed_at: int = -1) -> bool:
+        """Whether a piece that failed at compute node failed_at (-1: at the
+        end) may run again on the CUDA backend."""
+        return bool(self.plugin.ggml_zest_rerun_safe(self.graph(nodes), failed_at))
+
+    def rerun(self, nodes: list[Tensor]) -> int:
+        """The piece run on the CUDA backend as after a failure: its status."""
+        return self.plugin.ggml_zest_rerun(self.graph(nodes))
+
+    def sibling(self, status: int = 0, init_fails: bool = False) -> None:
+        """What the fake CUDA backend answers from now on; its records reset."""
+        self.fake.fake_sibling_reset()
+        self.fake.fake_sibling_set(status, int(init_fails))
+
+    def sibling_stats(self) -> dict:
+        v = (ctypes.c_long * 8)()
+        total = self.fake.fake_sibling_stats(v)
+        keys = ("runs", "nodes", "moved", "started", "stopped", "buffers", "buffers_freed", "sets")
+        return dict(zip(keys, list(v)), moved_sum=int(total))
 
     # --- registry / device / backend ------------------------------------------
     def reg(self):
