@@ -188,6 +188,7 @@ struct budget_t {
     int contexts = 0;
     bool started = false, cut = false, running = false;
     double limit = 0, taken = 0;
+    const char *source = "";  // where the limit came from
     struct entry {
         int layer;
         double bytes;
@@ -196,6 +197,7 @@ struct budget_t {
     void reset() {
         started = cut = running = false;
         limit = taken = 0;
+        source = "";
         in.clear();
         out.clear();
     }
@@ -212,7 +214,9 @@ bool budget_decide(budget_t &b, const ggml_tensor *w) {
         const char *s = zenv("GGML_XDNA_MAX_COPY_GB");
         if (s) {
             b.limit = atof(s) * GB;
+            b.source = "GGML_XDNA_MAX_COPY_GB";
         } else {
+            b.source = "free GPU memory less a reserve of max(4 GB, a tenth)";
             size_t free_b = 0, total_b = 0;
             int prev = 0;
             cudaGetDevice(&prev);
@@ -248,6 +252,58 @@ bool budget_decide(budget_t &b, const ggml_tensor *w) {
     }
     b.out[key] = e;
     return false;
+}
+
+// Said once, as the first prompt runs, what the weight copies came to
+// (src/ggml-zest.cpp:556-564): the report is left out when the budget cut,
+// which said so when it happened.
+void budget_report() {
+    std::lock_guard<std::mutex> lk(g_budget.mu);
+    budget_t &b = g_budget;
+    if (b.running) return;
+    b.running = true;
+    if (!b.started || b.cut) return;
+    char msg[256];
+    snprintf(msg, sizeof msg, "weight copies: %.1f GB for %zu weights (limit %.1f GB: %s)", b.taken / GB, b.in.size(),
+             std::max(0.0, b.limit) / GB, b.source);
+    log_line("", msg);
+}
+
+// What we noticed about the model while llama.cpp planned its graph, said
+// once from graph_compute (src/ggml-zest.cpp:566-655): llama.cpp's
+// memory-fitting trial plans graphs with warnings hidden but never computes
+// one. A mixture-of-experts model's expert step is a MUL_MAT_ID, which is
+// not claimed, and rounding its router's multiply to bfp16 can change which
+// experts a token uses. (The reference's second note, on narrow models, rests
+// on its NPU-against-iGPU measurements and is not made here.)
+struct notes_t {
+    std::atomic<bool> moe{ false };
+    std::atomic<bool> said{ false };
+    void reset() {
+        moe = false;
+        said = false;
+    }
+};
+notes_t g_notes;
+
+void note_model(const ggml_tensor *op) {
+    if (op_is(op, "MUL_MAT_ID")) g_notes.moe.store(true, std::memory_order_relaxed);
+}
+
+std::string model_notes() {
+    std::string s;
+    if (g_notes.moe.load())
+        s += "mixture-of-experts model: XDNA0 does not take the expert step (MUL_MAT_ID), so it gets only part "
+             "of the work, and rounding the router's multiply to bfp16 can change which experts a token uses "
+             "(the reference measured such models drifting further from the GPU's answers than dense ones). "
+             "Running it on XDNA0 as asked; -dev CUDA0 would use the GPU backend alone";
+    return s;
+}
+
+void say_notes() {
+    if (g_notes.said.exchange(true)) return;
+    const std::string s = model_notes();
+    if (!s.empty()) log_line("warning: ", s);
 }
 
 bool budget_takes(const ggml_tensor *w) {
@@ -415,6 +471,31 @@ bool read_outside(const ggml_tensor *t, const Set &in_piece) {
     for (const ggml_tensor *r : it->second)
         if (!in_piece.count(r)) return true;
     return false;
+}
+
+// GGML_XDNA_TRACE=1: matmul results with no recorded reader (their readers
+// decide what a piece writes back and what it folds), one line each, and a
+// count every 100 pieces (src/ggml-zest.cpp:1111-1129).
+void trace_piece(ggml_cgraph *cgraph) {
+    static std::atomic<int64_t> pieces{ 0 }, results{ 0 }, unseen{ 0 };
+    const int64_t p = ++pieces;
+    const int n = ggml_graph_n_nodes(cgraph);
+    for (int i = 0; i < n; i++) {
+        const ggml_tensor *t = ggml_graph_node(cgraph, i);
+        if (!op_is(t, "MUL_MAT")) continue;
+        results++;
+        std::lock_guard<std::mutex> lk(g_read_mu);
+        if (!g_readers.count(t)) {
+            unseen++;
+            log_line("trace: ", std::string(t->name) + " (MUL_MAT) has no recorded reader");
+        }
+    }
+    if (p % 100 == 0) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "%lld pieces, %lld matmul results, %lld with no recorded reader", (long long) p,
+                 (long long) results.load(), (long long) unseen.load());
+        log_line("trace: ", msg);
+    }
 }
 
 // The whole policy (src/ggml-zest.cpp:1182-1226): a matmul we can take, or a
@@ -612,7 +693,10 @@ void backend_free(ggml_backend_t backend) {
     delete (context *) backend->context;
     delete backend;
     std::lock_guard<std::mutex> lk(g_budget.mu);
-    if (--g_budget.contexts == 0) g_budget.reset();
+    if (--g_budget.contexts == 0) {
+        g_budget.reset();
+        g_notes.reset();  // the next model gets its own notes
+    }
 }
 
 const ggml_tensor *owner(const ggml_tensor *t) {
@@ -1210,10 +1294,9 @@ bool plain_job(const mm_job &j) {
 
 enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgraph) {
     context &ctx = *(context *) backend->context;
-    {
-        std::lock_guard<std::mutex> lk(g_budget.mu);
-        g_budget.running = true;
-    }
+    budget_report();
+    say_notes();
+    if (trace()) trace_piece(cgraph);
     const auto t0 = std::chrono::steady_clock::now();
     int prev = 0;
     cudaGetDevice(&prev);
@@ -1426,6 +1509,7 @@ ggml_backend_buffer_type_t dev_get_buffer_type(ggml_backend_dev_t) { return sibl
 
 bool dev_supports_op(ggml_backend_dev_t, const ggml_tensor *op) {
     if (blocks()) note_readers(op);
+    note_model(op);
     if (!sibling().dev || g_broken || !gpu_usable()) return false;
     return policy(op);
 }
@@ -1556,6 +1640,12 @@ int ggml_zest_rerun_safe(ggml_cgraph *cgraph, int failed_at) {
     const piece_plan pl = plan_piece(nodes, in_piece);
     const size_t at = failed_at < 0 || (size_t) failed_at >= nodes.size() ? nodes.size() - 1 : (size_t) failed_at;
     return rerun_safe(nodes, at, pl.skip) ? 1 : 0;
+}
+
+int ggml_zest_model_notes(char *out, int n) {
+    const std::string s = model_notes();
+    if (out && n > 0) snprintf(out, (size_t) n, "%s", s.c_str());
+    return (int) s.size();
 }
 
 int ggml_zest_rerun(ggml_cgraph *cgraph) {

@@ -73,6 +73,11 @@ __attribute__((visibility("default"))) int ggml_zest_piece_plan(struct ggml_cgra
  * does, moving host-memory inputs into CUDA memory for the call. Host logic
  * only; for tests. */
 __attribute__((visibility("default"))) int ggml_zest_rerun_safe(struct ggml_cgraph *cgraph, int failed_at);
+/* The notes about the model that graph_compute says once as the first prompt
+ * runs (src/ggml-zest.cpp:566-655), gathered while supports_op was asked:
+ * writes them to out (at most n bytes) and returns their length, 0 for none.
+ * Host logic only; for tests. */
+__attribute__((visibility("default"))) int ggml_zest_model_notes(char *out, int n);
 __attribute__((visibility("default"))) int ggml_zest_rerun(struct ggml_cgraph *cgraph);
 
 #ifdef __cplusplus

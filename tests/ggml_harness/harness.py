@@ -103,6 +103,7 @@ class Harness:
         self.plugin.ggml_zest_piece_groups.argtypes = [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
         self.plugin.ggml_zest_rerun_safe.argtypes = [_vp, ctypes.c_int]
         self.plugin.ggml_zest_rerun.argtypes = [_vp]
+        self.plugin.ggml_zest_model_notes.argtypes = [ctypes.c_char_p, ctypes.c_int]
         self.fake.fake_sibling_set.argtypes = [_int, _int]
         self.fake.fake_sibling_stats.argtypes = [ctypes.POINTER(ctypes.c_long)]
         self.fake.fake_sibling_stats.restype = ctypes.c_ulonglong
@@ -153,6 +154,12 @@ class Harness:
     def rerun(self, nodes: list[Tensor]) -> int:
         """The piece run on the CUDA backend as after a failure: its status."""
         return self.plugin.ggml_zest_rerun(self.graph(nodes))
+
+    def model_notes(self) -> str:
+        """What graph_compute would say about the model as the first prompt runs."""
+        buf = ctypes.create_string_buffer(2048)
+        self.plugin.ggml_zest_model_notes(buf, len(buf))
+        return buf.value.decode()
 
     def sibling(self, status: int = 0, init_fails: bool = False) -> None:
         """What the fake CUDA backend answers from now on; its records reset."""

@@ -104,6 +104,17 @@ def test_mul_mat_id_not_claimed(h):
     assert h.policy(mm(h, Q4_0, 2048, 2048, 2048)), "ordinary matmuls are still claimed afterwards"
 
 
+def test_mixture_of_experts_is_noted(h):
+    # src/ggml-zest.cpp:566-655: a MUL_MAT_ID seen while llama.cpp plans the
+    # graph makes the first prompt's graph_compute warn that the expert step
+    # stays with the GPU backend
+    experts = h.tensor(Q4_0, [2048, 2048, 8], buffer=h.buffer(USAGE_WEIGHTS))
+    rows = h.tensor(F32, [2048, 1, 2048])
+    h.supports_op(h.tensor(F32, [2048, 1, 2048], op="MUL_MAT_ID", src=(experts, rows)))
+    notes = h.model_notes()
+    assert "mixture-of-experts" in notes and "MUL_MAT_ID" in notes
+
+
 def test_supports_op_needs_a_usable_gpu(h):
     # supports_op = a usable GPU (start-up self-test) and the policy; without
     # a GPU the plugin still registers but no device is offered and nothing
