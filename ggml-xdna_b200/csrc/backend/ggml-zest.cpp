@@ -1508,7 +1508,7 @@ ggml_backend_t dev_init_backend(ggml_backend_dev_t dev, const char *) {
 ggml_backend_buffer_type_t dev_get_buffer_type(ggml_backend_dev_t) { return sibling().buft; }
 
 bool dev_supports_op(ggml_backend_dev_t, const ggml_tensor *op) {
-    if (blocks()) note_readers(op);
+    if (blocks() || trace()) note_readers(op);
     note_model(op);
     if (!sibling().dev || g_broken || !gpu_usable()) return false;
     return policy(op);
