@@ -92,6 +92,13 @@ int zest_convert_weight(int type, const void *raw, int64_t rows_total, int64_t r
 int zest_convert_gate_up(int type, const void *gate, const void *up, int64_t rows_total, int64_t row0, int64_t F,
                          int64_t K, int64_t f_pad, uint8_t *b_bfp16, uint16_t *b_bf16, void *stream);
 
+/* Launches of K3 (zest_gemm, zest_gemm_group, zest_gemm_segs) whose last
+ * waves are cut into stream-K runs (zest_plan_gemm reports which) share one
+ * partial-sum workspace per device. The library orders such launches across
+ * streams. Inside a stream capture it orders them within the capture only,
+ * so a CUDA graph holding them must not replay while another stream runs one
+ * (ZEST_GEMM_SK=0 takes stream-K out). */
+
 /* K3, the GEMM: c[M][ldc] = A[M][K] * B[N][K]^T in fp32 on the tensor cores,
  * then `mode`. In ZEST_MODE_SWIGLU, B comes from zest_convert_gate_up and c
  * gets N/2 values a row. err: a device word the kernel ORs ZEST_ERR_* bits
