@@ -1363,6 +1363,10 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
         std::string err;
         if (!rerun_safe(nodes, failed_at, plan.skip))
             log_line("", "the failed piece does not run again: a result it wrote lies on one of its inputs");
+        else if (cudaDeviceSynchronize() != cudaSuccess)
+            // a kernel fault leaves the context unusable for the CUDA backend too
+            log_line("", std::string("the failed piece does not run again: the GPU reports ") +
+                             cudaGetErrorString(cudaGetLastError()));
         else if (sibling_compute(ctx.again, cgraph, err)) {
             log_line("", std::string("the failed piece ran again on ") + ggml_backend_dev_name(sibling().dev));
             status = GGML_STATUS_SUCCESS;
