@@ -744,7 +744,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         dead = true;  // keep step with the other warps through the barriers below
                         break;
                     }
-            const int row_local = q * 32 + lane;
             const int64_t row0 = (int64_t) mb * P_BM + rank * 128 + q * 32, row = row0 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * ACC_COLS);
             // each chunk's TMEM load goes out while the chunk before it is
