@@ -82,6 +82,32 @@ bool op_is(const ggml_tensor *t, const char *name) {
     return n && strcmp(n, name) == 0;
 }
 
+// A node that computes nothing: a leaf, or a new description of existing memory.
+bool is_noop(const ggml_tensor *t) {
+    return op_is(t, "NONE") || op_is(t, "RESHAPE") || op_is(t, "VIEW") || op_is(t, "PERMUTE") ||
+           op_is(t, "TRANSPOSE");
+}
+
+// A piece's nodes in graph order, and which tensors are nodes of it. `nodes`
+// leaves out leaves, and with compute_only also the nodes that only
+// re-describe memory; every node stays a member (count).
+struct piece_nodes {
+    std::vector<ggml_tensor *> nodes;
+    std::unordered_map<const ggml_tensor *, int> index;
+    size_t count(const ggml_tensor *t) const { return index.count(t); }
+};
+
+piece_nodes collect_piece(ggml_cgraph *g, bool compute_only) {
+    piece_nodes p;
+    const int n = ggml_graph_n_nodes(g);
+    for (int i = 0; i < n; i++) {
+        ggml_tensor *node = ggml_graph_node(g, i);
+        p.index[node] = i;
+        if (compute_only ? !is_noop(node) : !op_is(node, "NONE")) p.nodes.push_back(node);
+    }
+    return p;
+}
+
 // ---------------------------------------------------------------------------
 // run mode and the sticky failure (src/ggml-zest.cpp:91-130)
 // ---------------------------------------------------------------------------
@@ -1303,21 +1329,9 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
     cudaSetDevice(cuda_device());
     ctx.stage_next = 0;
     enum ggml_status status = GGML_STATUS_SUCCESS;
-    std::vector<ggml_tensor *> nodes;
-    const int n = ggml_graph_n_nodes(cgraph);
-    for (int i = 0; i < n; i++) {
-        ggml_tensor *node = ggml_graph_node(cgraph, i);
-        if (!(op_is(node, "NONE") || op_is(node, "RESHAPE") || op_is(node, "VIEW") || op_is(node, "PERMUTE") ||
-              op_is(node, "TRANSPOSE")))
-            nodes.push_back(node);
-    }
-    std::unordered_map<const ggml_tensor *, int> in_piece_map;
-    for (int i = 0; i < n; i++) in_piece_map[ggml_graph_node(cgraph, i)] = i;
-    struct piece_set {
-        const std::unordered_map<const ggml_tensor *, int> &m;
-        size_t count(const ggml_tensor *t) const { return m.count(t); }
-    } in_piece{ in_piece_map };
-    const piece_plan plan = plan_piece(nodes, in_piece);
+    const piece_nodes piece = collect_piece(cgraph, true);
+    const std::vector<ggml_tensor *> &nodes = piece.nodes;
+    const piece_plan plan = plan_piece(nodes, piece);
     cudaStream_t st = (cudaStream_t) zest_stream(ctx.npu);
     size_t failed_at = nodes.size();  // the compute node that failed, if one did
     for (size_t k = 0; k < nodes.size(); k++) {
@@ -1397,25 +1411,15 @@ void backend_graph_optimize(ggml_backend_t backend, ggml_cgraph *cgraph, ggml_ba
     static const bool at_load = env_int("GGML_XDNA_COPY_AT_LOAD", 1) != 0;
     if (!at_load || g_broken) return;
     context &ctx = *(context *) backend->context;
-    const int n = ggml_graph_n_nodes(cgraph);
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(cuda_device());
     // the copies the piece will use, as running it would make them
     // (xdna_exec_weights, src/xdna-exec.cpp:435-448): fused gate/up pairs once
-    std::vector<ggml_tensor *> nodes;
-    std::unordered_map<const ggml_tensor *, int> in_piece_map;
-    for (int i = 0; i < n; i++) {
-        ggml_tensor *node = ggml_graph_node(cgraph, i);
-        in_piece_map[node] = i;
-        if (!op_is(node, "NONE")) nodes.push_back(node);
-    }
-    struct piece_set {
-        const std::unordered_map<const ggml_tensor *, int> &m;
-        size_t count(const ggml_tensor *t) const { return m.count(t); }
-    } in_piece{ in_piece_map };
+    const piece_nodes piece = collect_piece(cgraph, false);
+    const std::vector<ggml_tensor *> &nodes = piece.nodes;
     std::unordered_map<const ggml_tensor *, const fusion *> fused;
-    const std::vector<fusion> fusions = blocks() ? find_fusions(nodes, in_piece) : std::vector<fusion>();
+    const std::vector<fusion> fusions = blocks() ? find_fusions(nodes, piece) : std::vector<fusion>();
     for (const fusion &f : fusions) {
         fused[f.gate] = &f;
         if (f.up) fused[f.up] = nullptr;
@@ -1573,14 +1577,9 @@ ggml_backend_reg_t ggml_backend_xdna_reg(void) {
 int ggml_zest_policy_supports(const ggml_tensor *op) { return op && policy(op) ? 1 : 0; }
 
 int ggml_zest_piece_groups(ggml_cgraph *cgraph, int *sizes, int max_groups) {
-    std::vector<ggml_tensor *> nodes;
-    const int n = ggml_graph_n_nodes(cgraph);
-    for (int i = 0; i < n; i++) {
-        ggml_tensor *node = ggml_graph_node(cgraph, i);
-        if (!op_is(node, "NONE")) nodes.push_back(node);
-    }
+    const piece_nodes piece = collect_piece(cgraph, false);
     const std::unordered_map<const ggml_tensor *, bool> none;
-    const auto groups = find_groups(nodes, none);
+    const auto groups = find_groups(piece.nodes, none);
     for (int i = 0; i < (int) groups.size() && i < max_groups; i++) sizes[i] = (int) groups[i].size();
     return (int) groups.size();
 }
@@ -1607,41 +1606,16 @@ int ggml_zest_budget_plan(double limit_gb, const ggml_tensor *const *weights, in
 }
 
 int ggml_zest_piece_plan(ggml_cgraph *cgraph, int *counts) {
-    std::vector<ggml_tensor *> nodes;
-    std::unordered_map<const ggml_tensor *, int> in_piece_map;
-    const int n = ggml_graph_n_nodes(cgraph);
-    for (int i = 0; i < n; i++) {
-        ggml_tensor *node = ggml_graph_node(cgraph, i);
-        in_piece_map[node] = i;
-        if (!(op_is(node, "NONE") || op_is(node, "RESHAPE") || op_is(node, "VIEW") || op_is(node, "PERMUTE") ||
-              op_is(node, "TRANSPOSE")))
-            nodes.push_back(node);
-    }
-    struct piece_set {
-        const std::unordered_map<const ggml_tensor *, int> &m;
-        size_t count(const ggml_tensor *t) const { return m.count(t); }
-    } in_piece{ in_piece_map };
-    const piece_plan pl = plan_piece(nodes, in_piece);
+    const piece_nodes piece = collect_piece(cgraph, true);
+    const piece_plan pl = plan_piece(piece.nodes, piece);
     for (int i = 0; i < 6; i++) counts[i] = pl.counts[i];
     return (int) pl.jobs.size();
 }
 
 int ggml_zest_rerun_safe(ggml_cgraph *cgraph, int failed_at) {
-    std::vector<ggml_tensor *> nodes;
-    std::unordered_map<const ggml_tensor *, int> in_piece_map;
-    const int n = ggml_graph_n_nodes(cgraph);
-    for (int i = 0; i < n; i++) {
-        ggml_tensor *node = ggml_graph_node(cgraph, i);
-        in_piece_map[node] = i;
-        if (!(op_is(node, "NONE") || op_is(node, "RESHAPE") || op_is(node, "VIEW") || op_is(node, "PERMUTE") ||
-              op_is(node, "TRANSPOSE")))
-            nodes.push_back(node);
-    }
-    struct piece_set {
-        const std::unordered_map<const ggml_tensor *, int> &m;
-        size_t count(const ggml_tensor *t) const { return m.count(t); }
-    } in_piece{ in_piece_map };
-    const piece_plan pl = plan_piece(nodes, in_piece);
+    const piece_nodes piece = collect_piece(cgraph, true);
+    const std::vector<ggml_tensor *> &nodes = piece.nodes;
+    const piece_plan pl = plan_piece(nodes, piece);
     const size_t at = failed_at < 0 || (size_t) failed_at >= nodes.size() ? nodes.size() - 1 : (size_t) failed_at;
     return rerun_safe(nodes, at, pl.skip) ? 1 : 0;
 }
@@ -1661,19 +1635,8 @@ int ggml_zest_rerun(ggml_cgraph *cgraph) {
 }
 
 int ggml_zest_piece_fusions(ggml_cgraph *cgraph) {
-    std::vector<ggml_tensor *> nodes;
-    std::unordered_map<const ggml_tensor *, int> in_piece_map;
-    const int n = ggml_graph_n_nodes(cgraph);
-    for (int i = 0; i < n; i++) {
-        ggml_tensor *node = ggml_graph_node(cgraph, i);
-        in_piece_map[node] = i;
-        if (!op_is(node, "NONE")) nodes.push_back(node);
-    }
-    struct piece_set {
-        const std::unordered_map<const ggml_tensor *, int> &m;
-        size_t count(const ggml_tensor *t) const { return m.count(t); }
-    } in_piece{ in_piece_map };
-    return (int) find_fusions(nodes, in_piece).size();
+    const piece_nodes piece = collect_piece(cgraph, false);
+    return (int) find_fusions(piece.nodes, piece).size();
 }
 
 GGML_BACKEND_API ggml_backend_reg_t ggml_backend_init(void) { return ggml_backend_xdna_reg(); }
