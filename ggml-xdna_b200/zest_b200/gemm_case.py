@@ -3,6 +3,7 @@
     python -m zest_b200.gemm_case C1                 # six launches (for an ncu capture of the 6th)
     python -m zest_b200.gemm_case --time             # device time per launch of every shape
     ZEST_GEMM_SK=0 python -m zest_b200.gemm_case --time C1 "C3 o"
+    python -m zest_b200.gemm_case --plan             # the launch plans, on the host (no GPU)
 
 Operands are bf16 on the device (A ~ N(0, 0.25), B ~ N(0, 0.0004), seeded); the
 output is f32 holding bf16-rounded values, as the plugin's default. `--time`
@@ -82,12 +83,20 @@ def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("shapes", nargs="*", help=f"shape names (default: all): {', '.join(SHAPES)}")
     ap.add_argument("--time", action="store_true", help="print device time per launch instead of just running")
+    ap.add_argument("--plan", action="store_true", help="print each shape's launch plan (no GPU needed)")
+    ap.add_argument("--sms", type=int, default=148, help="--plan: the SMs to plan for")
     ap.add_argument("--launches", type=int, default=6)
     args = ap.parse_args(argv)
     names = args.shapes or list(SHAPES)
     for s in names:
         if s not in SHAPES:
             ap.error(f"unknown shape {s!r}")
+    if args.plan:
+        from . import plan_gemm
+        for s in names:
+            M, Ns, K = SHAPES[s]
+            print(json.dumps({"shape": s, **plan_gemm(M, K, Ns, args.sms)}))
+        return
     if args.time:
         print(json.dumps({s: [round(v, 1) for v in timed(s)] for s in names}))
     else:

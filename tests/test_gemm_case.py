@@ -20,3 +20,11 @@ def test_shapes_are_the_configs_launches():
 def test_unknown_shape_refused():
     with pytest.raises(SystemExit):
         gemm_case.main(["no such shape"])
+
+
+def test_plan_lines_without_gpu(capsys):
+    gemm_case.main(["--plan", "C1", "C3 o"])
+    import json
+    plans = [json.loads(x) for x in capsys.readouterr().out.splitlines()]
+    assert [p["shape"] for p in plans] == ["C1", "C3 o"]
+    assert plans[0]["stream_k"] == 0 and plans[1]["stream_k"] == 1
