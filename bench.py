@@ -328,7 +328,7 @@ def run_ours(args, w: dict) -> None:
     # tokens: every rank its own prompt chunk through whole weights (no
     # collective); nshard: every rank an N-slab of each weight, outputs
     # all-gathered into ggml's row-major [M][N]
-    from zest_b200.shard import gather_slabs, shard_rows, slab_width
+    from zest_b200.shard import any_rank, gather_slabs, shard_rows, slab_width
     nshard = world > 1 and args.mode != "tokens"
     gather = nshard and args.mode == "nshard"
 
@@ -403,8 +403,8 @@ def run_ours(args, w: dict) -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if int(err.item()):
-        raise Z.ZestError(f"device error bits {int(err.item()):#x} during warm-up")
+    if any_rank(int(err.item()) != 0):  # every rank stops together
+        raise Z.ZestError(f"device error bits {int(err.item()):#x} during warm-up (this rank)")
     ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in groups]
           for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -422,8 +422,8 @@ def run_ours(args, w: dict) -> None:
     ms = t0.elapsed_time(t1) / args.steps
     gemm_ms = [sum(ev[s][i][0].elapsed_time(ev[s][i][1]) for s in range(args.steps)) / args.steps
                for i in range(len(groups))]
-    if int(err.item()):
-        raise Z.ZestError(f"device error bits {int(err.item()):#x} in the timed region")
+    if any_rank(int(err.item()) != 0):
+        raise Z.ZestError(f"device error bits {int(err.item()):#x} in the timed region (this rank)")
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -924,6 +924,7 @@ def run_model(args, w: dict) -> None:
     import torch
 
     import zest_b200 as Z
+    from zest_b200.shard import any_rank
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -944,8 +945,8 @@ def run_model(args, w: dict) -> None:
     for _ in range(args.warmup):
         m.run(ids_host)
     torch.cuda.synchronize()
-    if int(m.err.item()):
-        raise Z.ZestError(f"device error bits {int(m.err.item()):#x} during warm-up")
+    if any_rank(int(m.err.item()) != 0):  # every rank stops together
+        raise Z.ZestError(f"device error bits {int(m.err.item()):#x} during warm-up (this rank)")
     if not torch.isfinite(m.logits).all():
         raise Z.ZestError("non-finite logits")
     # eager prefills with events around every MUL_MAT launch and attention:
@@ -977,8 +978,8 @@ def run_model(args, w: dict) -> None:
             m.run(ids_host, graphs=True)
         t1.record()
         torch.cuda.synchronize()
-    if int(m.err.item()):
-        raise Z.ZestError(f"device error bits {int(m.err.item()):#x} in the timed region")
+    if any_rank(int(m.err.item()) != 0):
+        raise Z.ZestError(f"device error bits {int(m.err.item()):#x} in the timed region (this rank)")
     ms = t0.elapsed_time(t1) / steps
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if world > 1:
@@ -1086,7 +1087,7 @@ def run_tp(args, w: dict) -> None:
     import torch.distributed as dist
 
     import zest_b200 as Z
-    from zest_b200.shard import all_reduce_rows, shard_cols, shard_rows
+    from zest_b200.shard import all_reduce_rows, any_rank, shard_cols, shard_rows
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1213,8 +1214,8 @@ def run_tp(args, w: dict) -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if int(err.item()):
-        raise Z.ZestError(f"device error bits {int(err.item()):#x} during warm-up")
+    if any_rank(int(err.item()) != 0):  # every rank stops together
+        raise Z.ZestError(f"device error bits {int(err.item()):#x} during warm-up (this rank)")
     check = None
     if mc:
         # the multicast sums against the same partials summed by NCCL
@@ -1229,8 +1230,8 @@ def run_tp(args, w: dict) -> None:
                 dist.all_reduce(part)
                 worst = max(worst, ((out[nm] - part).abs().max() / part.abs().max()).item())
         check = {"max_rel_diff_vs_nccl": worst}
-        if not worst <= 1e-5:
-            raise Z.ZestError(f"multicast sums differ from NCCL's by {worst}")
+        if any_rank(not worst <= 1e-5):
+            raise Z.ZestError(f"multicast sums differ from NCCL's by {worst} (this rank)")
     mk = lambda: [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
     ev = [[[mk() for _ in chunks] for _ in groups] for _ in range(args.steps)]
     t0, t1 = mk()
@@ -1245,8 +1246,8 @@ def run_tp(args, w: dict) -> None:
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    if int(err.item()):
-        raise Z.ZestError(f"device error bits {int(err.item()):#x} in the timed region")
+    if any_rank(int(err.item()) != 0):
+        raise Z.ZestError(f"device error bits {int(err.item()):#x} in the timed region (this rank)")
     ms = t0.elapsed_time(t1) / args.steps
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if world > 1:

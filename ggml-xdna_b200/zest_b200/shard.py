@@ -65,3 +65,18 @@ def all_reduce_rows(partial, row0: int, rows: int, group=None, async_op: bool = 
     order; returns the work handle when async_op."""
     import torch.distributed as dist
     return dist.all_reduce(partial[row0:row0 + rows], op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+
+
+def any_rank(flag: bool, group=None) -> bool:
+    """Whether `flag` holds on any rank of the group (this rank's own flag
+    when no process group is up): ranks take an error path together, so none
+    is left waiting in a collective that a failing rank skipped. Collective:
+    every rank calls it, in order."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()):
+        return bool(flag)
+    dev = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return bool(t.item())

@@ -136,3 +136,46 @@ def test_k_sharded_partials_sum_to_the_product_gloo():
     results = dict(q.get(timeout=10) for _ in range(world))
     assert all(p.exitcode == 0 for p in procs)
     assert results == {0: True, 1: True}
+
+
+def _any_rank_rank(rank: int, world: int, port: int, q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root), str(root / "ggml-xdna_b200")]
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from zest_b200.shard import any_rank
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        # a failure seen by rank 1 alone sends every rank down the error path,
+        # and after it every rank still meets the next collective
+        seen = [any_rank(False), any_rank(rank == 1), any_rank(True)]
+        dist.barrier()
+        q.put((rank, seen))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ranks_take_an_error_path_together_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_any_rank_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    results = dict(q.get(timeout=10) for _ in range(world))
+    assert all(p.exitcode == 0 for p in procs)
+    assert results == {0: [False, True, True], 1: [False, True, True]}
+
+
+def test_any_rank_without_a_process_group():
+    from zest_b200.shard import any_rank
+    assert any_rank(True) is True and any_rank(False) is False
