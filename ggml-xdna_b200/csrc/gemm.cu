@@ -1209,7 +1209,8 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
                       unsigned *err_flag, cudaStream_t st) {
     if (M <= 0 || nseg <= 0) return 0;
     if (nseg > MAX_SEG) return set_error("gemm: at most 4 weights in a group");
-    if (K <= 0 || K % 8 || lda < K || lda % 8 || ((uintptr_t) a_bf16 & 15) || !err_flag)
+    if (!err_flag) return set_error("gemm: no device error word");
+    if (K <= 0 || K % 8 || lda < K || lda % 8 || ((uintptr_t) a_bf16 & 15))
         return set_error("gemm: K and the row strides must be multiples of 8 and the operands 16-byte aligned");
     for (int s = 0; s < nseg; s++) {
         gemm_seg &g = segs[s];

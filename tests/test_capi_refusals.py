@@ -39,7 +39,7 @@ def test_gemm_refuses_what_the_kernel_cannot_take():
     refused(gemm(lda=120), "multiples of 8")
     refused(gemm(a=ODD), "16-byte aligned")
     refused(gemm(b=ODD), "16-byte aligned")
-    refused(gemm(err=0), "multiples of 8")  # no error word
+    refused(gemm(err=0), "no device error word")
     refused(gemm(mode=7), "bad output mode")
     refused(gemm(N=520, mode=Z.MODE_SWIGLU), "bad output mode")  # SwiGLU pairs 8 + 8 columns
     refused(gemm(c=0), "no output")
