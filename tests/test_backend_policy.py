@@ -246,6 +246,29 @@ def test_matmul_groups(h):
     assert piece(n_extra=2) == [4], "at most 4 to a group"
 
 
+def test_a_bias_row_is_not_folded_as_a_residual(h):
+    # the GEMM epilogue adds a [T][N] residual; a bias row ([N], broadcast
+    # over the tokens, Qwen2's q/k/v bias) stays an ADD of its own
+    k, n, t = 2048, 2048, 2048
+    C, W = h.buffer(USAGE_COMPUTE), h.buffer(USAGE_WEIGHTS)
+    base = 0x7f0000000000
+    addr = iter(range(base, base + (64 << 30), 1 << 30))
+
+    def T(type_, ne, name, buf=C):
+        return h.tensor(type_, ne, name, buf, next(addr))
+
+    def plan(second):
+        x = T(F32, [k, t], "x")
+        d = h.mul_mat(T(Q4_K, [k, n], "blk.0.attn_q.weight", W), x, "q", C, next(addr))
+        out = h.add(d, second, name="q_out", buffer=C, data=next(addr))
+        for nd in (d, out):
+            h.supports_op(nd)
+        return h.piece_plan([d, out])
+
+    assert plan(T(F32, [n], "blk.0.attn_q.bias", W))["add"] == 0
+    assert plan(T(F32, [n, t], "resid"))["add"] == 1, "the same piece with a residual folds"
+
+
 def test_piece_plan_folds_the_block_ops(h):
     # what graph_compute folds into its matmul calls: the RMS_NORM (and MUL)
     # before a matmul into the pack, the residual ADD after o/down into the
