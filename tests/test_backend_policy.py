@@ -269,6 +269,37 @@ def test_a_bias_row_is_not_folded_as_a_residual(h):
     assert plan(T(F32, [n, t], "resid"))["add"] == 1, "the same piece with a residual folds"
 
 
+def test_a_swiglu_read_elsewhere_keeps_its_result(h):
+    # the hand-off writes down's packed input instead of the f32 SwiGLU
+    # result: with another reader of that result there is no hand-off (the
+    # gate/up GEMM still applies SwiGLU in its epilogue)
+    k, f, t = 2048, 5632, 2048
+    C, W = h.buffer(USAGE_COMPUTE), h.buffer(USAGE_WEIGHTS)
+    base = 0x7d0000000000
+    addr = iter(range(base, base + (64 << 30), 1 << 30))
+
+    def T(type_, ne, name, buf=C):
+        return h.tensor(type_, ne, name, buf, next(addr))
+
+    def plan(other_reader):
+        x = T(F32, [k, t], "x")
+        g = h.mul_mat(T(Q4_K, [k, f], "blk.0.ffn_gate.weight", W), x, "gate", C, next(addr))
+        u = h.mul_mat(T(Q4_K, [k, f], "blk.0.ffn_up.weight", W), x, "up", C, next(addr))
+        sw = h.glu(g, u, kind=2, name="swiglu", buffer=C, data=next(addr))
+        d = h.mul_mat(T(Q4_K, [f, k], "blk.0.ffn_down.weight", W), sw, "down", C, next(addr))
+        nodes = [g, u, sw, d]
+        if other_reader:
+            nodes.append(h.scale(sw, 0.5, name="other", buffer=C, data=next(addr)))
+        for nd in nodes:
+            h.supports_op(nd)
+        return h.piece_plan(nodes)
+
+    p = plan(False)
+    assert (p["swiglu"], p["handoff"]) == (1, 1), p
+    p = plan(True)
+    assert (p["swiglu"], p["handoff"]) == (1, 0), p
+
+
 def test_piece_plan_folds_the_block_ops(h):
     # what graph_compute folds into its matmul calls: the RMS_NORM (and MUL)
     # before a matmul into the pack, the residual ADD after o/down into the
