@@ -269,6 +269,26 @@ def test_a_bias_row_is_not_folded_as_a_residual(h):
     assert plan(T(F32, [n, t], "resid"))["add"] == 1, "the same piece with a residual folds"
 
 
+def test_a_matmul_result_read_elsewhere_is_not_folded_into_its_add(h):
+    # the folded epilogue writes only the sum: a second reader of the
+    # matmul's own result keeps the ADD separate
+    k, n, t = 2048, 2048, 2048
+    C, W = h.buffer(USAGE_COMPUTE), h.buffer(USAGE_WEIGHTS)
+    base = 0x7c0000000000
+    addr = iter(range(base, base + (64 << 30), 1 << 30))
+
+    def T(type_, ne, name, buf=C):
+        return h.tensor(type_, ne, name, buf, next(addr))
+
+    x = T(F32, [k, t], "x")
+    d = h.mul_mat(T(Q4_K, [k, n], "blk.0.attn_output.weight", W), x, "o", C, next(addr))
+    out = h.add(d, T(F32, [n, t], "resid"), name="o_out", buffer=C, data=next(addr))
+    other = h.scale(d, 2.0, name="other", buffer=C, data=next(addr))
+    for nd in (d, out, other):
+        h.supports_op(nd)
+    assert h.piece_plan([d, out, other])["add"] == 0
+
+
 def test_a_swiglu_read_elsewhere_keeps_its_result(h):
     # the hand-off writes down's packed input instead of the f32 SwiGLU
     # result: with another reader of that result there is no hand-off (the
