@@ -1166,8 +1166,12 @@ piece_plan plan_piece(const std::vector<ggml_tensor *> &nodes, const Set &in_pie
                 ggml_tensor *a = nodes[after];
                 if (op_is(a, "ADD") && (a->src[0] == m || a->src[1] == m) && only_read_by(m, { a })) {
                     const ggml_tensor *r = a->src[0] == m ? a->src[1] : a->src[0];
-                    if (r && f32_contig(r) && same_shape(r, a) && same_shape(m, a) && f32_contig(a) && dev(r) &&
-                        dev(a) && pos(owner(r)) < pos(m)) {
+                    // the epilogue reads each residual element before writing the same
+                    // one: the sum may go in place, or anywhere apart, not half over it
+                    const uintptr_t ad = (uintptr_t) a->data, rd = r ? (uintptr_t) r->data : 0;
+                    const bool placed = r && (ad == rd || ad + ggml_nbytes(a) <= rd || rd + ggml_nbytes(r) <= ad);
+                    if (r && placed && f32_contig(r) && same_shape(r, a) && same_shape(m, a) && f32_contig(a) &&
+                        dev(r) && dev(a) && pos(owner(r)) < pos(m)) {
                         j.add[0] = a;
                         pl.skip[a] = true;
                         pl.counts[3]++;

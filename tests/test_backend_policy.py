@@ -269,6 +269,29 @@ def test_a_bias_row_is_not_folded_as_a_residual(h):
     assert plan(T(F32, [n, t], "resid"))["add"] == 1, "the same piece with a residual folds"
 
 
+def test_a_sum_half_over_its_residual_is_not_folded(h):
+    # the folded epilogue reads each residual element and writes the same one:
+    # the sum in place (x += o) folds, a sum placed part-way over the residual
+    # does not
+    k, n, t = 2048, 2048, 2048
+    C, W = h.buffer(USAGE_COMPUTE), h.buffer(USAGE_WEIGHTS)
+    base = 0x7b0000000000
+    addr = iter(range(base, base + (64 << 30), 1 << 30))
+
+    def plan(out_offset):
+        x = h.tensor(F32, [k, t], "x", C, next(addr))
+        d = h.mul_mat(h.tensor(Q4_K, [k, n], "blk.0.attn_output.weight", W, next(addr)), x, "o", C, next(addr))
+        r_ptr = next(addr)
+        r = h.tensor(F32, [n, t], "resid", C, r_ptr)
+        out = h.add(d, r, name="o_out", buffer=C, data=r_ptr + out_offset)
+        for nd in (d, out):
+            h.supports_op(nd)
+        return h.piece_plan([d, out])["add"]
+
+    assert plan(0) == 1, "in place"
+    assert plan(n * 4 * 16) == 0, "16 rows over"
+
+
 def test_a_matmul_result_read_elsewhere_is_not_folded_into_its_add(h):
     # the folded epilogue writes only the sum: a second reader of the
     # matmul's own result keeps the ADD separate
