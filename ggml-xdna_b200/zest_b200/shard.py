@@ -32,16 +32,20 @@ def slab_width(N: int, world: int, granule: int = GRANULE) -> int:
     return max(shard_rows(N, world, r, granule)[1] for r in range(world))
 
 
-def gather_slabs(slab_out, full_out, world: int, N: int, group=None, granule: int = GRANULE):
+def gather_slabs(slab_out, full_out, world: int, N: int, group=None, granule: int = GRANULE, wire=None):
     """slab_out: this rank's [M][slab_width] output (columns past its slab
     unused); full_out: [M][N]. All-gathers the slabs and writes them into
-    their columns of full_out. Collective: every rank calls it, in order."""
+    their columns of full_out. wire: the dtype the slabs cross the link in
+    (default: their own). torch.bfloat16 halves an f32 gather and loses
+    nothing when the values are bf16-rounded already, as the GEMM's default
+    output is (GGML_XDNA_OUT16=1). Collective: every rank calls it, in order."""
     import torch
     import torch.distributed as dist
 
     M, w = slab_out.shape
-    flat = torch.empty((world * M, w), dtype=slab_out.dtype, device=slab_out.device)
-    dist.all_gather_into_tensor(flat, slab_out.contiguous(), group=group)
+    send = slab_out.contiguous() if wire is None else slab_out.to(wire).contiguous()
+    flat = torch.empty((world * M, w), dtype=send.dtype, device=slab_out.device)
+    dist.all_gather_into_tensor(flat, send, group=group)
     gathered = flat.view(world, M, w)
     for r in range(world):
         lo, n = shard_rows(N, world, r, granule)

@@ -29,7 +29,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank: int, world: int, port: int, q):
+def _rank(rank: int, world: int, port: int, q, wire_bf16: bool = False):
     import sys
     from pathlib import Path
     root = Path(__file__).resolve().parents[1]
@@ -52,22 +52,25 @@ def _rank(rank: int, world: int, port: int, q):
         lo, n = shard_rows(N, world, rank)
         w = slab_width(N, world)
         slab = torch.zeros((M, w), dtype=torch.float32)
+        rounded = O.round_bf16 if wire_bf16 else (lambda a: a)  # the GEMM's default bf16-rounded output
         if n:
-            slab[:, :n] = torch.from_numpy(O.mul_mat(W[lo:lo + n], X))
+            slab[:, :n] = torch.from_numpy(rounded(O.mul_mat(W[lo:lo + n], X)))
         full = torch.full((M, N), float("nan"))
-        gather_slabs(slab, full, world, N)
-        want = O.mul_mat(W, X)
+        gather_slabs(slab, full, world, N, wire=torch.bfloat16 if wire_bf16 else None)
+        want = rounded(O.mul_mat(W, X))
         q.put((rank, bool(np.array_equal(full.numpy(), want))))
     finally:
         dist.destroy_process_group()
 
 
-def test_gather_rebuilds_row_major_product_gloo():
+@pytest.mark.parametrize("wire_bf16", [False, True])
+def test_gather_rebuilds_row_major_product_gloo(wire_bf16):
+    # with bf16-rounded results, bf16 slabs on the wire rebuild them exactly
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, wire_bf16)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
