@@ -60,7 +60,9 @@ __attribute__((visibility("default"))) int ggml_zest_budget_plan(double limit_gb
  * service calls and writes counts[0..5]: fused SwiGLUs, grouped matmul
  * calls, RMS_NORMs folded into a pack, residual ADDs folded into a GEMM
  * epilogue, SwiGLU results handed to the next matmul packed, and
- * RMS_NORM + MUL + ROPE runs done as one kernel. Host logic only; for tests. */
+ * RMS_NORM + MUL + ROPE runs done as one kernel: the ops the reference folds
+ * into its passes over a piece's rows (run_pass and find_fusions,
+ * src/xdna-exec.cpp:368-388,392-431). Host logic only; for tests. */
 __attribute__((visibility("default"))) int ggml_zest_piece_plan(struct ggml_cgraph *cgraph, int *counts);
 
 /* The failure path's host side (src/ggml-zest.cpp:709-755,887-891). After a

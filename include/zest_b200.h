@@ -52,7 +52,8 @@ extern "C" {
 #define ZEST_ERR_TIMEOUT 2u    /* a bounded wait inside a kernel ran out */
 
 int zest_version(void);
-/* Why the last call on this thread failed. */
+/* Why the last call on this thread failed: the reference's `std::string & err`
+ * (xdna_npu::mul_mat and friends, src/xdna-npu.h:40-136). */
 const char *zest_last_error(void);
 
 /* ---------------------------------------------------------------------------
@@ -204,24 +205,26 @@ int zest_mul_mat_noalloc(const float *x, int64_t T, int64_t K, int64_t ldx, cons
 #define ZEST_GLU_GEGLU_QUICK 5
 #define ZEST_ROPE_NORMAL 0 /* ggml rope modes */
 #define ZEST_ROPE_NEOX 2
-/* y = x / sqrt(mean(x^2) + eps), per row of d (RMS_NORM) */
+/* y = x / sqrt(mean(x^2) + eps), per row of d (RMS_NORM; run_rows, src/xdna-exec.cpp:258-269) */
 int zest_rms_norm(const float *x, int64_t rows, int64_t d, float eps, float *y, void *stream);
-/* y = x * w, w one row of d broadcast over every row (MUL by a norm's scale) */
+/* y = x * w, w one row of d broadcast over every row (MUL by a norm's scale;
+ * src/xdna-exec.cpp:271-276) */
 int zest_mul_row(const float *x, const float *w, int64_t rows, int64_t d, float *y, void *stream);
-/* y = x + b, b the same shape or (bias_row) one row of d (ADD) */
+/* y = x + b, b the same shape or (bias_row) one row of d (ADD; src/xdna-exec.cpp:278-288) */
 int zest_add(const float *x, const float *b, int bias_row, int64_t rows, int64_t d, float *y, void *stream);
-/* y = x * s + bias (SCALE) */
+/* y = x * s + bias (SCALE; src/xdna-exec.cpp:290-294) */
 int zest_scale(const float *x, int64_t n, float s, float bias, float *y, void *stream);
 /* y = act(g) * u row by row, g and u with their own row strides (GLU: split
- * tensors, or the two halves of one tensor) */
+ * tensors, or the two halves of one tensor; src/xdna-exec.cpp:296-319) */
 int zest_glu(int kind, const float *g, int64_t g_stride, const float *u, int64_t u_stride, int64_t rows, int64_t f,
              float *y, void *stream);
 /* the [T][n_dims] cos/sin table of positions pos (device), YaRN and optional
  * per-frequency factors ff (device, may be NULL); par (host) = freq_base,
- * freq_scale, ext_factor, attn_factor, beta_fast, beta_slow */
+ * freq_scale, ext_factor, attn_factor, beta_fast, beta_slow
+ * (rope_table, src/xdna-exec.cpp:199-239) */
 int zest_rope_table(const int32_t *pos, int64_t T, int n_dims, int n_ctx_orig, const float *par, const float *ff,
                     float *table, void *stream);
-/* x [T][heads][d] -> y, the first n_dims of each head rotated (ROPE) */
+/* x [T][heads][d] -> y, the first n_dims of each head rotated (ROPE; src/xdna-exec.cpp:321-341) */
 int zest_rope(const float *x, int64_t T, int64_t heads, int64_t d, int n_dims, int mode, const float *table, float *y,
               void *stream);
 
@@ -340,7 +343,8 @@ int zest_mul_mat_group_ex(zest_npu *npu, int n, const zest_wkey *keys, const int
                           float norm_eps, const float *norm_w, float *x_normed, const uint16_t *a_bf16, int64_t T,
                           const zest_mm_out *outs);
 
-/* The service's CUDA stream (a cudaStream_t). */
+/* The service's CUDA stream (a cudaStream_t): the reference's service owns its
+ * NPU queue the same way (xdna_npu, src/xdna-npu.h:40-136). */
 void *zest_stream(zest_npu *npu);
 
 /* Replaces: xdna_npu::take_times (src/xdna-npu.cpp:555-559). */
