@@ -50,7 +50,6 @@ QNAME = {Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", IQ3_S: "IQ3_S"}
 # (name, N, K, input) per projection; projections sharing an input share one pack
 WORKLOADS = {
     "qwen3-4b-layer": dict(config="BASELINE configs[1]: Qwen3-4B-shaped layer, 7 projections", M=8192, qtype=Q4_K,
-                           profiled="down",
                            proj=[("q", 4096, 2560, "attn"), ("k", 1024, 2560, "attn"), ("v", 1024, 2560, "attn"),
                                  ("o", 2560, 4096, "o"), ("gate", 9728, 2560, "ffn"), ("up", 9728, 2560, "ffn"),
                                  ("down", 2560, 9728, "down")]),
@@ -219,17 +218,34 @@ def measured_peaks() -> dict:
     return {"tflops_burst": 1590.0, "tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def profiled_traffic(kernel: str, workload: str):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary for this
-    workload (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch: X'),
-    or None when no capture exists."""
-    p = ROOT / "profiles" / f"{kernel}_{workload}.md"
+def choose_peak(peaks: dict, timed_s: float, clocks: dict) -> tuple[float, str]:
+    """The bf16 roofline denominator for a timed region. MEASURED_PEAKS.json
+    holds cuBLAS's bf16 GEMM timed alone at full clock (burst) and back to
+    back for seconds under the 1 kW cap (sustained). A region of under two
+    seconds, or one whose sampled SM clock stayed near its maximum, runs as
+    the burst did; only a region of seconds whose median clock sat well
+    below the maximum is held to the sustained figure."""
+    sm, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    capped = sm is not None and mx and sm < 0.9 * mx
+    if timed_s >= 2.0 and capped:
+        return peaks["tflops_sustained"], (f"bf16 sustained ({peaks['source']}): {timed_s:.1f} s timed at a median "
+                                           f"{sm:.0f} of {mx:.0f} MHz")
+    return peaks["tflops_burst"], (f"bf16 burst ({peaks['source']}): {timed_s * 1e3:.0f} ms timed at a median "
+                                   f"{sm} of {mx} MHz")
+
+
+def profiled_traffic(workload: str, launch: str):
+    """DRAM bytes (read + write) per launch of `launch` from the committed ncu
+    summary of this workload's K3 launches (profiles/k3_gemm_<workload>.md,
+    a line 'traffic_bytes_per_launch[<launch>]: X'), or None."""
+    p = ROOT / "profiles" / f"k3_gemm_{workload}.md"
     if not p.exists():
         return None
+    key = f"traffic_bytes_per_launch[{launch}]:"
     for ln in p.read_text().splitlines():
-        if ln.startswith("traffic_bytes_per_launch:"):
+        if ln.startswith(key):
             try:
-                return float(ln.split(":", 1)[1].strip())
+                return float(ln[len(key):].strip())
             except ValueError:
                 return None
     return None
@@ -239,66 +255,93 @@ def profiled_traffic(kernel: str, workload: str):
 # the reference's CPU path
 # ---------------------------------------------------------------------------
 
-def cpu_reference_run(w: dict, rows: int, threads: int, raws: dict) -> tuple[float, float]:
-    """xdna_ref_mul_mat (oracle/_ref) over `rows` tokens of every projection,
-    all host threads. Returns (flops, seconds)."""
+def ref_activations(w: dict) -> dict:
+    """Every input of the layer, all M token rows (seeded), for the CPU path."""
     from oracle import oracle as O
-    kinds = {}
-    fl, t = 0.0, 0.0
+    xs = {}
+    for _, _, K, kind in w["proj"]:
+        if kind not in xs:
+            xs[kind] = O.activations(w["M"], K, seed_of(kind, 2), outliers=w.get("outliers", False))
+    return xs
+
+
+def cpu_reference_sample(w: dict, raws: dict, xs: dict, frac: float, threads: int) -> tuple[float, float, int]:
+    """xdna_ref_mul_mat (oracle/_ref; the oracle's port where it is not built)
+    over ALL M token rows and the first max(threads, frac * N) weight rows of
+    every projection. The reference splits its threads over weight rows and
+    streams every token row past each one, so a slice of weight rows costs
+    per flop what the whole weight does. Returns (flops, seconds, rows)."""
+    from oracle import oracle as O
+    M, qt = w["M"], w["qtype"]
+    fl, t, rows = 0.0, 0.0, 0
     for name, N, K, kind in w["proj"]:
-        if kind not in kinds:
-            kinds[kind] = O.activations(rows, K, seed_of(kind, 2), outliers=w.get("outliers", False))
-        x = kinds[kind]
+        n = min(N, max(threads, int(round(N * frac))))
+        raw = raws[name][:n * O.row_bytes(qt, K)]
         t0 = time.perf_counter()
         if O.has_ref():
-            O.ref_mul_mat(w["qtype"], raws[name], N, K, x, n_threads=threads)
+            O.ref_mul_mat(qt, raw, n, K, xs[kind], n_threads=threads)
         else:
-            O.mul_mat(O.dequant(w["qtype"], raws[name], N, K), x, n_threads=threads)
+            O.mul_mat(O.dequant(qt, raw, n, K), xs[kind], n_threads=threads)
         t += time.perf_counter() - t0
-        fl += 2.0 * rows * N * K
-    return fl, t
+        fl += 2.0 * M * n * K
+        rows += n
+    return fl, t, rows
+
+
+def cpu_sample_frac(w: dict, raws: dict, xs: dict, threads: int, seconds: float) -> float:
+    """The weight-row fraction whose sample takes about `seconds` (calibrated
+    on a sample of `threads` rows per projection)."""
+    fl, t, _ = cpu_reference_sample(w, raws, xs, 0.0, threads)
+    return min(1.0, seconds * fl / max(t, 1e-6) / flops(w))
 
 
 def cpu_baseline(w: dict, raws: dict, budget_s: float = 12.0) -> dict:
     from oracle import oracle as O
     threads = os.cpu_count() or 1
-    fl, t = cpu_reference_run(w, 16, threads, raws)  # calibration
-    rows = int(max(16, min(w["M"], 16 * budget_s / max(t, 1e-3))))
-    fl, t = cpu_reference_run(w, rows, threads, raws)
+    xs = ref_activations(w)
+    frac = cpu_sample_frac(w, raws, xs, threads, budget_s)
+    fl, t, rows = cpu_reference_sample(w, raws, xs, frac, threads)
+    total_rows = sum(N for _, N, _, _ in w["proj"])
     return {"value": fl / t / 1e12, "unit": "TFLOP/s", "cores": threads,
             "kind": "reference" if O.has_ref() else "port",
-            "sample": f"{rows} of {w['M']} token rows through every projection ({fl / 1e9:.1f} GFLOP, {t:.1f} s)",
-            "tokens_per_s": rows / t}
+            "sample": f"all {w['M']} token rows x {rows} of the {total_rows} weight rows (every projection's first "
+                      f"{100 * rows / total_rows:.0f} %): {fl / 1e9:.1f} GFLOP in {t:.1f} s",
+            "tokens_per_s": w["M"] * fl / flops(w) / t}
 
 
 def run_reference(args, w: dict) -> None:
+    """The reference's CPU path on the host cores, on our arm's config: each
+    step all M token rows through a slice of every projection's weight rows,
+    the slice sized so the whole run takes about a minute (ZEST_REF_SECONDS)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # the CPU path runs once, on rank 0
     from oracle import oracle as O
     threads = os.cpu_count() or 1
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     raws = {name: weight_raw(w["qtype"], name, N, K, threads) for name, N, K, _ in w["proj"]}
-    # rows per step: a bounded sample sized so all steps take about a minute
-    _, t16 = cpu_reference_run(w, 16, threads, raws)
-    rows = int(max(8, min(128, 16 * 60.0 / (args.steps + args.warmup) / max(t16, 1e-3))))
+    xs = ref_activations(w)
+    budget = float(os.environ.get("ZEST_REF_SECONDS") or 60.0)  # the whole run's CPU time, about
+    frac = cpu_sample_frac(w, raws, xs, threads, budget / (args.steps + args.warmup))
     for _ in range(args.warmup):
-        cpu_reference_run(w, rows, threads, raws)
-    fl, t = 0.0, 0.0
+        cpu_reference_sample(w, raws, xs, frac, threads)
+    fl, t, rows = 0.0, 0.0, 0
     for _ in range(args.steps):
-        f, s = cpu_reference_run(w, rows, threads, raws)
+        f, s_, rows = cpu_reference_sample(w, raws, xs, frac, threads)
         fl += f
-        t += s
+        t += s_
     value = fl / t / 1e12
     kind = "reference" if O.has_ref() else "port"
+    total_rows = sum(N for _, N, _, _ in w["proj"])
+    sample = (f"each step all {w['M']} token rows x {rows} of the {total_rows} weight rows (every projection's "
+              f"first {100 * rows / total_rows:.1f} %), {fl / args.steps / 1e9:.1f} GFLOP")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "none", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "desc": w["config"], "M": w["M"], "weights": QNAME[w["qtype"]],
-                   "sample_rows_per_step": rows},
-        "tokens_per_s": rows * args.steps / t,
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-                         "sample": f"{rows} of {w['M']} token rows through every projection per step"},
+        "scaling": layer_scaling(world, args.mode), "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": layer_config(w, args.workload, world, args.mode),
+        "tokens_per_s": w["M"] * fl / flops(w) / t,
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -306,6 +349,165 @@ def run_reference(args, w: dict) -> None:
 # ---------------------------------------------------------------------------
 # ours
 # ---------------------------------------------------------------------------
+
+def layer_mode(world: int, mode) -> str:
+    """--mode, defaulted: one GPU runs the whole layer; N > 1 the north
+    star's partition, N-slabs of every weight with the output all-gather."""
+    return mode or ("tokens" if world == 1 else "nshard")
+
+
+def layer_scaling(world: int, mode) -> str:
+    if world == 1:
+        return "none"
+    return "weak" if layer_mode(world, mode) == "tokens" else "strong"
+
+
+def layer_config(w: dict, workload: str, world: int, mode) -> dict:
+    """The run's config, the same in both arms."""
+    from zest_b200.shard import slab_width
+    mode = layer_mode(world, mode)
+    nshard = world > 1 and mode != "tokens"
+    M = w["M"]
+    kinds = {}
+    for _, _, K, kind in w["proj"]:
+        kinds.setdefault(kind, K)
+    if not nshard:
+        par = "1 GPU" if world == 1 else f"tokens{world} (each GPU its own {M}-token chunk, no collective)"
+    elif mode == "nshard":
+        par = (f"n-shard{world}: every GPU a slab of each weight's rows (whole 128-row granules), the output "
+               "slabs all-gathered over NCCL as bf16 (exact: the results are bf16-rounded) into ggml's "
+               "row-major f32 [M][N] on every GPU, each gather overlapping the next launch")
+    else:
+        par = f"n-shard{world}, no gather: every GPU a slab of each weight's rows, the output slabs left in place"
+    wbytes = sum((slab_width(N, world) if nshard else N) * K * 2 for _, N, K, _ in w["proj"])
+    return {"workload": workload, "desc": w["config"], "M": M, "weights": QNAME[w["qtype"]],
+            "projections": {name: [N, K] for name, N, K, _ in w["proj"]},
+            "parallelism": par, "global_tokens_per_step": M * (1 if nshard else world),
+            "output": "f32 holding bf16-rounded values (reference default GGML_XDNA_OUT16=1)",
+            "l2": "no flush: each step reads %.0f MB of inputs and weights (> 126 MB L2)" %
+                  ((sum(M * K * 4 for K in kinds.values()) + wbytes) / 1e6)}
+
+
+class LayerStep:
+    """One layer's MUL_MATs on this rank as the bench runs them: per distinct
+    input one K2 pack, then one grouped K3 launch per input (q+k+v, o,
+    gate+up, down), weights converted beforehand (K1) as the reference
+    converts them at load. nshard: this rank's N-slab of every weight; with
+    gather, each launch's output slabs all-gathered (bf16 on the wire) on a
+    side stream while the next launch runs."""
+
+    def __init__(self, w: dict, raws: dict, world: int, rank: int, nshard: bool, gather: bool, Z, torch):
+        from zest_b200.shard import shard_rows, slab_width
+        self.w, self.world, self.nshard, self.gather, self.Z, self.torch = w, world, nshard, gather, Z, torch
+        M, qt = w["M"], w["qtype"]
+        self.bh, self.slabs = {}, {}
+        for name, N, K, _ in w["proj"]:
+            row0, n = shard_rows(N, world, rank) if nshard else (0, N)
+            self.slabs[name] = (row0, n)
+            raw_dev = torch.from_numpy(raws[name]).cuda()
+            _, self.bh[name] = Z.convert_weight(qt, raw_dev, N, K, row0=row0, n_rows=n, want_bytes=False)
+            del raw_dev
+        torch.cuda.synchronize()
+        self.kinds = {}
+        for name, N, K, kind in w["proj"]:
+            self.kinds.setdefault(kind, K)
+        self.x, self.ah = {}, {}
+        gen = torch.Generator("cuda").manual_seed(1234 + (0 if nshard else rank))  # tokens: each rank its own chunk
+        for kind, K in self.kinds.items():
+            self.x[kind] = torch.randn(M, K, device="cuda", generator=gen)
+            if w.get("outliers"):
+                mask = torch.rand(M, K, device="cuda", generator=gen) < 0.01
+                self.x[kind] = torch.where(mask, self.x[kind] * 50, self.x[kind])
+            self.ah[kind] = torch.empty((Z.pad_to(M, 128), K), dtype=torch.int16, device="cuda")
+        width = {name: (slab_width(N, world) if nshard else N) for name, N, *_ in w["proj"]}
+        self.out = {name: torch.zeros((M, max(1, width[name])), dtype=torch.float32, device="cuda")
+                    for name, *_ in w["proj"]}
+        self.full = {name: torch.empty((M, N), dtype=torch.float32, device="cuda")
+                     for name, N, _, _ in w["proj"]} if gather else {}
+        self.err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.stream = torch.cuda.current_stream()
+        self.comm = torch.cuda.Stream() if gather else None
+        self.sp = ctypes.c_void_p(self.stream.cuda_stream)
+        self.groups = launch_groups(w)
+        self.gargs = []
+        for kind, members in self.groups:
+            n = len(members)
+            self.gargs.append((kind, (ctypes.c_void_p * n)(*[self.bh[nm].data_ptr() for nm, _, _ in members]),
+                               (ctypes.c_int64 * n)(*[K for _, _, K in members]),
+                               (ctypes.c_int64 * n)(*[self.slabs[nm][1] for nm, _, _ in members]),
+                               (ctypes.c_int * n)(*[Z.MODE_BF16] * n),
+                               (ctypes.c_void_p * n)(*[self.out[nm].data_ptr() for nm, _, _ in members]),
+                               (ctypes.c_int64 * n)(*[self.out[nm].shape[1] for nm, _, _ in members]), members))
+        self.launches = len(self.kinds) + len(self.groups)
+
+    def step(self, events=None):
+        from zest_b200.shard import gather_slabs
+        torch, Z, L = self.torch, self.Z, self.Z.lib()
+        M = self.w["M"]
+        for kind, K in self.kinds.items():
+            rc = L.zest_pack_activations(ctypes.c_void_p(self.x[kind].data_ptr()), M, K, K, self.ah[kind].shape[0],
+                                         None, ctypes.c_void_p(self.ah[kind].data_ptr()), K, self.sp)
+            if rc:
+                raise Z.ZestError(L.zest_last_error().decode())
+        for i, (kind, bp, ldb, ns, modes, cp, ldc, members) in enumerate(self.gargs):
+            K = self.kinds[kind]
+            if events is not None:
+                events[i][0].record(self.stream)
+            rc = L.zest_gemm_group(ctypes.c_void_p(self.ah[kind].data_ptr()), K, M, K, len(members), bp, ldb, ns,
+                                   modes, cp, ldc, ctypes.c_void_p(self.err.data_ptr()), self.sp)
+            if events is not None:
+                events[i][1].record(self.stream)
+            if rc:
+                raise Z.ZestError(L.zest_last_error().decode())
+            if self.gather:
+                # the gather of this launch's slabs overlaps the next launch
+                self.comm.wait_stream(self.stream)
+                with torch.cuda.stream(self.comm):
+                    for name, N, _ in members:
+                        gather_slabs(self.out[name], self.full[name], self.world, N, wire=torch.bfloat16)
+        if self.gather:
+            self.stream.wait_stream(self.comm)
+
+    def timed(self, steps: int, warmup: int, local: int, clocked: bool = True):
+        """(ms per step on this rank, per-launch ms, clock summary)."""
+        import torch.distributed as dist
+        from zest_b200.shard import any_rank
+        torch, Z = self.torch, self.Z
+        for _ in range(warmup):
+            self.step()
+        torch.cuda.synchronize()
+        if any_rank(int(self.err.item()) != 0):  # every rank stops together
+            raise Z.ZestError(f"device error bits {int(self.err.item()):#x} during warm-up (this rank)")
+        mk = lambda: [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        ev = [[mk() for _ in self.groups] for _ in range(steps)]
+        t0, t1 = mk()
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            t0.record(self.stream)
+            for s_ in range(steps):
+                self.step(ev[s_])
+            t1.record(self.stream)
+            torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier()
+        if any_rank(int(self.err.item()) != 0):
+            raise Z.ZestError(f"device error bits {int(self.err.item()):#x} in the timed region (this rank)")
+        ms = t0.elapsed_time(t1) / steps
+        gemm_ms = [sum(ev[s_][i][0].elapsed_time(ev[s_][i][1]) for s_ in range(steps)) / steps
+                   for i in range(len(self.groups))]
+        return ms, gemm_ms, clocks.summary()
+
+
+def max_over_ranks(v: float, world: int, torch) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
 
 def run_ours(args, w: dict) -> None:
     import torch
@@ -324,141 +526,59 @@ def run_ours(args, w: dict) -> None:
     if w["qtype"] == IQ3_S:
         Z.load_iq3s_grid()
     M, qt = w["M"], w["qtype"]
+    mode = layer_mode(world, args.mode)
+    nshard = world > 1 and mode != "tokens"
+    gather = nshard and mode == "nshard"
+    raws = {name: weight_raw(qt, name, N, K, threads) for name, N, K, _ in w["proj"]}
 
-    # tokens: every rank its own prompt chunk through whole weights (no
-    # collective); nshard: every rank an N-slab of each weight, outputs
-    # all-gathered into ggml's row-major [M][N]
-    from zest_b200.shard import any_rank, gather_slabs, shard_rows, slab_width
-    nshard = world > 1 and args.mode != "tokens"
-    gather = nshard and args.mode == "nshard"
+    layer = LayerStep(w, raws, world, rank, nshard, gather, Z, torch)
+    ms, gemm_ms, clocks = layer.timed(args.steps, args.warmup, local)
+    ms_max = max_over_ranks(ms, world, torch)
+    groups, slabs = layer.groups, layer.slabs
+    launches = layer.launches
+    del layer
+    torch.cuda.empty_cache()
 
-    # --- load: every projection's (slab of) weight converted once (K1) ---------
-    raws, bh, slabs = {}, {}, {}
-    for name, N, K, _ in w["proj"]:
-        raws[name] = weight_raw(qt, name, N, K, threads)
-        row0, n = shard_rows(N, world, rank) if nshard else (0, N)
-        slabs[name] = (row0, n)
-        raw_dev = torch.from_numpy(raws[name]).cuda()
-        _, bh[name] = Z.convert_weight(qt, raw_dev, N, K, row0=row0, n_rows=n, want_bytes=False)
-        del raw_dev
-    torch.cuda.synchronize()
-
-    # --- inputs and outputs ------------------------------------------------
-    kinds = {}
-    for name, N, K, kind in w["proj"]:
-        kinds.setdefault(kind, K)
-    x, ah = {}, {}
-    gen = torch.Generator("cuda").manual_seed(1234 + (0 if nshard else rank))  # tokens: each rank its own chunk
-    for kind, K in kinds.items():
-        x[kind] = torch.randn(M, K, device="cuda", generator=gen)
-        if w.get("outliers"):
-            mask = torch.rand(M, K, device="cuda", generator=gen) < 0.01
-            x[kind] = torch.where(mask, x[kind] * 50, x[kind])
-        ah[kind] = torch.empty((Z.pad_to(M, 128), K), dtype=torch.int16, device="cuda")
-    width = {name: (slab_width(N, world) if nshard else N) for name, N, *_ in w["proj"]}
-    out = {name: torch.zeros((M, max(1, width[name])), dtype=torch.float32, device="cuda") for name, *_ in w["proj"]}
-    full = {}
-    if gather:
-        for name, N, K, _ in w["proj"]:
-            full[name] = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    stream = torch.cuda.current_stream()
-    L = Z.lib()
-    sp = ctypes.c_void_p(stream.cuda_stream)
-
-    # one K3 launch per input: the projections that share it (q, k, v; gate, up)
-    # are the segments of one grouped launch
-    groups = launch_groups(w)
-    gargs = []
-    for kind, members in groups:
-        n = len(members)
-        gargs.append((kind, (ctypes.c_void_p * n)(*[bh[name].data_ptr() for name, _, _ in members]),
-                      (ctypes.c_int64 * n)(*[K for _, _, K in members]),
-                      (ctypes.c_int64 * n)(*[slabs[name][1] for name, _, _ in members]),
-                      (ctypes.c_int * n)(*[Z.MODE_BF16] * n),
-                      (ctypes.c_void_p * n)(*[out[name].data_ptr() for name, _, _ in members]),
-                      (ctypes.c_int64 * n)(*[out[name].shape[1] for name, _, _ in members]), members))
-
-    def step(events=None):
-        for kind, K in kinds.items():
-            rc = L.zest_pack_activations(ctypes.c_void_p(x[kind].data_ptr()), M, K, K, ah[kind].shape[0], None,
-                                         ctypes.c_void_p(ah[kind].data_ptr()), K, sp)
-            if rc:
-                raise Z.ZestError(L.zest_last_error().decode())
-        for i, (kind, bp, ldb, ns, modes, cp, ldc, members) in enumerate(gargs):
-            K = kinds[kind]
-            if events is not None:
-                events[i][0].record(stream)
-            rc = L.zest_gemm_group(ctypes.c_void_p(ah[kind].data_ptr()), K, M, K, len(members), bp, ldb, ns, modes,
-                                   cp, ldc, ctypes.c_void_p(err.data_ptr()), sp)
-            if events is not None:
-                events[i][1].record(stream)
-            if rc:
-                raise Z.ZestError(L.zest_last_error().decode())
-            if gather:
-                for name, N, _ in members:
-                    gather_slabs(out[name], full[name], world, N)
-
-    # --- warm-up, then K timed steps ---------------------------------------
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if any_rank(int(err.item()) != 0):  # every rank stops together
-        raise Z.ZestError(f"device error bits {int(err.item()):#x} during warm-up (this rank)")
-    ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in groups]
-          for _ in range(args.steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        t0.record(stream)
-        for s in range(args.steps):
-            step(ev[s])
-        t1.record(stream)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms = t0.elapsed_time(t1) / args.steps
-    gemm_ms = [sum(ev[s][i][0].elapsed_time(ev[s][i][1]) for s in range(args.steps)) / args.steps
-               for i in range(len(groups))]
-    if any_rank(int(err.item()) != 0):
-        raise Z.ZestError(f"device error bits {int(err.item()):#x} in the timed region (this rank)")
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    # N > 1 with the N-shard: the token split's figure beside it (every rank
+    # its own chunk through whole weights, no collective)
+    tokens_leg = None
+    if nshard:
+        tl = LayerStep(w, raws, world, rank, False, False, Z, torch)
+        t_ms, _, _ = tl.timed(args.steps, args.warmup, local)
+        del tl
+        torch.cuda.empty_cache()
+        t_max = max_over_ranks(t_ms, world, torch)
+        tokens_leg = {"value": world * flops(w) / (t_max * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": t_max,
+                      "parallelism": f"tokens{world}: each GPU its own {M}-token chunk through whole weights, "
+                                     "no collective (weak scaling)"}
 
     total_flops = flops(w) * (1 if nshard else world)  # the whole job: all ranks' tokens
     local_gemm_flops = sum(2.0 * M * slabs[name][1] * K for name, N, K, _ in w["proj"])
     peaks = measured_peaks()
+    peak, peak_kind = choose_peak(peaks, ms * args.steps * 1e-3, clocks)
     gemm_total_ms = sum(gemm_ms)
-    # the roofline's launch: the group holding the profiled projection (the
-    # one the committed ncu capture profiles), else the one with the most work
+    # the roofline's launch: the one with the most work (gate+up at C2)
     gflops = [sum(2.0 * M * slabs[name][1] * K for name, _, K in members) for _, members in groups]
-    names = [[name for name, _, _ in members] for _, members in groups]
-    top = next((i for i, ns in enumerate(names) if w.get("profiled") in ns), None)
-    if top is None:
-        top = max(range(len(groups)), key=lambda i: gflops[i])
-    top_flops = gflops[top]
+    names = ["+".join(name for name, _, _ in members) for _, members in groups]
+    top = max(range(len(groups)), key=lambda i: gflops[i])
     top_desc = " + ".join(f"{name} {M}x{slabs[name][1]}x{K}" for name, _, K in groups[top][1])
-    achieved = top_flops / (gemm_ms[top] * 1e-3) / 1e12
-    traffic = profiled_traffic("k3_gemm", args.workload) if world == 1 else None
+    achieved = gflops[top] / (gemm_ms[top] * 1e-3) / 1e12
+    traffic = profiled_traffic(args.workload, names[top]) if world == 1 else None
+    algo_bytes = sum(2.0 * M * K + 2.0 * slabs[name][1] * K + 4.0 * M * slabs[name][1]
+                     for name, _, K in groups[top][1])
+    algo_bytes -= 2.0 * M * groups[top][1][0][2] * (len(groups[top][1]) - 1)  # one A per launch
 
     # --- end to end through the C ABI, host buffers: each rank its own chunk ----
-    e2e = None
-    if not nshard:
-        if world > 1:
-            dist.barrier()
-        e2e = e2e_run(args, w, raws, Z, torch)
-        if world > 1:
-            t = torch.tensor([e2e["ms_per_step"]], dtype=torch.float64, device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e["ms_per_step"] = float(t.item())
-            e2e["value"] = world * flops(w) / (e2e["ms_per_step"] * 1e-3) / 1e12
-            e2e["tokens_per_s"] = world * M / (e2e["ms_per_step"] * 1e-3)
-            e2e["h2d_bytes_per_step"] *= world
-            e2e["d2h_bytes_per_step"] *= world
+    if world > 1:
+        dist.barrier()
+    e2e = e2e_run(args, w, raws, Z, torch)
+    if world > 1:
+        e2e["ms_per_step"] = max_over_ranks(e2e["ms_per_step"], world, torch)
+        e2e["value"] = world * flops(w) / (e2e["ms_per_step"] * 1e-3) / 1e12
+        e2e["tokens_per_s"] = world * M / (e2e["ms_per_step"] * 1e-3)
+        e2e["h2d_bytes_per_step"] *= world
+        e2e["d2h_bytes_per_step"] *= world
+        e2e["api"] += f"; each of the {world} GPUs its own {M}-token chunk"
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -469,32 +589,31 @@ def run_ours(args, w: dict) -> None:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-            "scaling": ("strong" if nshard else "weak") if world > 1 else "none", "vs_baseline": None,
+            "scaling": layer_scaling(world, args.mode), "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": args.workload, "desc": w["config"], "M": M, "weights": QNAME[qt],
-                       "projections": {name: [N, K] for name, N, K, _ in w["proj"]},
-                       "parallelism": (f"n-shard{world}" + ("+allgather" if gather else "")) if nshard else
-                                      f"tokens{world} (each GPU its own {M}-token chunk, no collective)",
-                       "global_tokens_per_step": M * (1 if nshard else world),
-                       "output": "f32 holding bf16-rounded values (reference default GGML_XDNA_OUT16=1)",
-                       "l2": "no flush: each step reads %.0f MB of inputs and weights (> 126 MB L2)" %
-                             (sum(M * K * 4 for K in kinds.values()) / 1e6 +
-                              sum(slabs[n][1] * K * 2 for n, N, K, _ in w["proj"]) / 1e6)},
+            "config": layer_config(w, args.workload, world, args.mode),
             "tokens_per_s": M * (1 if nshard else world) / (ms_max * 1e-3),
-            "pct_of_bf16_peak": 100.0 * value / (world * peaks["tflops_sustained"]),
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["tflops_sustained"],
-                         "unit": "TFLOP/s", "frac": achieved / peaks["tflops_sustained"],
-                         "traffic": traffic,
-                         "kernel": "k3 gemm_bf16_tc_pair_kernel<256> (the stream-K instance at K >= 8192 with a full wave, or a quarter of the pair-slots idle at K >= 4096)",
-                         "launch": f"{top_desc}: {top_flops / 1e9:.1f} GFLOP, {gemm_ms[top] * 1e3:.1f} us avg",
-                         "peak_kind": f"bf16 sustained ({peaks['source']})", "peak_burst": peaks["tflops_burst"],
+            "pct_of_bf16_peak": 100.0 * value / (world * peak),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "traffic_vs_algorithmic": traffic / algo_bytes if traffic else None,
+                         "algorithmic_bytes": algo_bytes,
+                         "kernel": "k3 gemm_bf16_tc_pair_kernel<256> (whole tiles; the stream-K instance where "
+                                   "zest_plan_gemm says so)",
+                         "launch": f"{top_desc}: {gflops[top] / 1e9:.1f} GFLOP, {gemm_ms[top] * 1e3:.1f} us avg",
+                         "peak_kind": peak_kind, "peak_burst": peaks["tflops_burst"],
+                         "peak_sustained": peaks["tflops_sustained"],
+                         "per_launch": {n: {"us": round(t * 1e3, 1), "tflops": round(f / (t * 1e-3) / 1e12, 1),
+                                            "frac": round(f / (t * 1e-3) / 1e12 / peak, 3)}
+                                        for n, t, f in zip(names, gemm_ms, gflops)},
                          "all_gemms": {"ms_per_step": gemm_total_ms,
                                        "tflops": local_gemm_flops / (gemm_total_ms * 1e-3) / 1e12,
-                                       "per_launch_us": {"+".join(ns): round(t * 1e3, 1)
-                                                         for ns, t in zip(names, gemm_ms)}}},
-            "gpu_launches": args.steps * (len(kinds) + len(groups)),
-            "clocks": clocks.summary(),
+                                       "frac": local_gemm_flops / (gemm_total_ms * 1e-3) / 1e12 / peak}},
+            "gpu_launches": args.steps * launches,
+            "clocks": clocks,
         }
+        if tokens_leg:
+            line["tokens_mode"] = tokens_leg
         if e2e:
             line["e2e"] = e2e
         if cpu:
@@ -1005,6 +1124,8 @@ def run_model(args, w: dict) -> None:
     down_fl = 2.0 * CH * H * F
     achieved = down_fl / (per_launch["down"] * 1e-3) / 1e12
     peaks = measured_peaks()
+    clk = clocks.summary()
+    peak, peak_kind = choose_peak(peaks, ms * steps * 1e-3, clk)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         lw = WORKLOADS["qwen3-4b-layer"]
@@ -1046,19 +1167,19 @@ def run_model(args, w: dict) -> None:
                              "note": "eager prefills with events around each launch; the rest is the small ops, "
                                      "packs, cache writes, the unclaimed tail, the LM head and the host gaps"},
             "load": {"weight_conversion_s": m.load_s, "layers": nL},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["tflops_sustained"],
-                         "unit": "TFLOP/s", "frac": achieved / peaks["tflops_sustained"], "traffic": None,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
                          "kernel": "k3 gemm_bf16_tc_pair_kernel",
                          "launch": f"down {CH}x{H}x{F}: {down_fl / 1e9:.1f} GFLOP, "
                                    f"{per_launch['down'] * 1e3:.1f} us avg over layers and chunks",
-                         "peak_kind": f"bf16 sustained ({peaks['source']})"},
+                         "peak_kind": peak_kind},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": P * 8 * world,
                     "d2h_bytes_per_step": c["vocab"] * 4 * world,
                     "api": "token ids in, last-token logits out; claimed ops through include/zest_b200.h"},
             "gpu_launches": steps * len(claimed) * (1 + nL * (Prefill.LAUNCHES_PER_LAYER_FUSED if m.fused
                                                               else Prefill.LAUNCHES_PER_LAYER)),
             "steps_note": f"{steps} timed prefills of {P} tokens (--steps capped at 20 for this workload)",
-            "clocks": clocks.summary(),
+            "clocks": clk,
         }
         if cpu:
             line["cpu_baseline"] = cpu
@@ -1151,6 +1272,15 @@ def run_tp(args, w: dict) -> None:
         except Exception as e:  # fall back to NCCL
             mc = {}
             reduce_how = f"NCCL all-reduce (multicast unavailable: {type(e).__name__}: {e})"
+        # the ranks take the same collective steps: if any rank has no
+        # multicast buffers, every rank sums through NCCL
+        if any_rank(not mc):
+            if mc:
+                reduce_how = "NCCL all-reduce (multicast unavailable on another rank)"
+            mc = {}
+            for name, N, K, kind in w["proj"]:
+                if kind in ksh:
+                    out[name] = torch.zeros((M, max(1, n_of[name])), dtype=torch.float32, device="cuda")
     tick = torch.zeros(1, dtype=torch.float32, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
@@ -1256,6 +1386,8 @@ def run_tp(args, w: dict) -> None:
     gemm_ms = [sum(ev[s][gi][ci][0].elapsed_time(ev[s][gi][ci][1]) for s in range(args.steps)
                    for ci in range(len(chunks))) / args.steps for gi in range(len(groups))]
     peaks = measured_peaks()
+    clk = clocks.summary()
+    peak, peak_kind = choose_peak(peaks, ms * args.steps * 1e-3, clk)
     if rank == 0:
         value = flops(w) / (ms_max * 1e-3) / 1e12
         names = ["+".join(nm for nm, _, _ in members) for _, members in groups]
@@ -1271,11 +1403,11 @@ def run_tp(args, w: dict) -> None:
                                   "f32 sums of the partials on every rank",
                        "global_tokens_per_step": M},
             "tokens_per_s": M / (ms_max * 1e-3),
-            "pct_of_bf16_peak": 100.0 * value / (world * peaks["tflops_sustained"]),
+            "pct_of_bf16_peak": 100.0 * value / (world * peak), "peak_kind": peak_kind,
             "per_rank_gemm_us": {nm: round(v * 1e3, 1) for nm, v in zip(names, gemm_ms)},
             "reduce_check": check,
             "gpu_launches": args.steps * len(chunks) * (len(kinds) + len(groups)),
-            "clocks": clocks.summary(),
+            "clocks": clk,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -1297,10 +1429,10 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--mode", choices=["tokens", "nshard", "nshard-nogather", "tp"], default="tokens",
-                    help="N>1: each GPU its own token chunk (default, no collective), N-slabs of every weight "
-                         "with (nshard) or without the NCCL all-gather of the output slabs, or the layer as "
-                         "one tensor-parallel block (tp: o/down K-sharded, one all-reduce per row chunk)")
+    ap.add_argument("--mode", choices=["tokens", "nshard", "nshard-nogather", "tp"], default=None,
+                    help="N>1: N-slabs of every weight with (nshard, the default) or without the NCCL all-gather "
+                         "of the output slabs, each GPU its own token chunk (tokens, no collective), or the layer "
+                         "as one tensor-parallel block (tp: o/down K-sharded, one all-reduce per row chunk)")
     ap.add_argument("--tp-chunks", type=int, default=1, help="tp with NCCL: row chunks whose all-reduce overlaps the next")
     ap.add_argument("--tp-reduce", choices=["multicast", "nccl"], default="nccl",
                     help="tp: K-sharded partials summed by NCCL, or in the GEMM epilogue through NVLink multicast "

@@ -146,23 +146,29 @@ struct sibling_t {
     ggml_backend_buffer_type_t buft = nullptr;
 };
 
+// The device whose buffers we share: llama.cpp's CUDA<n> by its name, or,
+// registered under another name, the first GPU device that is not this
+// plugin's own.
+ggml_backend_dev_t find_sibling() {
+    char want[32];
+    snprintf(want, sizeof want, "CUDA%d", cuda_device());
+    if (ggml_backend_dev_t by_name = ggml_backend_dev_by_name(want)) return by_name;
+    auto other_gpu = [](ggml_backend_dev_t c) {
+        const enum ggml_backend_dev_type t = ggml_backend_dev_type(c);
+        const bool gpu = t == GGML_BACKEND_DEVICE_TYPE_GPU || t == GGML_BACKEND_DEVICE_TYPE_IGPU;
+        return gpu && std::string(ggml_backend_dev_name(c)) != GGML_XDNA_DEVICE_NAME;
+    };
+    const size_t n = ggml_backend_dev_count();
+    size_t i = 0;
+    while (i < n && !other_gpu(ggml_backend_dev_get(i))) i++;
+    return i < n ? ggml_backend_dev_get(i) : nullptr;
+}
+
 const sibling_t &sibling() {
     static sibling_t s;
     static std::once_flag once;
     std::call_once(once, [] {
-        char name[32];
-        snprintf(name, sizeof name, "CUDA%d", cuda_device());
-        ggml_backend_dev_t d = ggml_backend_dev_by_name(name);
-        if (!d)
-            for (size_t i = 0; i < ggml_backend_dev_count(); i++) {
-                ggml_backend_dev_t c = ggml_backend_dev_get(i);
-                const enum ggml_backend_dev_type t = ggml_backend_dev_type(c);
-                if ((t == GGML_BACKEND_DEVICE_TYPE_GPU || t == GGML_BACKEND_DEVICE_TYPE_IGPU) &&
-                    strcmp(ggml_backend_dev_name(c), GGML_XDNA_DEVICE_NAME) != 0) {
-                    d = c;
-                    break;
-                }
-            }
+        ggml_backend_dev_t d = find_sibling();
         if (!d) {
             log_line("", "no CUDA device registered; " GGML_XDNA_DEVICE_NAME " works next to one");
             return;
@@ -346,9 +352,50 @@ bool budget_takes(const ggml_tensor *w) {
 
 int64_t op_batch(const ggml_tensor *op) { return op_is(op, "MUL_MAT") ? op->ne[1] : ggml_nrows(op); }
 
+// ggml's IQ3_S codebook (512 entries of four magnitudes), read back through
+// the host ggml's own to_float, the dequantiser the reference converts every
+// weight type with (src/xdna-npu.cpp:339-348), so no table is built in. One
+// 256-value block per entry i: scale 1 (fp16 d = 1, scale nibbles 0), no
+// signs, and every 9-bit grid index equal to i (the low byte in all of qs,
+// the high bit in all of qh). to_float then gives entry i's four bytes as the
+// block's first four values, and every later group of four repeats them.
+// Empty when ggml has no IQ3_S dequantiser or it does not answer that way;
+// the GPU converter then does not take IQ3_S.
+const std::vector<uint32_t> &iq3s_codebook() {
+    static const std::vector<uint32_t> grid = []() -> std::vector<uint32_t> {
+        const ggml_type_traits *tr = ggml_get_type_traits(GGML_TYPE_IQ3_S);
+        if (!tr || !tr->to_float) return {};
+        constexpr int QS = 2, QH = QS + 64, SIGNS = QH + 8, SCALES = SIGNS + 32, BLOCK = SCALES + 4;
+        static_assert(BLOCK == 110, "block_iq3_s is 110 bytes");
+        std::vector<uint32_t> g(512);
+        uint8_t blk[BLOCK];
+        float y[256];
+        for (int i = 0; i < 512; i++) {
+            memset(blk, 0, sizeof blk);
+            blk[0] = 0x00;  // d = 1.0 as fp16 (0x3c00), little-endian
+            blk[1] = 0x3c;
+            memset(blk + QS, i & 0xff, 64);
+            memset(blk + QH, i >= 256 ? 0xff : 0x00, 8);
+            tr->to_float(blk, y, 256);
+            uint32_t e = 0;
+            for (int j = 0; j < 4; j++) {
+                const float v = y[j];
+                if (!(v >= 0.0f && v <= 255.0f) || v != (float) (int) v) return {};
+                e |= (uint32_t) v << (8 * j);
+            }
+            for (int j = 4; j < 256; j++)
+                if (y[j] != y[j % 4]) return {};
+            g[i] = e;
+        }
+        return g;
+    }();
+    return grid;
+}
+
 bool native_type(int t) {
+    if (t == GGML_TYPE_IQ3_S) return !iq3s_codebook().empty();
     return t == GGML_TYPE_F32 || t == GGML_TYPE_F16 || t == GGML_TYPE_Q8_0 || t == GGML_TYPE_Q4_K ||
-           t == GGML_TYPE_Q6_K || t == GGML_TYPE_IQ3_S;
+           t == GGML_TYPE_Q6_K;
 }
 
 // The weight side of a matmul we can take: a plain 2D leaf (not a view, not
@@ -524,6 +571,31 @@ void trace_piece(ggml_cgraph *cgraph) {
     }
 }
 
+// GGML_XDNA_BLOCK_OPS, when set, names the small ops block claiming may take
+// (op names split at commas); unset, it may take every op exec_supports runs.
+bool block_op_allowed(const ggml_tensor *op) {
+    struct allow_list {
+        bool given = false;
+        std::unordered_set<std::string> names;
+    };
+    static const allow_list allow = [] {
+        allow_list a;
+        const char *v = zenv("GGML_XDNA_BLOCK_OPS");
+        if (!v) return a;
+        a.given = true;
+        std::string s(v);
+        size_t from = 0;
+        while (from <= s.size()) {
+            size_t to = s.find(',', from);
+            if (to == std::string::npos) to = s.size();
+            if (to > from) a.names.insert(s.substr(from, to - from));
+            from = to + 1;
+        }
+        return a;
+    }();
+    return !allow.given || allow.names.count(ggml_op_name(op->op)) > 0;
+}
+
 // The whole policy (src/ggml-zest.cpp:1182-1226): a matmul we can take, or a
 // small op the GPU runs that covers a prompt-sized batch, keeps its
 // parameters in plain leaves, cannot have its result placed in host memory,
@@ -532,16 +604,7 @@ bool policy(const ggml_tensor *op, int depth = 0) {
     if (op_is(op, "MUL_MAT")) return claim_mul_mat(op);
     if (!blocks() || depth > 8) return false;
     if (!op_is(op, "RESHAPE") && tokens_of(op) < min_batch()) return false;
-    if (!exec_supports(op)) return false;
-    {
-        // GGML_XDNA_BLOCK_OPS: a comma list of the small ops block claiming may take
-        static const std::string allow = [] {
-            const char *s = zenv("GGML_XDNA_BLOCK_OPS");
-            return s ? "," + std::string(s) + "," : std::string();
-        }();
-        if (!allow.empty() && allow.find("," + std::string(ggml_op_name(op->op)) + ",") == std::string::npos)
-            return false;
-    }
+    if (!exec_supports(op) || !block_op_allowed(op)) return false;
     if (const ggml_tensor *w = exec_param(op))
         if (w->op != GGML_OP_NONE || w->view_src) return false;
     for (int j = 0; j < GGML_MAX_SRC; j++)
@@ -558,22 +621,8 @@ bool policy(const ggml_tensor *op, int depth = 0) {
 // the backend context (src/ggml-zest.cpp:184-423)
 // ---------------------------------------------------------------------------
 
-// The CUDA backend's own instance, for a piece that failed here, and its
-// buffer for the piece's host-memory inputs (grown as needed).
-struct sibling_run {
-    ggml_backend_t backend = nullptr;
-    ggml_backend_buffer_t in = nullptr;
-    size_t in_size = 0;
-    int64_t runs = 0;
-    ~sibling_run() {
-        if (in) ggml_backend_buffer_free(in);
-        if (backend) ggml_backend_free(backend);
-    }
-};
-
 struct context {
     zest_npu *npu = nullptr;
-    sibling_run again;  // failed pieces run again on the CUDA backend
     std::vector<float> host_values;  // a weight of a type without a GPU converter, dequantised
     std::vector<uint8_t> host_raw;
     float *stage_x = nullptr, *stage_y = nullptr;
@@ -728,125 +777,6 @@ void backend_free(ggml_backend_t backend) {
 const ggml_tensor *owner(const ggml_tensor *t) {
     while (t->view_src) t = t->view_src;
     return t;
-}
-
-// ---------------------------------------------------------------------------
-// a failed piece, run again on the CUDA backend (src/ggml-zest.cpp:709-755,
-// 887-891: the reference runs it again on its Vulkan sibling)
-// ---------------------------------------------------------------------------
-
-// GGML_ZEST_RERUN=0 leaves a failed piece failed (GGML_STATUS_FAILED).
-bool rerun_on() {
-    static const bool v = env_int("GGML_ZEST_RERUN", 1) != 0;
-    return v;
-}
-
-// Whether running the piece again reads what its first run read. The
-// reference's piece writes nothing back until it has finished; here results
-// go to their tensors as each op runs, and ggml's allocator may have put a
-// result on the memory of a piece input it outlives. So: no result the first
-// run may have written (the compute nodes up to the one that failed, and
-// every result folded into an earlier node's job) may overlap an input.
-bool rerun_safe(const std::vector<ggml_tensor *> &nodes, size_t failed_at,
-                const std::unordered_map<const ggml_tensor *, bool> &folded) {
-    struct range {
-        uintptr_t lo, hi;
-    };
-    auto span = [](const ggml_tensor *t) {
-        const uintptr_t lo = (uintptr_t) t->data;
-        return range{ lo, lo + ggml_nbytes(t) };
-    };
-    const std::unordered_set<const ggml_tensor *> made(nodes.begin(), nodes.end());
-    std::vector<range> written, inputs;
-    for (size_t k = 0; k < nodes.size(); k++)
-        if ((k <= failed_at || folded.count(nodes[k])) && nodes[k]->data) written.push_back(span(nodes[k]));
-    for (const ggml_tensor *n : nodes)
-        for (int j = 0; j < GGML_MAX_SRC; j++) {
-            const ggml_tensor *src = n->src[j];
-            if (!src || !src->data || made.count(src) || made.count(owner(src))) continue;
-            inputs.push_back(span(src));
-        }
-    for (const range &w : written)
-        for (const range &in : inputs)
-            if (w.lo < in.hi && in.lo < w.hi) return false;
-    return true;
-}
-
-// The piece on the CUDA backend; inputs in host memory (rotary positions)
-// move into CUDA memory for the call, and the tensors point back after it.
-bool sibling_compute(sibling_run &sr, ggml_cgraph *g, std::string &err) {
-    const sibling_t &sb = sibling();
-    if (!sb.dev || !sb.buft) {
-        err = "no CUDA backend to run it";
-        return false;
-    }
-    if (!sr.backend && !(sr.backend = ggml_backend_dev_init(sb.dev, nullptr))) {
-        err = "cannot start the CUDA backend";
-        return false;
-    }
-    std::vector<ggml_tensor *> owners, views;
-    std::unordered_set<const ggml_tensor *> seen;
-    const int n = ggml_graph_n_nodes(g);
-    for (int i = 0; i < n; i++) {
-        ggml_tensor *node = ggml_graph_node(g, i);
-        for (int j = 0; j < GGML_MAX_SRC; j++) {
-            ggml_tensor *src = node->src[j];
-            if (!src || !is_host(src) || !seen.insert(src).second) continue;
-            if (!src->view_src) {
-                owners.push_back(src);
-                continue;
-            }
-            views.push_back(src);
-            ggml_tensor *root = src;
-            while (root->view_src) root = root->view_src;
-            if (seen.insert(root).second) owners.push_back(root);
-        }
-    }
-    const size_t align = ggml_backend_buft_get_alignment(sb.buft);
-    auto padded = [align](size_t b) { return (b + align - 1) / align * align; };
-    size_t need = 0;
-    for (const ggml_tensor *o : owners) need += padded(ggml_nbytes(o));
-    if (need > sr.in_size) {
-        if (sr.in) ggml_backend_buffer_free(sr.in);
-        sr.in = ggml_backend_buft_alloc_buffer(sb.buft, need);
-        sr.in_size = sr.in ? need : 0;
-        if (!sr.in) {
-            err = "cannot hold the piece's host-memory inputs in CUDA memory";
-            return false;
-        }
-    }
-    // each view's place in its owner, taken before the owners move
-    std::vector<size_t> view_off;
-    for (const ggml_tensor *v : views) view_off.push_back((size_t) ((const char *) v->data - (const char *) owner(v)->data));
-    struct place {
-        ggml_tensor *t;
-        ggml_backend_buffer_t buffer;
-        void *data;
-    };
-    std::vector<place> moved;
-    char *base = owners.empty() ? nullptr : (char *) ggml_backend_buffer_get_base(sr.in);
-    size_t off = 0;
-    for (ggml_tensor *o : owners) {
-        moved.push_back({ o, o->buffer, o->data });
-        o->buffer = sr.in;
-        o->data = base + off;
-        ggml_backend_tensor_set(o, moved.back().data, 0, ggml_nbytes(o));
-        off += padded(ggml_nbytes(o));
-    }
-    for (size_t i = 0; i < views.size(); i++) {
-        ggml_tensor *v = views[i];
-        moved.push_back({ v, v->buffer, v->data });
-        v->buffer = sr.in;
-        v->data = (char *) owner(v)->data + view_off[i];
-    }
-    const bool ok = ggml_backend_graph_compute(sr.backend, g) == GGML_STATUS_SUCCESS;
-    for (auto it = moved.rbegin(); it != moved.rend(); ++it) {
-        it->t->buffer = it->buffer;
-        it->t->data = it->data;
-    }
-    sr.runs++;
-    if (!ok) err = "the CUDA backend failed it too";
-    return ok;
 }
 
 // SiLU(gate) * up as one GEMM (output mode 2): a SwiGLU whose gate and up are
@@ -1337,7 +1267,6 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
     const std::vector<ggml_tensor *> &nodes = piece.nodes;
     const piece_plan plan = plan_piece(nodes, piece);
     cudaStream_t st = (cudaStream_t) zest_stream(ctx.npu);
-    size_t failed_at = nodes.size();  // the compute node that failed, if one did
     for (size_t k = 0; k < nodes.size(); k++) {
         ggml_tensor *node = nodes[k];
         if (status != GGML_STATUS_SUCCESS) break;
@@ -1367,29 +1296,11 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
         if (!ok) {
             failed(err);
             status = GGML_STATUS_FAILED;
-            failed_at = k;
         }
     }
     if (cudaStreamSynchronize(st) != cudaSuccess && status == GGML_STATUS_SUCCESS) {
         failed(std::string("a kernel failed: ") + cudaGetErrorString(cudaGetLastError()));
         status = GGML_STATUS_FAILED;
-        failed_at = nodes.size() - 1;
-    }
-    if (status != GGML_STATUS_SUCCESS && rerun_on()) {
-        // the failure is sticky (nothing is claimed from now on); this piece
-        // runs again on the CUDA backend when its inputs are intact
-        std::string err;
-        if (!rerun_safe(nodes, failed_at, plan.skip))
-            log_line("", "the failed piece does not run again: a result it wrote lies on one of its inputs");
-        else if (cudaDeviceSynchronize() != cudaSuccess)
-            // a kernel fault leaves the context unusable for the CUDA backend too
-            log_line("", std::string("the failed piece does not run again: the GPU reports ") +
-                             cudaGetErrorString(cudaGetLastError()));
-        else if (sibling_compute(ctx.again, cgraph, err)) {
-            log_line("", std::string("the failed piece ran again on ") + ggml_backend_dev_name(sibling().dev));
-            status = GGML_STATUS_SUCCESS;
-        } else
-            log_line("", "the failed piece could not run again: " + err);
     }
     cudaSetDevice(prev);
     ctx.compute_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -1510,6 +1421,13 @@ ggml_backend_t dev_init_backend(ggml_backend_dev_t dev, const char *) {
         delete ctx;
         return nullptr;
     }
+    // the IQ3_S converter's codebook, as the host ggml dequantises it
+    const std::vector<uint32_t> &grid = iq3s_codebook();
+    if (!grid.empty() && zest_load_iq3s_grid(grid.data())) {
+        log_line("", std::string("cannot load the IQ3_S codebook: ") + zest_last_error());
+        delete ctx;
+        return nullptr;
+    }
     {
         std::lock_guard<std::mutex> lk(g_budget.mu);
         g_budget.contexts++;
@@ -1616,26 +1534,17 @@ int ggml_zest_piece_plan(ggml_cgraph *cgraph, int *counts) {
     return (int) pl.jobs.size();
 }
 
-int ggml_zest_rerun_safe(ggml_cgraph *cgraph, int failed_at) {
-    const piece_nodes piece = collect_piece(cgraph, true);
-    const std::vector<ggml_tensor *> &nodes = piece.nodes;
-    const piece_plan pl = plan_piece(nodes, piece);
-    const size_t at = failed_at < 0 || (size_t) failed_at >= nodes.size() ? nodes.size() - 1 : (size_t) failed_at;
-    return rerun_safe(nodes, at, pl.skip) ? 1 : 0;
+int ggml_zest_iq3s_codebook(uint32_t *out) {
+    const std::vector<uint32_t> &g = iq3s_codebook();
+    if (g.empty()) return 0;
+    if (out) memcpy(out, g.data(), g.size() * sizeof(uint32_t));
+    return 1;
 }
 
 int ggml_zest_model_notes(char *out, int n) {
     const std::string s = model_notes();
     if (out && n > 0) snprintf(out, (size_t) n, "%s", s.c_str());
     return (int) s.size();
-}
-
-int ggml_zest_rerun(ggml_cgraph *cgraph) {
-    sibling_run sr;
-    std::string err;
-    if (sibling_compute(sr, cgraph, err)) return GGML_STATUS_SUCCESS;
-    log_line("", "the piece could not run on the CUDA backend: " + err);
-    return GGML_STATUS_FAILED;
 }
 
 int ggml_zest_piece_fusions(ggml_cgraph *cgraph) {

@@ -232,15 +232,6 @@ ggml_backend_dev_t ggml_backend_dev_get(size_t index);
 const char *ggml_backend_dev_name(ggml_backend_dev_t device);
 enum ggml_backend_dev_type ggml_backend_dev_type(ggml_backend_dev_t device);
 ggml_backend_buffer_type_t ggml_backend_dev_buffer_type(ggml_backend_dev_t device);
-// for running a failed piece again on the CUDA backend
-ggml_backend_t ggml_backend_dev_init(ggml_backend_dev_t device, const char *params);
-void ggml_backend_free(ggml_backend_t backend);
-enum ggml_status ggml_backend_graph_compute(ggml_backend_t backend, struct ggml_cgraph *cgraph);
-ggml_backend_buffer_t ggml_backend_buft_alloc_buffer(ggml_backend_buffer_type_t buft, size_t size);
-size_t ggml_backend_buft_get_alignment(ggml_backend_buffer_type_t buft);
-void *ggml_backend_buffer_get_base(ggml_backend_buffer_t buffer);
-void ggml_backend_buffer_free(ggml_backend_buffer_t buffer);
-void ggml_backend_tensor_set(struct ggml_tensor *tensor, const void *data, size_t offset, size_t size);
 
 #ifdef __cplusplus
 }

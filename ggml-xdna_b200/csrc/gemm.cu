@@ -909,18 +909,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
 }
 
-// Plain CUDA-core GEMM: one thread per output, fp32 accumulation.
-__global__ void gemm_simt_kernel(const uint16_t *a, int64_t lda, const uint16_t *b, int64_t ldb, int64_t M, int64_t N,
-                                 int64_t K, float *c, int64_t ldc) {
-    const int64_t n = blockIdx.x * (int64_t) blockDim.x + threadIdx.x, m = blockIdx.y;
-    if (n >= N || m >= M) return;
-    float acc = 0.0f;
-    for (int64_t k = 0; k < K; k++)
-        acc = fmaf(__uint_as_float((uint32_t) a[m * lda + k] << 16), __uint_as_float((uint32_t) b[n * ldb + k] << 16),
-                   acc);
-    c[m * ldc + n] = acc;
-}
-
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -1018,36 +1006,60 @@ bool plan_stream_k(gemm_plan &gp, int pairs) {
 }
 
 // The stream-K workspace is one per device, so launches that may use it run
-// one at a time: a launch on another stream than the last one waits for it
-// (and inside a stream capture, where it cannot wait on outside work, runs
-// without stream-K).
+// one at a time. A live launch on another stream than the last live one
+// waits for it (an event recorded after each). A launch being captured into
+// a CUDA graph runs nothing now, so it can neither wait for a live launch
+// nor order the ones after it: it leaves the live record alone and takes
+// stream-K only when no live launch on another stream may still hold the
+// workspace and no other stream of the same capture took it (two branches of
+// one graph may run at once). A graph's own stream-K launches are thereby
+// ordered within the graph; replaying it beside live launches on other
+// streams is the caller's to order.
 struct sk_owner {
-    cudaStream_t last = nullptr;
-    cudaEvent_t done = nullptr;
+    cudaStream_t last = nullptr;  // the stream of the last live stream-K launch
+    cudaEvent_t done = nullptr;   // recorded on it after that launch
     bool recorded = false;
+    unsigned long long cap_id = 0;  // the last capture that took stream-K, and its stream
+    cudaStream_t cap_stream = nullptr;
     int epoch = 0;
 };
 std::mutex g_sk_mu;
 sk_owner g_sk_owner[64];
 
+// What a launch on `st` may do with the workspace, given the record `o`:
+// run stream-K (true) and, for a live launch, first wait for `o.done`.
+// Updates the record for a launch that takes it. Host logic only.
+bool sk_decide(sk_owner &o, cudaStream_t st, bool capturing, unsigned long long cap_id, bool *wait) {
+    *wait = false;
+    if (capturing) {
+        if (o.recorded && o.last != st) return false;
+        if (o.cap_id == cap_id && o.cap_stream != st) return false;
+        o.cap_id = cap_id;
+        o.cap_stream = st;
+        return true;
+    }
+    *wait = o.recorded && o.last != st;
+    o.last = st;
+    return true;
+}
+
 bool sk_claim(cudaStream_t st, int *epoch) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return false;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) return false;
+    unsigned long long cap_id = 0;
+    if (cudaStreamGetCaptureInfo(st, &cs, &cap_id) != cudaSuccess) return false;
     const bool capturing = cs != cudaStreamCaptureStatusNone;
     std::lock_guard<std::mutex> lk(g_sk_mu);
     sk_owner &o = g_sk_owner[dev];
     if (!o.done && cudaEventCreateWithFlags(&o.done, cudaEventDisableTiming) != cudaSuccess) return false;
-    if (o.recorded && o.last != st) {
-        if (capturing) {
-            o.last = st;  // later launches in this capture follow this one in stream order
-            o.recorded = false;
-            return false;
-        }
-        if (cudaStreamWaitEvent(st, o.done, 0) != cudaSuccess) return false;
+    sk_owner before = o;
+    bool wait = false;
+    if (!sk_decide(o, st, capturing, cap_id, &wait)) return false;
+    if (wait && cudaStreamWaitEvent(st, o.done, 0) != cudaSuccess) {
+        o = before;
+        return false;
     }
-    o.last = st;
     o.epoch = o.epoch == 0x7fffffff ? 1 : o.epoch + 1;
     *epoch = o.epoch;
     return true;
@@ -1314,14 +1326,6 @@ int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int
     if (M <= 0 || N <= 0) return 0;
     gemm_seg g = { b_bf16, ldb, N, ldc, n_out, mode, c };
     return launch_gemm_group(a_bf16, lda, M, K, 1, &g, err_flag, st);
-}
-
-int launch_gemm_simt(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
-                     int64_t K, float *c, int64_t ldc, cudaStream_t st) {
-    if (M <= 0 || N <= 0) return 0;
-    dim3 grid((unsigned) ((N + 127) / 128), (unsigned) M);
-    gemm_simt_kernel<<<grid, 128, 0, st>>>(a_bf16, lda, b_bf16, ldb, M, N, K, c, ldc);
-    return check_launch("gemm_simt");
 }
 
 }  // namespace zest

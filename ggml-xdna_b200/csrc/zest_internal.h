@@ -81,9 +81,4 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
 int launch_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
                 int64_t K, int mode, float *c, int64_t ldc, int64_t n_out, unsigned *err_flag, cudaStream_t st);
 
-// The plain CUDA-core GEMM used by the start-up self-test as a second
-// opinion on the tensor-core kernel.
-int launch_gemm_simt(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64_t ldb, int64_t M, int64_t N,
-                     int64_t K, float *c, int64_t ldc, cudaStream_t st);
-
 }  // namespace zest

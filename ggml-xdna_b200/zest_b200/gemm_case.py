@@ -1,21 +1,15 @@
 """K3 launches of the benchmark configs' shapes, for profiling and tuning.
 
     python -m zest_b200.gemm_case C1                 # six launches (for an ncu capture of the 6th)
-    python -m zest_b200.gemm_case --time             # device time per launch of every shape
-    ZEST_GEMM_SK=0 python -m zest_b200.gemm_case --time C1 "C3 o"
     python -m zest_b200.gemm_case --plan             # the launch plans, on the host (no GPU)
 
 Operands are bf16 on the device (A ~ N(0, 0.25), B ~ N(0, 0.0004), seeded); the
-output is f32 holding bf16-rounded values, as the plugin's default. `--time`
-queues 50 launches behind a GPU sleep, so the CUDA events around them measure
-device time only, and prints microseconds per launch, TFLOP/s, and the host
-time per launch (which must stay below the device time for the figure to hold).
+output is f32 holding bf16-rounded values, as the plugin's default.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import time
 
 # (M, the N of each weight sharing A, K): one grouped launch of each config's layer
 SHAPES = {
@@ -53,36 +47,9 @@ def run(name: str, launches: int = 6) -> None:
         raise RuntimeError(f"{name}: device error bits {int(err.item()):#x}")
 
 
-def timed(name: str, n: int = 50) -> tuple[float, float, float]:
-    """(device us per launch, TFLOP/s, host us per launch)."""
-    import torch
-    from . import MODE_BF16, gemm_group
-    M, Ns, K = SHAPES[name]
-    a, bs, outs = operands(M, Ns, K)
-    modes = [MODE_BF16] * len(Ns)
-    err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    for _ in range(10):
-        gemm_group(a, bs, M, Ns, modes, outs, err=err)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    torch.cuda._sleep(40_000_000)  # the host queues every launch while the GPU sleeps
-    e0.record()
-    h0 = time.perf_counter()
-    for _ in range(n):
-        gemm_group(a, bs, M, Ns, modes, outs, err=err)
-    host_us = (time.perf_counter() - h0) * 1e6 / n
-    e1.record()
-    torch.cuda.synchronize()
-    if int(err.item()):
-        raise RuntimeError(f"{name}: device error bits {int(err.item()):#x}")
-    us = e0.elapsed_time(e1) * 1e3 / n
-    return us, 2.0 * M * sum(Ns) * K / (us * 1e6), host_us
-
-
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("shapes", nargs="*", help=f"shape names (default: all): {', '.join(SHAPES)}")
-    ap.add_argument("--time", action="store_true", help="print device time per launch instead of just running")
     ap.add_argument("--plan", action="store_true", help="print each shape's launch plan (no GPU needed)")
     ap.add_argument("--sms", type=int, default=148, help="--plan: the SMs to plan for")
     ap.add_argument("--launches", type=int, default=6)
@@ -97,12 +64,9 @@ def main(argv=None) -> None:
             M, Ns, K = SHAPES[s]
             print(json.dumps({"shape": s, **plan_gemm(M, K, Ns, args.sms)}))
         return
-    if args.time:
-        print(json.dumps({s: [round(v, 1) for v in timed(s)] for s in names}))
-    else:
-        for s in names:
-            run(s, args.launches)
-        print("ok")
+    for s in names:
+        run(s, args.launches)
+    print("ok")
 
 
 if __name__ == "__main__":

@@ -21,6 +21,8 @@ extern "C" {
 #define GGML_XDNA_NAME "XDNA"         /* the backend (registry) name */
 #define GGML_XDNA_DEVICE_NAME "XDNA0" /* the device, as -dev names it */
 
+#include <stdint.h>
+
 typedef struct ggml_backend_reg *ggml_backend_reg_t;
 struct ggml_tensor;
 
@@ -65,22 +67,20 @@ __attribute__((visibility("default"))) int ggml_zest_budget_plan(double limit_gb
  * src/xdna-exec.cpp:368-388,392-431). Host logic only; for tests. */
 __attribute__((visibility("default"))) int ggml_zest_piece_plan(struct ggml_cgraph *cgraph, int *counts);
 
-/* The failure path's host side (src/ggml-zest.cpp:709-755,887-891). After a
- * failed piece, graph_compute runs it again on the CUDA backend and returns
- * its status, unless GGML_ZEST_RERUN=0 or a result the first run may have
- * written (the compute nodes up to the failing one, failed_at; -1 for all,
- * and every result folded into an earlier node's job) overlaps one of the
- * piece's inputs. ggml_zest_rerun_safe answers that check (1: safe to run
- * again); ggml_zest_rerun runs the piece on the CUDA backend as graph_compute
- * does, moving host-memory inputs into CUDA memory for the call. Host logic
- * only; for tests. */
-__attribute__((visibility("default"))) int ggml_zest_rerun_safe(struct ggml_cgraph *cgraph, int failed_at);
 /* The notes about the model that graph_compute says once as the first prompt
  * runs (src/ggml-zest.cpp:566-655), gathered while supports_op was asked:
  * writes them to out (at most n bytes) and returns their length, 0 for none.
  * Host logic only; for tests. */
 __attribute__((visibility("default"))) int ggml_zest_model_notes(char *out, int n);
-__attribute__((visibility("default"))) int ggml_zest_rerun(struct ggml_cgraph *cgraph);
+
+/* The IQ3_S codebook the plugin converts IQ3_S weights with: ggml's own,
+ * read back through the host ggml's to_float when the library loads (the
+ * reference dequantises every weight type with that to_float,
+ * src/xdna-npu.cpp:339-348). Writes the 512 entries (four magnitude bytes
+ * each, the first in the low byte) to out and returns 1; returns 0 when
+ * ggml offers no IQ3_S dequantiser, and IQ3_S weights are then not
+ * claimed. Host logic only; for tests. */
+__attribute__((visibility("default"))) int ggml_zest_iq3s_codebook(uint32_t *out);
 
 #ifdef __cplusplus
 }

@@ -96,9 +96,12 @@ int zest_convert_gate_up(int type, const void *gate, const void *up, int64_t row
 /* Launches of K3 (zest_gemm, zest_gemm_group, zest_gemm_segs) whose last
  * waves are cut into stream-K runs (zest_plan_gemm reports which) share one
  * partial-sum workspace per device. The library orders such launches across
- * streams. Inside a stream capture it orders them within the capture only,
- * so a CUDA graph holding them must not replay while another stream runs one
- * (ZEST_GEMM_SK=0 takes stream-K out). */
+ * streams: a launch on another stream than the last one waits for it. A
+ * launch being captured into a CUDA graph runs whole tiles when a live
+ * launch on another stream may still hold the workspace, or when another
+ * stream of the same capture took it; so a graph's own stream-K launches are
+ * ordered within the graph, and a graph holding them must not replay while
+ * another stream runs one (ZEST_GEMM_SK=0 takes stream-K out). */
 
 /* K3, the GEMM: c[M][ldc] = A[M][K] * B[N][K]^T in fp32 on the tensor cores,
  * then `mode`. In ZEST_MODE_SWIGLU, B comes from zest_convert_gate_up and c
@@ -188,7 +191,10 @@ int zest_plan_gemm(int64_t M, int64_t K, int n, const int64_t *N, int sms, zest_
  * stream capture. Every call shares the one array, so calls that overlap on
  * the GPU (other streams, other threads) race: serialise them. Nothing in
  * the array needs clearing between calls: each call writes every row it
- * reads. */
+ * reads. A launch that takes the stream-K route (zest_plan_gemm) keeps its
+ * partial sums in K3's own fixed workspace, another device array, ordered
+ * across streams as below; the first such launch on a device creates the
+ * one CUDA event that orders them. */
 #define ZEST_NOALLOC_MAX_VALUES (16 * 1024 * 1024)
 int zest_mul_mat_noalloc(const float *x, int64_t T, int64_t K, int64_t ldx, const uint16_t *w_bf16, int64_t ldw,
                          int64_t N, int mode, float *y, int64_t ldy, unsigned *err, void *stream);

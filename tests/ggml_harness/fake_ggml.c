@@ -84,11 +84,47 @@ static void q4_0_to_float(const void *x, float *y, int64_t k) {
     }
 }
 
+/* IQ3_S as ggml stores it, 110 bytes per 256 values: {fp16 d; u8 qs[64];
+ * u8 qh[8]; u8 signs[32]; u8 scales[4]}. Value e of 32-value group g:
+ * magnitude byte e%4 of codebook entry qs[8g + e/4] | (bit e/4 of qh[g]) << 8,
+ * times d * (1 + 2 * (nibble g%2 of scales[g/2])), negated when bit e%8 of
+ * signs[4g + e/8] is set. The codebook is the one the tests load from the
+ * installed gguf package (fake_ggml_set_iq3s_grid); without it ggml reports
+ * no IQ3_S dequantiser. */
+static uint32_t IQ3S_GRID[512];
+static int IQ3S_READY;
+
+void fake_ggml_set_iq3s_grid(const uint32_t *grid) {
+    memcpy(IQ3S_GRID, grid, sizeof IQ3S_GRID);
+    IQ3S_READY = 1;
+}
+
+static void iq3_s_to_float(const void *x, float *y, int64_t k) {
+    const uint8_t *b = (const uint8_t *) x;
+    for (int64_t blk = 0; blk < k / 256; blk++, b += 110) {
+        const float d = half_to_float((uint16_t) (b[0] | (b[1] << 8)));
+        const uint8_t *qs = b + 2, *qh = b + 66, *signs = b + 74, *scales = b + 106;
+        for (int g = 0; g < 8; g++) {
+            const float db = d * (float) (1 + 2 * ((scales[g / 2] >> (4 * (g % 2))) & 0xf));
+            for (int e = 0; e < 32; e++) {
+                const int slot = e / 4;
+                const uint32_t idx = qs[8 * g + slot] | (((qh[g] >> slot) & 1u) << 8);
+                const float mag = (float) ((IQ3S_GRID[idx] >> (8 * (e % 4))) & 0xffu);
+                const int neg = (signs[4 * g + e / 8] >> (e % 8)) & 1;
+                y[blk * 256 + 32 * g + e] = db * mag * (neg ? -1.0f : 1.0f);
+            }
+        }
+    }
+}
+
 static const struct ggml_type_traits Q4_0_TRAITS = { "q4_0", 32, 0, 18, true, q4_0_to_float, NULL };
+static const struct ggml_type_traits IQ3_S_TRAITS = { "iq3_s", 256, 0, 110, true, iq3_s_to_float, NULL };
 static const struct ggml_type_traits NO_TRAITS = { "other", 1, 0, 4, false, NULL, NULL };
 
 const struct ggml_type_traits *ggml_get_type_traits(enum ggml_type type) {
-    return type == GGML_TYPE_Q4_0 ? &Q4_0_TRAITS : &NO_TRAITS;
+    if (type == GGML_TYPE_Q4_0) return &Q4_0_TRAITS;
+    if (type == GGML_TYPE_IQ3_S && IQ3S_READY) return &IQ3_S_TRAITS;
+    return &NO_TRAITS;
 }
 
 /* graphs: {int n; ggml_tensor **nodes} */
@@ -107,8 +143,6 @@ struct ggml_backend_buffer_type {
 struct ggml_backend_buffer {
     int usage;
     int is_host;
-    char *base; /* set for buffers the fake CUDA backend allocates (host memory standing in) */
-    size_t size;
 };
 
 static struct ggml_backend_buffer_type CUDA_BUFT = { 0 }, CPU_BUFT = { 1 };
@@ -142,87 +176,7 @@ const char *ggml_backend_dev_name(ggml_backend_dev_t d) { return ((struct fake_d
 enum ggml_backend_dev_type ggml_backend_dev_type(ggml_backend_dev_t d) { return ((struct fake_dev *) d)->type; }
 ggml_backend_buffer_type_t ggml_backend_dev_buffer_type(ggml_backend_dev_t d) { return ((struct fake_dev *) d)->buft; }
 
-/* The CUDA backend, as far as running a failed piece again needs it: its
- * instances record each graph they are given (how many nodes, how many of
- * their sources lie in a buffer it allocated, and a checksum of those
- * bytes) and answer with a status the test sets. It computes nothing. */
-static struct {
-    int status, init_fails;
-    long runs, last_nodes, moved_srcs, started, stopped, buffers, buffers_freed, sets;
-    unsigned long long moved_sum;
-} SIB;
-
-static int in_fake_buffer(const struct ggml_tensor *t) {
-    return t->buffer && t->buffer->base && (const char *) t->data >= t->buffer->base &&
-           (const char *) t->data < t->buffer->base + t->buffer->size;
-}
-
-ggml_backend_t ggml_backend_dev_init(ggml_backend_dev_t device, const char *params) {
-    (void) params;
-    if (SIB.init_fails || ((struct fake_dev *) device)->type != GGML_BACKEND_DEVICE_TYPE_GPU) return NULL;
-    ggml_backend_t b = (ggml_backend_t) calloc(1, sizeof *b);
-    b->device = device;
-    SIB.started++;
-    return b;
-}
-void ggml_backend_free(ggml_backend_t backend) {
-    if (!backend) return;
-    free(backend);
-    SIB.stopped++;
-}
-enum ggml_status ggml_backend_graph_compute(ggml_backend_t backend, struct ggml_cgraph *g) {
-    (void) backend;
-    SIB.runs++;
-    SIB.last_nodes = g->n_nodes;
-    for (int i = 0; i < g->n_nodes; i++)
-        for (int j = 0; j < GGML_MAX_SRC; j++) {
-            const struct ggml_tensor *s = g->nodes[i]->src[j];
-            if (!s || !in_fake_buffer(s)) continue;
-            SIB.moved_srcs++;
-            const unsigned char *p = (const unsigned char *) s->data;
-            for (size_t k = 0; k < ggml_nbytes(s); k++) SIB.moved_sum += p[k];
-        }
-    return (enum ggml_status) SIB.status;
-}
-ggml_backend_buffer_t ggml_backend_buft_alloc_buffer(ggml_backend_buffer_type_t buft, size_t size) {
-    ggml_backend_buffer_t b = (ggml_backend_buffer_t) calloc(1, sizeof *b);
-    b->is_host = buft->is_host;
-    b->base = (char *) calloc(1, size ? size : 1);
-    b->size = size;
-    SIB.buffers++;
-    return b;
-}
-size_t ggml_backend_buft_get_alignment(ggml_backend_buffer_type_t buft) {
-    (void) buft;
-    return 128;
-}
-void *ggml_backend_buffer_get_base(ggml_backend_buffer_t b) { return b->base; }
-void ggml_backend_buffer_free(ggml_backend_buffer_t b) {
-    if (!b) return;
-    free(b->base);
-    free(b);
-    SIB.buffers_freed++;
-}
-void ggml_backend_tensor_set(struct ggml_tensor *t, const void *data, size_t offset, size_t size) {
-    memcpy((char *) t->data + offset, data, size);
-    SIB.sets++;
-}
-
 /* harness helpers the tests call through ctypes */
-void fake_sibling_set(int status, int init_fails) {
-    SIB.status = status;
-    SIB.init_fails = init_fails;
-}
-/* out[0..8]: runs, nodes of the last graph, moved sources seen, backends
- * started, backends freed, buffers allocated, buffers freed, tensor_set
- * calls; returns the checksum of the moved sources' bytes */
-unsigned long long fake_sibling_stats(long *out) {
-    const long v[8] = { SIB.runs, SIB.last_nodes, SIB.moved_srcs, SIB.started, SIB.stopped, SIB.buffers,
-                        SIB.buffers_freed, SIB.sets };
-    memcpy(out, v, sizeof v);
-    return SIB.moved_sum;
-}
-void fake_sibling_reset(void) { memset(&SIB, 0, sizeof SIB); }
 ggml_backend_buffer_t fake_buffer_new(int usage, int is_host) {
     ggml_backend_buffer_t b = (ggml_backend_buffer_t) calloc(1, sizeof *b);
     b->usage = usage;

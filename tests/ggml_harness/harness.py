@@ -92,6 +92,19 @@ class Harness:
         self.fake.fake_cuda_buft.restype = _vp
         self.fake.fake_cpu_buft.restype = _vp
         self.fake.fake_op_id.argtypes = [ctypes.c_char_p]
+        # ggml's IQ3_S dequantiser needs its codebook, here the installed
+        # gguf package's (the plugin reads it back through to_float)
+        self.fake.fake_ggml_set_iq3s_grid.argtypes = [_vp]
+        try:
+            import numpy as np
+            from gguf.quants import IQ3_S as _IQ3S
+            _IQ3S.init_grid()
+            g = np.asarray(_IQ3S.grid, dtype=np.float32).reshape(512, 4).astype(np.uint32)
+            self.iq3s_grid = np.ascontiguousarray(g[:, 0] | (g[:, 1] << 8) | (g[:, 2] << 16) | (g[:, 3] << 24),
+                                                  dtype=np.uint32)
+            self.fake.fake_ggml_set_iq3s_grid(self.iq3s_grid.ctypes.data)
+        except ImportError:
+            self.iq3s_grid = None
         self.plugin = ctypes.CDLL(str(PLUGIN))
         self.plugin.ggml_backend_xdna_reg.restype = ctypes.POINTER(Reg)
         self.plugin.ggml_backend_init.restype = ctypes.POINTER(Reg)
@@ -101,12 +114,8 @@ class Harness:
         self.plugin.ggml_zest_piece_plan.argtypes = [_vp, ctypes.POINTER(ctypes.c_int)]
         self.plugin.ggml_zest_budget_plan.argtypes = [ctypes.c_double, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         self.plugin.ggml_zest_piece_groups.argtypes = [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
-        self.plugin.ggml_zest_rerun_safe.argtypes = [_vp, ctypes.c_int]
-        self.plugin.ggml_zest_rerun.argtypes = [_vp]
         self.plugin.ggml_zest_model_notes.argtypes = [ctypes.c_char_p, ctypes.c_int]
-        self.fake.fake_sibling_set.argtypes = [_int, _int]
-        self.fake.fake_sibling_stats.argtypes = [ctypes.POINTER(ctypes.c_long)]
-        self.fake.fake_sibling_stats.restype = ctypes.c_ulonglong
+        self.plugin.ggml_zest_iq3s_codebook.argtypes = [_vp]
         # ctypes objects the C side points at, kept for the whole process: the
         # plugin remembers who read each tensor by address (as the reference
         # does), and a freed tensor's address reused by a later test's tensor
@@ -146,31 +155,18 @@ class Harness:
         self.keep.append(arr)
         return self.fake.fake_graph_new(len(nodes), ctypes.cast(arr, _vp))
 
-    def rerun_safe(self, nodes: list[Tensor], failed_at: int = -1) -> bool:
-        """Whether a piece that failed at compute node failed_at (-1: at the
-        end) may run again on the CUDA backend."""
-        return bool(self.plugin.ggml_zest_rerun_safe(self.graph(nodes), failed_at))
-
-    def rerun(self, nodes: list[Tensor]) -> int:
-        """The piece run on the CUDA backend as after a failure: its status."""
-        return self.plugin.ggml_zest_rerun(self.graph(nodes))
+    def iq3s_codebook(self):
+        """The IQ3_S codebook the plugin read back through ggml's to_float
+        (uint32 x 512), or None when it has none."""
+        import numpy as np
+        out = np.zeros(512, dtype=np.uint32)
+        return out if self.plugin.ggml_zest_iq3s_codebook(out.ctypes.data) else None
 
     def model_notes(self) -> str:
         """What graph_compute would say about the model as the first prompt runs."""
         buf = ctypes.create_string_buffer(2048)
         self.plugin.ggml_zest_model_notes(buf, len(buf))
         return buf.value.decode()
-
-    def sibling(self, status: int = 0, init_fails: bool = False) -> None:
-        """What the fake CUDA backend answers from now on; its records reset."""
-        self.fake.fake_sibling_reset()
-        self.fake.fake_sibling_set(status, int(init_fails))
-
-    def sibling_stats(self) -> dict:
-        v = (ctypes.c_long * 8)()
-        total = self.fake.fake_sibling_stats(v)
-        keys = ("runs", "nodes", "moved", "started", "stopped", "buffers", "buffers_freed", "sets")
-        return dict(zip(keys, list(v)), moved_sum=int(total))
 
     # --- registry / device / backend ------------------------------------------
     def reg(self):

@@ -11,7 +11,7 @@ import sys
 import pytest
 
 sys.path.insert(0, os.path.join(os.path.dirname(__file__), "ggml_harness"))
-from harness import (DEV_IGPU, F16, F32, FLAG_INPUT, Harness, Props, Q4_0, Q4_K, Q8_0, Tensor,  # noqa: E402
+from harness import (DEV_IGPU, F16, F32, FLAG_INPUT, IQ3_S, Harness, Props, Q4_0, Q4_K, Q8_0, Tensor,  # noqa: E402
                      USAGE_COMPUTE, USAGE_WEIGHTS, fn)
 
 
@@ -200,9 +200,37 @@ def test_block_ops_env():
     env = dict(os.environ, GGML_XDNA_BLOCK_OPS="ADD")
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
     assert "ADD True SCALE False" in out.stdout, out.stdout + out.stderr
+    env = dict(os.environ, GGML_XDNA_BLOCK_OPS="SCALE,ADD")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
+    assert "ADD True SCALE True" in out.stdout, out.stdout + out.stderr
+    env = dict(os.environ, GGML_XDNA_BLOCK_OPS=",")  # given, but naming no op: none taken
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
+    assert "ADD False SCALE False" in out.stdout, out.stdout + out.stderr
     env = dict(os.environ, GGML_XDNA_BLOCKS="0")
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
     assert "ADD False SCALE False" in out.stdout, out.stdout + out.stderr
+
+
+def test_iq3s_codebook_read_back_through_to_float(h):
+    # the plugin builds in no IQ3_S table: it reads ggml's back through the
+    # host ggml's to_float (the stand-in's holds the gguf package's codebook)
+    got = h.iq3s_codebook()
+    assert h.iq3s_grid is not None and got is not None
+    assert (got == h.iq3s_grid).all()
+    w = h.tensor(IQ3_S, [5120, 17408], buffer=h.buffer(USAGE_WEIGHTS))
+    assert h.policy(h.mul_mat(w, h.tensor(F32, [5120, 2048]))), "IQ3_S weights are claimed"
+
+
+def test_iq3s_not_claimed_without_a_dequantiser():
+    # a ggml with no IQ3_S to_float: no codebook, and IQ3_S is not claimed
+    code = ("import sys; sys.path.insert(0, %r); "
+            "from harness import *; import ctypes; "
+            "fake = ctypes.CDLL(str(FAKE), mode=ctypes.RTLD_GLOBAL); "
+            "plugin = ctypes.CDLL(str(PLUGIN)); plugin.ggml_zest_iq3s_codebook.argtypes = [ctypes.c_void_p]; "
+            "print('CODEBOOK', plugin.ggml_zest_iq3s_codebook(None))"
+            % os.path.join(os.path.dirname(__file__), "ggml_harness"))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert "CODEBOOK 0" in out.stdout, out.stdout + out.stderr
 
 
 def test_min_batch_env():

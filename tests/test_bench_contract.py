@@ -22,7 +22,8 @@ def lines(stdout: str) -> list[dict]:
 
 def test_reference_arm_line():
     r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "0"],
-                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+                       capture_output=True, text=True, timeout=600, cwd=ROOT,
+                       env=dict(os.environ, ZEST_REF_SECONDS="4"))
     assert r.returncode == 0, r.stderr[-2000:]
     (d,) = lines(r.stdout)
     baseline = json.loads((ROOT / "BASELINE.json").read_text())
@@ -32,6 +33,12 @@ def test_reference_arm_line():
     for key in ("unit", "ms_per_step", "scaling", "vs_baseline", "dtype", "data"):
         assert key in d, key
     assert d["config"]["workload"] == "qwen3-4b-layer"
+    sys.path[:0] = [str(ROOT), str(ROOT / "ggml-xdna_b200")]
+    import bench
+    # the same config as our arm's line, so the two arms compare like with like
+    assert d["config"] == bench.layer_config(bench.WORKLOADS["qwen3-4b-layer"], "qwen3-4b-layer", 1, None)
+    assert d["scaling"] == "none"
+    assert "all 8192 token rows" in d["cpu_baseline"]["sample"]
     cb = d["cpu_baseline"]
     assert cb["kind"] == "reference" and cb["cores"] >= 1 and cb["sample"] and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
@@ -42,7 +49,8 @@ def test_reference_arm_under_torchrun_prints_once():
            "127.0.0.1", "--master-port", "29541", str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "2",
            "--steps", "1", "--warmup", "3"]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, cwd=ROOT,
-                       env=dict(os.environ, OMP_NUM_THREADS="1"))
+                       env=dict(os.environ, OMP_NUM_THREADS="1", ZEST_REF_SECONDS="4"))
     assert r.returncode == 0, r.stderr[-2000:]
     (d,) = lines(r.stdout)
     assert d["impl"] == "reference" and d["n_gpus"] == 2
+    assert d["scaling"] == "strong" and d["config"]["parallelism"].startswith("n-shard2")

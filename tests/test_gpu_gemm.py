@@ -264,3 +264,41 @@ def test_stream_k_matches_whole_tiles():
     env = dict(os.environ, ZEST_GEMM_SK="1")
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=600)
     assert "STREAMK OK" in r.stdout, r.stdout + r.stderr
+
+
+def test_stream_k_order_survives_a_capture():
+    # Stream-K launches share one workspace per device. A live launch on
+    # stream A (held back behind a GPU sleep), then one captured into a CUDA
+    # graph on stream B, then a live one on stream C: C must still wait for
+    # A, whatever the capture did in between.
+    import time
+    M, N, K = 2048, 2560, 9728
+    assert Z.plan_gemm(M, K, [N])["stream_k"] == 1
+    _, bh = Z.convert_weight(O.Q8_0, dev(O.quantize(O.Q8_0, O.weights_f32(N, K, 61))), N, K)
+    _, ah = Z.pack_activations(dev(O.activations(M, K, 62)))
+    torch.cuda.synchronize()
+    outs = [torch.zeros((M, N), dtype=torch.float32, device="cuda") for _ in range(3)]
+    errs = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(3)]
+    sa, sb, sc = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    with torch.cuda.stream(sa):
+        torch.cuda._sleep(1_000_000_000)  # about half a second or more
+        Z.gemm(ah, bh, M, N, out=outs[0], err=errs[0])
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(sb):  # capture_begin, unlike torch.cuda.graph, does not synchronize first
+        g.capture_begin(capture_error_mode="relaxed")
+        Z.gemm(ah, bh, M, N, out=outs[1], err=errs[1])
+        g.capture_end()
+    with torch.cuda.stream(sc):
+        Z.gemm(ah, bh, M, N, out=outs[2], err=errs[2])
+        done_c = torch.cuda.Event()
+        done_c.record(sc)
+    time.sleep(0.1)
+    waited = not done_c.query()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    assert waited, "the launch on C ran while the one on A was still held back"
+    assert all(int(e.item()) == 0 for e in errs)
+    want = host(outs[0])
+    assert np.array_equal(host(outs[2]), want)
+    assert same_up_to_sum_order(host(outs[1]), want, rounded=False)
