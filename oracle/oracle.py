@@ -97,6 +97,18 @@ def ref() -> ctypes.CDLL:
         L.zr_unpack_b.argtypes = [_vp, _i64, _i64, _int, _int, _int, _vp]
         L.zr_interleave_gate_up.argtypes = [_vp, _vp, _i64, _i64, _vp]
         L.zr_mul_mat.argtypes = [_int, _vp, _i64, _i64, _vp, _i64, _vp, _int]
+        _f = ctypes.c_float
+        L.zr_rms_norm.argtypes = [_vp, _i64, _i64, _f, _vp, _int]
+        L.zr_mul_row.argtypes = [_vp, _vp, _i64, _i64, _vp, _int]
+        L.zr_add.argtypes = [_vp, _vp, _int, _i64, _i64, _vp, _int]
+        L.zr_scale.argtypes = [_vp, _i64, _i64, _f, _f, _vp, _int]
+        L.zr_glu.argtypes = [_int, _int, _vp, _vp, _i64, _i64, _vp, _int]
+        L.zr_rope.argtypes = [_vp, _i64, _i64, _i64, _vp, _int, _int, _int, _vp, _vp, _vp, _int]
+        L.zr_norm_mul.argtypes = [_vp, _i64, _i64, _f, _vp, _vp, _int]
+        L.zr_norm_mul_rope.argtypes = [_vp, _i64, _i64, _i64, _f, _vp, _vp, _int, _int, _int, _vp, _vp, _vp, _int]
+        for n in ("zr_rms_norm", "zr_mul_row", "zr_add", "zr_scale", "zr_glu", "zr_rope", "zr_norm_mul",
+                  "zr_norm_mul_rope"):
+            getattr(L, n).restype = _int
         # the reference build links its own copy of the oracle's dequantisers
         L.zo_set_iq3s_grid.argtypes = [_vp]
         try:
@@ -278,6 +290,89 @@ def ref_mul_mat(qtype: int, raw_w: np.ndarray, N: int, K: int, X: np.ndarray, n_
     Y = np.empty((M, N), dtype=np.float32)
     ref().zr_mul_mat(qtype, _p(np.ascontiguousarray(raw_w)), N, K, _p(X), M, _p(Y), n_threads)
     return Y
+
+
+# --- the reference's block executor (src/xdna-exec.cpp, xdna_exec_piece with no
+# NPU: its host path, so run_rows and the rope table are the reference's own) -------
+
+def _ref_ok(rc: int, what: str) -> None:
+    if rc:
+        raise RuntimeError(f"the reference's executor failed the {what} piece")
+
+
+def ref_rms_norm(x: np.ndarray, d: int, eps: float, n_threads: int = 4) -> np.ndarray:
+    x = _f32(x)
+    y = np.empty_like(x)
+    _ref_ok(ref().zr_rms_norm(_p(x), x.size // d, d, eps, _p(y), n_threads), "RMS_NORM")
+    return y
+
+
+def ref_mul_row(x: np.ndarray, w: np.ndarray, n_threads: int = 4) -> np.ndarray:
+    x, w = _f32(x), _f32(w)
+    y = np.empty_like(x)
+    _ref_ok(ref().zr_mul_row(_p(x), _p(w), x.size // w.size, w.size, _p(y), n_threads), "MUL")
+    return y
+
+
+def ref_add(x: np.ndarray, b: np.ndarray, n_threads: int = 4) -> np.ndarray:
+    x, b = _f32(x), _f32(b)
+    y = np.empty_like(x)
+    bias = int(b.size != x.size)
+    d = b.size if bias else x.shape[-1]
+    _ref_ok(ref().zr_add(_p(x), _p(b), bias, x.size // d, d, _p(y), n_threads), "ADD")
+    return y
+
+
+def ref_scale(x: np.ndarray, s: float, bias: float, n_threads: int = 4) -> np.ndarray:
+    x = _f32(x)
+    y = np.empty_like(x)
+    _ref_ok(ref().zr_scale(_p(x), x.shape[0], x.size // x.shape[0], s, bias, _p(y), n_threads), "SCALE")
+    return y
+
+
+def ref_glu(kind: int, g: np.ndarray, u: np.ndarray | None = None, swapped: bool = False,
+            n_threads: int = 4) -> np.ndarray:
+    g = _f32(g)
+    rows = g.shape[0]
+    f = g.shape[1] if u is not None else g.shape[1] // 2
+    y = np.empty((rows, f), np.float32)
+    up = _p(_f32(u)) if u is not None else None
+    _ref_ok(ref().zr_glu(kind, int(swapped), _p(g), up, rows, f, _p(y), n_threads), "GLU")
+    return y
+
+
+def ref_rope(x: np.ndarray, pos: np.ndarray, n_dims: int, mode: int, n_ctx_orig: int, par,
+             ff: np.ndarray | None = None, n_threads: int = 4) -> np.ndarray:
+    """x [T][heads][d]; par: freq_base, freq_scale, ext_factor, attn_factor, beta_fast, beta_slow."""
+    x = _f32(x)
+    T, H, d = x.shape
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    par = _f32(par)
+    y = np.empty_like(x)
+    ffp = _p(_f32(ff)) if ff is not None else None
+    _ref_ok(ref().zr_rope(_p(x), T, H, d, _p(pos), n_dims, mode, n_ctx_orig, _p(par), ffp, _p(y), n_threads),
+            "ROPE")
+    return y
+
+
+def ref_norm_mul(x: np.ndarray, eps: float, w: np.ndarray, n_threads: int = 4) -> np.ndarray:
+    x, w = _f32(x), _f32(w)
+    y = np.empty_like(x)
+    _ref_ok(ref().zr_norm_mul(_p(x), x.size // w.size, w.size, eps, _p(w), _p(y), n_threads), "RMS_NORM + MUL")
+    return y
+
+
+def ref_norm_mul_rope(x: np.ndarray, eps: float, w: np.ndarray, pos: np.ndarray, n_dims: int, mode: int,
+                      n_ctx_orig: int, par, ff: np.ndarray | None = None, n_threads: int = 4) -> np.ndarray:
+    x, w = _f32(x), _f32(w)
+    T, H, d = x.shape
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    par = _f32(par)
+    y = np.empty_like(x)
+    ffp = _p(_f32(ff)) if ff is not None else None
+    _ref_ok(ref().zr_norm_mul_rope(_p(x), T, H, d, eps, _p(w), _p(pos), n_dims, mode, n_ctx_orig, _p(par), ffp,
+                                   _p(y), n_threads), "RMS_NORM + MUL + ROPE")
+    return y
 
 
 # --- seeded synthetic inputs (the shapes and distributions of the configs) ---------

@@ -4,10 +4,13 @@ Run in a container that has the reference sources, after `make -C oracle ref`:
 
     python tests/golden/make_golden.py
 
+    python tests/golden/make_golden.py host_ops    # only the small-op fixture
+
 Every output byte / value here comes from oracle/_ref/libzest_ref.so, i.e.
-the reference's src/npu/bfp16_pack.cpp and src/xdna-ref.cpp compiled
-unmodified, except the dequantised weights, which come from gguf-py's numpy
-dequantisers (the independent cross-check of the restated ggml to_float).
+the reference's src/npu/bfp16_pack.cpp, src/xdna-ref.cpp and
+src/xdna-exec.cpp compiled unmodified, except the dequantised weights, which
+come from gguf-py's numpy dequantisers (the independent cross-check of the
+restated ggml to_float).
 Inputs are seeded (numpy PCG64) and stored alongside, so the fixtures stand
 on their own where neither the reference nor gguf is present.
 """
@@ -26,12 +29,35 @@ from oracle import oracle as O  # noqa: E402
 OUT = Path(__file__).resolve().parent
 
 
+def host_ops() -> None:
+    """5. the block executor's small ops (run_rows, src/xdna-exec.cpp:253-346,
+    and its rope table, :199-239), run by the reference's own executor with
+    no NPU: the cases of tests/golden/host_ops.py, inputs stored beside."""
+    import json
+
+    sys.path.insert(0, str(OUT))
+    import host_ops as HO
+
+    arrays = {"cases": np.array(json.dumps(HO.CASES))}
+    ops = HO.reference_ops(O)
+    for i, (name, spec) in enumerate(HO.CASES):
+        inp = HO.inputs(i, spec)
+        for k, v in inp.items():
+            arrays[f"{i}/{k}"] = v
+        arrays[f"{i}/y"] = HO.run(i, spec, ops, inp)
+    np.savez_compressed(OUT / "host_ops.npz", **arrays)
+
+
 def main() -> None:
     import gguf
     from gguf import GGMLQuantizationType as GT
 
     if not O.has_ref():
         raise SystemExit("oracle/_ref/libzest_ref.so is missing: make -C oracle ref")
+    if sys.argv[1:] == ["host_ops"]:
+        host_ops()
+        print("wrote host_ops.npz")
+        return
 
     # 1. the codec: adversarial blocks and special values (bfp16_pack.cpp:85-144)
     x = O.make_data(8 * 4096, 20261201)
@@ -79,6 +105,7 @@ def main() -> None:
     Wd = O.decode_blocks(O.ref_encode_blocks(O.dequant(O.Q8_0, raw, N, K))).reshape(N, K)
     Yd = O.ref_mul_mat(O.F32, Wd, N, K, Xd, n_threads=4)
     np.savez_compressed(OUT / "mul_mat_q8_0.npz", raw=raw, x=X, y=Y, y_decoded=Yd, N=N, K=K, M=M)
+    host_ops()
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 

@@ -150,3 +150,36 @@ def test_selftest_operands():
     a, w = O.selftest_operands()
     assert a.min() >= -2 and a.max() <= 2 and w.min() >= -3 and w.max() <= 3
     assert a.shape == (512, 128) and w.shape == (512, 128)
+
+
+def _host_ops():
+    import json
+    import sys
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    import host_ops as HO
+    g = np.load(Path(__file__).resolve().parent / "golden" / "host_ops.npz")
+    cases = json.loads(str(g["cases"]))
+    for i, (name, spec) in enumerate(cases):
+        inp = {k.split("/", 1)[1]: g[k] for k in g.files if k.startswith(f"{i}/") and not k.endswith("/y")}
+        yield HO, i, name, spec, inp, g[f"{i}/y"]
+
+
+def test_small_ops_match_the_reference_executor_fixtures():
+    # the oracle's restatement of run_rows (and its rope table) against the
+    # outputs of the reference's own executor (tests/golden/host_ops.npz), the
+    # 21 cases of tests/test-host-ops.cpp plus the two fused forms, at the
+    # reference's own bar (nrmse <= 1e-5)
+    n = 0
+    for HO, i, name, spec, inp, want in _host_ops():
+        got = HO.run(i, spec, HO.oracle_ops(O), inp)
+        assert O.nrmse(got, want) <= 1e-5, name
+        n += 1
+    assert n == 23
+
+
+@pytest.mark.skipif(not O.has_ref(), reason="oracle/_ref not built (needs the reference sources)")
+def test_reference_executor_reproduces_its_fixtures():
+    # the reference build here gives the committed fixtures back
+    for HO, i, name, spec, inp, want in _host_ops():
+        got = HO.run(i, spec, HO.reference_ops(O), inp)
+        assert O.nrmse(got, want) <= 1e-6, name
