@@ -658,11 +658,17 @@ def e2e_run(args, w: dict, raws: dict, Z, torch) -> dict:
     b.synchronize()
     ms = a.elapsed_time(b) / steps
     h2d = sum(M * members[0][2] * 4 for _, members in groups)
-    d2h = sum(sum(M * N * 4 for _, N, _ in members) + 4 for _, members in groups)
+    # results that hold bf16 values (GGML_XDNA_OUT16=1, the default) cross
+    # PCIe as bf16 and are widened to f32 on host threads inside the call
+    # (GGML_ZEST_WIRE16=0 sends the f32)
+    out_bytes = 2 if os.environ.get("GGML_ZEST_WIRE16", "1") != "0" and \
+        os.environ.get("GGML_XDNA_OUT16", "1") != "0" else 4
+    d2h = sum(sum(M * N * out_bytes for _, N, _ in members) + 4 for _, members in groups)
     npu.close()
     return {"value": flops(w) / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms, "tokens_per_s": M / (ms * 1e-3), "steps": steps,
-            "api": "zest_mul_mat_group (include/zest_b200.h), host buffers, one call per shared input"}
+            "api": "zest_mul_mat_group (include/zest_b200.h), host buffers, one call per shared input; f32 in, "
+                   "f32 out (bf16-rounded results cross PCIe as bf16 and are widened on the host)"}
 
 
 # ---------------------------------------------------------------------------

@@ -1,6 +1,7 @@
 // The C ABI of libzest_b200.so (include/zest_b200.h): the stream-level
 // kernel entry points and the matmul service zest_npu, the counterpart of
 // the reference's xdna_npu (src/xdna-npu.{h,cpp}).
+#include "host_copy.h"
 #include "zest_b200.h"
 #include "zest_device.cuh"
 #include "zest_internal.h"
@@ -11,8 +12,10 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <vector>
 
@@ -62,6 +65,19 @@ __global__ void check_finite_kernel(const float *y, int64_t n, unsigned *err) {
     for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x)
         bad |= (__float_as_uint(y[i]) & 0x7f800000u) == 0x7f800000u;
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x % 32) == 0) atomicOr(err, ERR_NOT_FINITE);
+}
+
+// The high 16 bits of n floats that hold bf16 values (the low bits zero):
+// the values themselves, in half the bytes, for the copy to the host.
+__global__ void narrow_bf16_kernel(const float *__restrict__ y, int64_t n, uint16_t *__restrict__ out) {
+    const int64_t stride = (int64_t) gridDim.x * blockDim.x;
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const uint4 v = reinterpret_cast<const uint4 *>(y)[i];
+        reinterpret_cast<uint2 *>(out)[i] = make_uint2((v.x >> 16) | (v.y & 0xffff0000u), (v.z >> 16) | (v.w & 0xffff0000u));
+    }
+    for (int64_t i = n4 * 4 + blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = (uint16_t) (__float_as_uint(y[i]) >> 16);
 }
 
 }  // namespace zest
@@ -137,9 +153,15 @@ struct zest_npu {
     float *x_dev = nullptr, *y_dev = nullptr;
     uint16_t *a_bf16 = nullptr;
     size_t x_cap = 0, y_cap = 0, a_cap = 0;
+    // host-buffer calls: bf16-rounded results cross PCIe as bf16 (y16_dev ->
+    // pinned y16_host) and host threads widen them into the caller's f32
+    uint16_t *y16_dev = nullptr, *y16_host = nullptr;
+    size_t y16_cap = 0, y16_host_cap = 0;
+    std::unique_ptr<host_pool> pool;
     unsigned *err_dev = nullptr, *err_host = nullptr;
     cudaEvent_t ev[5] = {};
     cudaEvent_t in_ev[MAX_CHUNKS] = {}, done_ev[MAX_CHUNKS] = {}, out_ev = nullptr;  // ordering only
+    cudaEvent_t copied_ev[MAX_CHUNKS] = {};  // a chunk's results are in host memory
     cudaEvent_t t_pack[MAX_CHUNKS] = {}, t_gemm[MAX_CHUNKS] = {}, t_end[MAX_CHUNKS] = {};
     zest_times times = {};
     // whether GGML_XDNA_FAIL_AFTER / _NAN_AFTER apply: not to the start-up
@@ -158,12 +180,14 @@ struct zest_npu {
         cudaFree(x_dev);
         cudaFree(y_dev);
         cudaFree(a_bf16);
+        cudaFree(y16_dev);
+        if (y16_host) cudaFreeHost(y16_host);
         cudaFree(err_dev);
         if (err_host) cudaFreeHost(err_host);
         for (cudaEvent_t e : ev)
             if (e) cudaEventDestroy(e);
         for (int c = 0; c < MAX_CHUNKS; c++)
-            for (cudaEvent_t e : { in_ev[c], done_ev[c], t_pack[c], t_gemm[c], t_end[c] })
+            for (cudaEvent_t e : { in_ev[c], done_ev[c], copied_ev[c], t_pack[c], t_gemm[c], t_end[c] })
                 if (e) cudaEventDestroy(e);
         if (out_ev) cudaEventDestroy(out_ev);
         if (st) cudaStreamDestroy(st);
@@ -189,6 +213,36 @@ static bool grow(void **p, size_t *cap, size_t need) {
     if (cudaMalloc(p, need) != cudaSuccess) return false;
     *cap = need;
     return true;
+}
+
+static bool grow_pinned(void **p, size_t *cap, size_t need) {
+    if (need <= *cap) return true;
+    if (*p) cudaFreeHost(*p);
+    *p = nullptr;
+    *cap = 0;
+    if (cudaMallocHost(p, need) != cudaSuccess) return false;
+    *cap = need;
+    return true;
+}
+
+// Host threads for widening results, GGML_ZEST_HOST_THREADS (default: the
+// machine's, at most 32).
+static int host_threads() {
+    static const int n = [] {
+        const long long v = env_ll("GGML_ZEST_HOST_THREADS", 0);
+        if (v > 0) return (int) v;
+        const unsigned hc = std::thread::hardware_concurrency();
+        return (int) std::min<unsigned>(32, hc ? hc : 8);
+    }();
+    return n;
+}
+
+// Whether a host-buffer call sends this weight's results as bf16: they hold
+// bf16 values exactly (the bf16 output mode, and SwiGLU's), unless
+// GGML_ZEST_WIRE16=0.
+static bool wire16(int mode) {
+    static const bool on = env_ll("GGML_ZEST_WIRE16", 1) != 0;
+    return on && (mode == MODE_BF16 || mode == MODE_SWIGLU);
 }
 
 // GGML_XDNA_FAIL_AFTER=n: every submission after the n-th fails, to test the
@@ -362,6 +416,7 @@ zest_npu *zest_open(int device) {
     for (int c = 0; c < zest_npu::MAX_CHUNKS && e == cudaSuccess; c++) {
         e = cudaEventCreateWithFlags(&npu->in_ev[c], cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&npu->done_ev[c], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&npu->copied_ev[c], cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreate(&npu->t_pack[c]);
         if (e == cudaSuccess) e = cudaEventCreate(&npu->t_gemm[c]);
         if (e == cudaSuccess) e = cudaEventCreate(&npu->t_end[c]);
@@ -465,6 +520,23 @@ int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *f
     // 128-row tile) whose copies in and out overlap the other chunks' kernels.
     const int64_t rows = on_device ? T : chunk_rows(T);
     const int nch = (int) ((T + rows - 1) / rows);
+    // Host buffers: results that hold bf16 values cross PCIe as bf16 and are
+    // widened on the host, chunk by chunk as their copies land.
+    bool w16[4] = {};
+    size_t y16_off[4] = {}, y16_total = 0;
+    for (int i = 0; i < n; i++) {
+        w16[i] = !on_device && wire16(w[i]->mode);
+        if (w16[i]) {
+            y16_off[i] = y16_total;
+            y16_total += (size_t) (T * w[i]->n_out);
+        }
+    }
+    if (y16_total) {
+        if (!grow((void **) &npu->y16_dev, &npu->y16_cap, y16_total * 2) ||
+            !grow_pinned((void **) &npu->y16_host, &npu->y16_host_cap, y16_total * 2))
+            return set_error("zest_mul_mat: out of memory for the bf16 copies of the results");
+        if (!npu->pool) npu->pool.reset(new host_pool(host_threads()));
+    }
     cudaEventRecord(npu->ev[0], st);
     cudaMemsetAsync(npu->err_dev, 0, sizeof(unsigned), st);
     cudaStreamWaitEvent(npu->st_in, npu->ev[0], 0);
@@ -492,13 +564,42 @@ int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *f
                 check_finite_kernel<<<148, 256, 0, st>>>(segs[i].c, m * w[i]->n_out, npu->err_dev);
             }
         }
+        if (!rc)
+            for (int i = 0; i < n; i++)
+                if (w16[i])
+                    narrow_bf16_kernel<<<148, 256, 0, st>>>(segs[i].c, m * w[i]->n_out,
+                                                             npu->y16_dev + y16_off[i] + r0 * w[i]->n_out);
         cudaEventRecord(npu->t_end[c], st);
         if (!on_device) {
             cudaEventRecord(npu->done_ev[c], st);
             cudaStreamWaitEvent(npu->st_out, npu->done_ev[c], 0);
-            for (int i = 0; i < n; i++)
-                cudaMemcpyAsync(y[i] + r0 * w[i]->n_out, segs[i].c, (size_t) (m * w[i]->n_out) * 4,
-                                cudaMemcpyDeviceToHost, npu->st_out);
+            for (int i = 0; i < n; i++) {
+                const size_t at = y16_off[i] + (size_t) (r0 * w[i]->n_out), cnt = (size_t) (m * w[i]->n_out);
+                if (w16[i])
+                    cudaMemcpyAsync(npu->y16_host + at, npu->y16_dev + at, cnt * 2, cudaMemcpyDeviceToHost,
+                                    npu->st_out);
+                else
+                    cudaMemcpyAsync(y[i] + r0 * w[i]->n_out, segs[i].c, cnt * 4, cudaMemcpyDeviceToHost,
+                                    npu->st_out);
+            }
+            cudaEventRecord(npu->copied_ev[c], npu->st_out);
+        }
+    }
+    // the bf16 results widened into the caller's f32 buffers as each chunk's
+    // copy lands (the later chunks' copies continue meanwhile)
+    for (int c = 0; c < nch && y16_total && !rc; c++) {
+        const cudaError_t ce = cudaEventSynchronize(npu->copied_ev[c]);
+        if (ce != cudaSuccess) {
+            rc = cuda_fail("zest_mul_mat", ce);
+            break;
+        }
+        const int64_t r0 = c * rows, m = std::min(rows, T - r0);
+        for (int i = 0; i < n; i++) {
+            if (!w16[i]) continue;
+            const uint16_t *src = npu->y16_host + y16_off[i] + r0 * w[i]->n_out;
+            float *dst = y[i] + r0 * w[i]->n_out;
+            npu->pool->run(m * w[i]->n_out, 1 << 16,
+                           [src, dst](int64_t lo, int64_t hi) { widen_bf16(src + lo, dst + lo, hi - lo); });
         }
     }
     cudaMemcpyAsync(npu->err_host, npu->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);

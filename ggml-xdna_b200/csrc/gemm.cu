@@ -416,23 +416,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // ---------------------------------------------------------------------------
 
 constexpr int P_BM = 256;
-constexpr int P_EPI_BYTES = 4 * 2 * 32 * 32 * 4;  // per epilogue warp, two 32 x 32 fp32 staging buffers
 
 // The pair kernel's shape for an N tile of P_BN columns (a multiple of 32,
-// at most 256): each CTA holds 128 rows of A and P_BN/2 rows of B per stage,
-// in about 192 KB of ring; the two accumulators sit 256 TMEM columns apart.
-template <int BN_T>
+// at most 256): each CTA holds 128 rows of A and P_BN/2 rows of B per stage;
+// each of the 4 epilogue warps has NBUF 32 x 32 fp32 staging buffers for its
+// TMA stores; the ring takes what is left of 224 KB. The two accumulators
+// sit 256 TMEM columns apart.
+template <int BN_T, int NBUF>
 struct pair_cfg {
     static constexpr int P_BN = BN_T;
+    static constexpr int P_EPI_BYTES = 4 * NBUF * 32 * 32 * 4;
     static constexpr int P_A_BYTES = 128 * BK * 2;       // this CTA's half of A
     static constexpr int P_B_BYTES = (BN_T / 2) * BK * 2; // this CTA's half of B
     static constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-    static constexpr int P_STAGES = 196608 / P_STAGE_BYTES;
+    static constexpr int P_STAGES = (229376 - P_EPI_BYTES) / P_STAGE_BYTES;
     static constexpr int P_NUM_BARRIERS = 2 * P_STAGES + 5;
     static constexpr int P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + P_NUM_BARRIERS * 8 + 16;
     static constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (BN_T >> 3) << 17) |
                                         ((uint32_t) (P_BM >> 4) << 24);
     static_assert(BN_T % 32 == 0 && BN_T <= 256 && P_STAGE_BYTES % 1024 == 0, "pair tile shape");
+    static_assert(NBUF >= 2 && P_STAGES >= 4, "staging buffers and ring stages");
 };
 
 // A grouped launch: up to MAX_SEG weights sharing one A (q, k and v; gate
@@ -552,13 +555,13 @@ __device__ __forceinline__ void pair_tile_coords(int t, const pair_params &pp, i
 
 // SK: whether this instance walks stream-K runs (a separate instance, so the
 // whole-tile kernel carries none of that code or its registers).
-template <int BN_T, bool SK>
+template <int BN_T, bool SK, int NBUF>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ pair_maps maps,
                              const __grid_constant__ pair_params pp) {
-    using C = pair_cfg<BN_T>;
+    using C = pair_cfg<BN_T, NBUF>;
     constexpr int P_BN = C::P_BN, P_A_BYTES = C::P_A_BYTES, P_STAGE_BYTES = C::P_STAGE_BYTES,
-                  P_STAGES = C::P_STAGES, P_NUM_BARRIERS = C::P_NUM_BARRIERS;
+                  P_STAGES = C::P_STAGES, P_NUM_BARRIERS = C::P_NUM_BARRIERS, P_EPI_BYTES = C::P_EPI_BYTES;
     constexpr uint32_t P_IDESC = C::P_IDESC;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
@@ -706,7 +709,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else {
         const int q = warp % 4;
-        const uint32_t tempty_leader[2] = { map_to_rank(&tempty[0], 0), map_to_rank(&tempty[1], 0) };
+        const uint32_t tempty_leader0 = map_to_rank(&tempty[0], 0), tempty_leader1 = map_to_rank(&tempty[1], 0);
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t bad = 0;
@@ -773,7 +776,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (ch + 1 < P_BN / 32) tmem_ld_32x32b_x32(tbase + (uint32_t) ((ch + 1) * 32), nx);
                 if (ch == P_BN / 32 - 1) {
                     tc_fence_before();
-                    mbar_arrive_cluster(tempty_leader[acc]);
+                    mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
                 }
                 if (part) {
                     float *dst = g_sk_part + (size_t) blockIdx.x * SK_SLOT_FLOATS;
@@ -814,9 +817,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     continue;
                 }
                 // this warp's 32 rows x 32 columns through a 128-byte-swizzled
-                // staging buffer (double-buffered) and one TMA store
-                uint8_t *buf = epi + (q * 2 + (ch & 1)) * 4096;
-                if (lane == 0) bulk_wait_read_1();  // the store from two chunks ago has read this buffer
+                // staging buffer (NBUF of them in turn) and one TMA store
+                uint8_t *buf = epi + (q * NBUF + (ch % NBUF)) * 4096;
+                if (lane == 0) bulk_wait_read<NBUF - 1>();  // the store NBUF chunks ago has read this buffer
                 __syncwarp();
                 float o[32];
 #pragma unroll
@@ -1078,10 +1081,10 @@ void sk_release(cudaStream_t st) {
 // The pair kernel for an N tile of BN_T over a group of weights sharing A:
 // B's tensor maps (BN_T/2-row boxes, one per CTA), the outputs' for TMA
 // stores, a cluster-of-2 launch.
-template <int BN_T>
+template <int BN_T, int NBUF>
 int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, const gemm_seg *segs, const gemm_plan &gp,
                       unsigned *err_flag, cudaStream_t st) {
-    using C = pair_cfg<BN_T>;
+    using C = pair_cfg<BN_T, NBUF>;
     pair_maps maps;
     pair_params pp;
     memset(&maps, 0, sizeof maps);
@@ -1127,9 +1130,9 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
         cudaGetDevice(&dev);
         std::lock_guard<std::mutex> lk(mu);
         if (dev >= 64 || !((set_on >> dev) & 1)) {
-            if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T, false>,
+            if (cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T, false, NBUF>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::P_SMEM_BYTES) != cudaSuccess ||
-                cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T, true>,
+                cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<BN_T, true, NBUF>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::P_SMEM_BYTES) != cudaSuccess)
                 return check_launch("gemm (shared memory size)");
             if (dev < 64) set_on |= 1ull << dev;
@@ -1166,9 +1169,9 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (sk)
-        cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T, true>, ta, maps, pp);
+        cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T, true, NBUF>, ta, maps, pp);
     else
-        cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T, false>, ta, maps, pp);
+        cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel<BN_T, false, NBUF>, ta, maps, pp);
     if (sk) sk_release(st);
     return check_launch("gemm");
 }
@@ -1254,10 +1257,10 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
         return 0;
     }
     switch (gp.bn) {
-        case 192: return launch_pair_group<192>(ta, M, K, nseg, segs, gp, err_flag, st);
-        case 160: return launch_pair_group<160>(ta, M, K, nseg, segs, gp, err_flag, st);
-        case 128: return launch_pair_group<128>(ta, M, K, nseg, segs, gp, err_flag, st);
-        default: return launch_pair_group<256>(ta, M, K, nseg, segs, gp, err_flag, st);
+        case 192: return launch_pair_group<192, 2>(ta, M, K, nseg, segs, gp, err_flag, st);
+        case 160: return launch_pair_group<160, 2>(ta, M, K, nseg, segs, gp, err_flag, st);
+        case 128: return launch_pair_group<128, 2>(ta, M, K, nseg, segs, gp, err_flag, st);
+        default: return launch_pair_group<256, 2>(ta, M, K, nseg, segs, gp, err_flag, st);
     }
 }
 

@@ -212,3 +212,46 @@ def test_host_buffer_chunks_equal_one_pass():
     env = dict(os.environ, GGML_ZEST_CHUNK_ROWS="256")
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
     assert "CHUNKS OK" in r.stdout, r.stdout + r.stderr
+
+
+_WIRE_CHILD = """
+import sys
+sys.path[:0] = [{root!r}, {pkg!r}, {tests!r}]
+import numpy as np, torch, zest_b200 as Z
+from oracle import oracle as O
+npu = Z.Npu(0)  # GGML_XDNA_OUT16 unset: bf16-rounded results
+K, T, F = 512, 1000, 300
+raws = [O.quantize(O.Q8_0, O.weights_f32(N, K, 80 + N)) for N in (768, 512)]
+keys = [Z.Npu.key(r.ctypes.data, O.Q8_0, K, N) for r, N in zip(raws, (768, 512))]
+for k, r in zip(keys, raws):
+    npu.add_weight(k, r.ctypes.data, on_device=False)
+g, u = (O.quantize(O.Q8_0, O.weights_f32(F, K, s)) for s in (90, 91))
+gkey = Z.Npu.key(g.ctypes.data, O.Q8_0, K, F)
+npu.add_fused(gkey, g.ctypes.data, u.ctypes.data, on_device=False)
+x = O.activations(T, K, 92)
+xp = torch.from_numpy(x).pin_memory()
+ys = [torch.empty((T, N), dtype=torch.float32).pin_memory() for N in (768, 512)]
+npu.mul_mat_group(keys, xp.data_ptr(), T, [y.data_ptr() for y in ys], False)
+sw = np.empty((T, F), np.float32)  # pageable host memory, SwiGLU results
+npu.mul_mat(gkey, x.ctypes.data, T, sw.ctypes.data, False, fused=True)
+np.savez({out!r}, y0=ys[0].numpy(), y1=ys[1].numpy(), sw=sw)
+"""
+
+
+def test_host_results_cross_pcie_as_bf16_exactly(tmp_path):
+    # host-buffer calls send bf16-rounded results (the default output mode,
+    # SwiGLU) to the host as bf16 and widen them there: the same f32 bits as
+    # sending the f32 values (GGML_ZEST_WIRE16=0), chunk by chunk
+    root = Z.PKG_DIR.parent
+    got = {}
+    for wire in ("1", "0"):
+        out = tmp_path / f"wire{wire}.npz"
+        code = _WIRE_CHILD.format(root=str(root), pkg=str(Z.PKG_DIR), tests=str(root / "tests"), out=str(out))
+        env = dict(os.environ, GGML_ZEST_CHUNK_ROWS="256", GGML_ZEST_WIRE16=wire)
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
+        assert r.returncode == 0, r.stdout + r.stderr
+        got[wire] = np.load(out)
+    for k in ("y0", "y1", "sw"):
+        a, b = got["1"][k], got["0"][k]
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), k
+        assert np.array_equal(a, O.round_bf16(a)), k
