@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], 4);  // one arrive per epilogue warp
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -375,8 +375,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tmem_ld_32x32b_x32(tbase + (uint32_t) (ch * 32), r);
                 tmem_ld_wait();
                 if (ch == BN / 32 - 1) {
+                    // the warp's loads of this accumulator are done: one
+                    // elected arrive hands it back to the MMA warp
                     tc_fence_before();
-                    mbar_arrive(&tempty[acc]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[acc]);
                 }
                 const int64_t col0 = (int64_t) nb * BN + ch * 32;
                 if (col0 < p.N) bad |= store_chunk(p, r, row, col0);
@@ -410,7 +413,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //              both CTAs' TMA loads complete on it
 //   empty[s]   each CTA: the leader's commit, multicast to both
 //   tfull[a]   each CTA: the leader's commit, multicast to both
-//   tempty[a]  leader: all 256 epilogue threads of the pair arrive
+//   tempty[a]  leader: each of the pair's 8 epilogue warps arrives once
 // Cluster syncs bracket barrier set-up and TMEM release, so neither CTA's
 // barriers are used before they exist or after it exits.
 // ---------------------------------------------------------------------------
@@ -582,7 +585,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 256);
+            mbar_init(&tempty[a], 8);  // one arrive per epilogue warp of the pair
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -775,8 +778,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int i = 0; i < 32; i++) r[i] = nx[i];
                 if (ch + 1 < P_BN / 32) tmem_ld_32x32b_x32(tbase + (uint32_t) ((ch + 1) * 32), nx);
                 if (ch == P_BN / 32 - 1) {
+                    // the warp's loads of this accumulator are done: one
+                    // elected arrive per warp (8 for the pair, not 256
+                    // arrivals of which half cross to the leader CTA) hands
+                    // it back to the MMA warp
                     tc_fence_before();
-                    mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
                 }
                 if (part) {
                     float *dst = g_sk_part + (size_t) blockIdx.x * SK_SLOT_FLOATS;
