@@ -1321,6 +1321,9 @@ enum ggml_status backend_graph_compute(ggml_backend_t backend, ggml_cgraph *cgra
 
 // Weight copies made as soon as llama.cpp plans a piece
 // (src/ggml-zest.cpp:928-965): the first prompt then need not wait for them.
+// Their conversions are queued on the service's load stream and run while
+// llama.cpp carries on (the reference's background builder, :261-330); the
+// first matmul that uses a copy waits for it on the GPU.
 // GGML_XDNA_COPY_AT_LOAD=0 leaves them to the first prompt.
 void backend_graph_optimize(ggml_backend_t backend, ggml_cgraph *cgraph, ggml_backend_graph_optimize_params *) {
     static const bool at_load = env_int("GGML_XDNA_COPY_AT_LOAD", 1) != 0;
@@ -1421,6 +1424,10 @@ ggml_backend_t dev_init_backend(ggml_backend_dev_t dev, const char *) {
         delete ctx;
         return nullptr;
     }
+    // weight copies from device-resident weights are built on the service's
+    // load stream; a claimed matmul waits for its copy on the GPU
+    // (GGML_ZEST_ASYNC_COPIES=0: built before graph_optimize returns)
+    zest_set_load_async(ctx->npu, env_int("GGML_ZEST_ASYNC_COPIES", 1) != 0 ? 1 : 0);
     // the IQ3_S converter's codebook, as the host ggml dequantises it
     const std::vector<uint32_t> &grid = iq3s_codebook();
     if (!grid.empty() && zest_load_iq3s_grid(grid.data())) {

@@ -139,6 +139,7 @@ struct zest_npu {
         uint16_t *bf16 = nullptr;   // [n_pad][K]
         int64_t K = 0, N = 0, n_pad = 0, n_out = 0;
         int mode = 0;
+        cudaEvent_t ready = nullptr;  // built on the load stream: recorded after its conversion
     };
     using key_t = std::tuple<const void *, const void *, int, int64_t, int64_t, int>;
 
@@ -147,6 +148,10 @@ struct zest_npu {
     static constexpr int MAX_CHUNKS = 16;
     int device = 0;
     cudaStream_t st = nullptr, st_in = nullptr, st_out = nullptr;
+    // weight copies from device-resident raw bytes are built on st_load
+    // without the host waiting, when async_load is on (zest_set_load_async)
+    cudaStream_t st_load = nullptr;
+    bool async_load = false;
     bool out16 = true;
     std::map<key_t, weight> weights;
     // per-call workspace; grows only
@@ -173,9 +178,11 @@ struct zest_npu {
         if (st) cudaStreamSynchronize(st);
         if (st_in) cudaStreamSynchronize(st_in);
         if (st_out) cudaStreamSynchronize(st_out);
+        if (st_load) cudaStreamSynchronize(st_load);
         for (auto &kv : weights) {
             cudaFree(kv.second.bytes);
             cudaFree(kv.second.bf16);
+            if (kv.second.ready) cudaEventDestroy(kv.second.ready);
         }
         cudaFree(x_dev);
         cudaFree(y_dev);
@@ -193,6 +200,7 @@ struct zest_npu {
         if (st) cudaStreamDestroy(st);
         if (st_in) cudaStreamDestroy(st_in);
         if (st_out) cudaStreamDestroy(st_out);
+        if (st_load) cudaStreamDestroy(st_load);
     }
 
     static key_t key_of(const zest_wkey *k, int fused) { return key_t(k->buffer, k->data, k->type, k->K, k->N, fused); }
@@ -302,6 +310,36 @@ static int add_copy(zest_npu *npu, const zest_wkey *key, const void *raw0, const
     w.n_pad = fused ? 2 * ((N + 255) / 256 * 256) : (N + 511) / 512 * 512;  // pad_f / pad_n (xdna-npu.cpp:46-47)
     w.mode = fused ? MODE_SWIGLU : (npu->out16 ? MODE_BF16 : MODE_F32);
     const size_t raw_bytes = (size_t) (row_bytes * N);
+    if (npu->async_load && raw_on_device) {
+        // built on the load stream; the first call that uses the copy waits
+        // for its event on the GPU, not the host (the reference's background
+        // copy builder, src/ggml-zest.cpp:261-330)
+        cudaError_t e = cudaMalloc(&w.bytes, (size_t) (w.n_pad * K / 8 * BLOCK_BYTES));
+        if (e == cudaSuccess) e = cudaMalloc(&w.bf16, (size_t) (w.n_pad * K) * 2);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&w.ready, cudaEventDisableTiming);
+        int rc = e == cudaSuccess ? 0 : cuda_fail("zest_add_weight: allocating the weight copy", e);
+        if (!rc)
+            rc = launch_convert_weight(ctype, raw0, fused ? raw1 : raw0, fused, N, 0, N, K, w.n_pad, w.bytes, w.bf16,
+                                       npu->st_load);
+        if (!rc && (e = cudaEventRecord(w.ready, npu->st_load)) != cudaSuccess) rc = cuda_fail("zest_add_weight", e);
+        if (rc) {
+            cudaFree(w.bytes);
+            cudaFree(w.bf16);
+            if (w.ready) cudaEventDestroy(w.ready);
+            return rc;
+        }
+        auto k = zest_npu::key_of(key, fused);
+        auto old = npu->weights.find(k);
+        if (old != npu->weights.end()) {
+            // an older copy under the same key may still be read by queued work
+            cudaDeviceSynchronize();
+            cudaFree(old->second.bytes);
+            cudaFree(old->second.bf16);
+            if (old->second.ready) cudaEventDestroy(old->second.ready);
+        }
+        npu->weights[k] = w;
+        return 0;
+    }
     const void *src0 = raw0, *src1 = raw1;
     void *staged[2] = { nullptr, nullptr };
     cudaEvent_t t0 = npu->ev[0], t1 = npu->ev[1];
@@ -342,8 +380,10 @@ static int add_copy(zest_npu *npu, const zest_wkey *key, const void *raw0, const
     auto k = zest_npu::key_of(key, fused);
     auto old = npu->weights.find(k);
     if (old != npu->weights.end()) {
+        cudaDeviceSynchronize();
         cudaFree(old->second.bytes);
         cudaFree(old->second.bf16);
+        if (old->second.ready) cudaEventDestroy(old->second.ready);
     }
     npu->weights[k] = w;
     return 0;
@@ -411,6 +451,7 @@ zest_npu *zest_open(int device) {
     cudaError_t e = cudaStreamCreateWithFlags(&npu->st, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&npu->st_in, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&npu->st_out, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&npu->st_load, cudaStreamNonBlocking);
     for (cudaEvent_t &ev : npu->ev)
         if (e == cudaSuccess) e = cudaEventCreate(&ev);
     for (int c = 0; c < zest_npu::MAX_CHUNKS && e == cudaSuccess; c++) {
@@ -477,13 +518,26 @@ int64_t zest_out_width(const zest_npu *npu, const zest_wkey *key, int fused) {
 
 const uint8_t *zest_weight_bfp16(const zest_npu *npu, const zest_wkey *key, int fused) {
     const zest_npu::weight *w = npu && key ? npu->find(key, fused) : nullptr;
+    if (w && w->ready) cudaEventSynchronize(w->ready);  // a copy still being built on the load stream
     return w ? w->bytes : nullptr;
 }
 
 const uint16_t *zest_weight_bf16(const zest_npu *npu, const zest_wkey *key, int fused, int64_t *n_pad) {
     const zest_npu::weight *w = npu && key ? npu->find(key, fused) : nullptr;
+    if (w && w->ready) cudaEventSynchronize(w->ready);
     if (w && n_pad) *n_pad = w->n_pad;
     return w ? w->bf16 : nullptr;
+}
+
+void zest_set_load_async(zest_npu *npu, int on) {
+    if (npu) npu->async_load = on != 0;
+}
+
+int zest_wait_weights(zest_npu *npu) {
+    if (!npu) return set_error("zest_wait_weights: no service");
+    if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_wait_weights: cannot select the device");
+    const cudaError_t e = cudaStreamSynchronize(npu->st_load);
+    return e == cudaSuccess ? 0 : cuda_fail("zest_wait_weights", e);
 }
 
 void *zest_stream(zest_npu *npu) { return npu ? (void *) npu->st : nullptr; }
@@ -500,6 +554,8 @@ int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *f
     if (T <= 0) return 0;
     if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_mul_mat: cannot select the device");
     if (npu->inject && injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
+    for (int i = 0; i < n; i++)
+        if (w[i]->ready) cudaStreamWaitEvent(npu->st, w[i]->ready, 0);  // its copy is built (load stream)
     const int64_t K = w[0]->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
     const size_t x_bytes = (size_t) (T * K) * 4;
     size_t y_off[4], y_total = 0;
@@ -644,6 +700,8 @@ int zest_mul_mat_group_ex(zest_npu *npu, int n, const zest_wkey *keys, const int
     if (T <= 0) return 0;
     if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_mul_mat_group_ex: cannot select the device");
     if (npu->inject && injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
+    for (int i = 0; i < n; i++)
+        if (w[i]->ready) cudaStreamWaitEvent(npu->st, w[i]->ready, 0);  // its copy is built (load stream)
     const int64_t K = w[0]->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
     cudaStream_t st = npu->st;
     const bool nan = npu->inject && injected_nan();

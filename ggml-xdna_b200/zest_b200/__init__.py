@@ -105,6 +105,8 @@ def lib() -> ctypes.CDLL:
         "zest_out_width": (_i64, [_vp, ctypes.POINTER(WKey), _int]),
         "zest_weight_bfp16": (_vp, [_vp, ctypes.POINTER(WKey), _int]),
         "zest_weight_bf16": (_vp, [_vp, ctypes.POINTER(WKey), _int, ctypes.POINTER(_i64)]),
+        "zest_set_load_async": (None, [_vp, _int]),
+        "zest_wait_weights": (_int, [_vp]),
         "zest_mul_mat": (_int, [_vp, ctypes.POINTER(WKey), _int, _vp, _i64, _vp, _int]),
         "zest_mul_mat_group": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, _i64, _vpp, _int]),
         "zest_mul_mat_group_ex": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, ctypes.c_float, _vp, _vp, _vp,
@@ -128,7 +130,8 @@ def exported_symbols() -> list[str]:
                         "zest_usable", "zest_open",
                         "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
                         "zest_add_weight_values",
-                        "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_mul_mat",
+                        "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_set_load_async",
+                        "zest_wait_weights", "zest_mul_mat",
                         "zest_mul_mat_group", "zest_mul_mat_group_ex", "zest_stream", "zest_take_times")]
 
 
@@ -281,6 +284,12 @@ class Npu:
 
     def set_out16(self, on: bool):
         lib().zest_set_out16(self.h, int(on))
+
+    def set_load_async(self, on: bool):
+        lib().zest_set_load_async(self.h, int(on))
+
+    def wait_weights(self):
+        _check(lib().zest_wait_weights(self.h), "zest_wait_weights")
 
     @staticmethod
     def key(data_addr: int, qtype: int, K: int, N: int, buffer: int = 0) -> WKey:

@@ -309,6 +309,20 @@ int zest_add_fused(zest_npu *npu, const zest_wkey *gate, const void *gate_raw, c
  * (xdna_npu::out_width, src/xdna-npu.h:74). -1 if unknown. */
 int64_t zest_out_width(const zest_npu *npu, const zest_wkey *key, int fused);
 
+/* Weight copies built without the host waiting. On (on = 1), a copy added
+ * from raw bytes already in device memory (zest_add_weight /
+ * zest_add_fused with raw_on_device) is converted on the service's load
+ * stream and the call returns at once; the first matmul that uses it waits
+ * for it on the GPU, and zest_weight_bf16 / zest_weight_bfp16 wait for it on
+ * the host before handing out its buffers. The raw bytes must stay in place
+ * until then. Copies from host memory are built before the call returns, as
+ * with it off (the default). zest_wait_weights waits for every copy queued.
+ * Replaces: the background weight-copy builder that graph_optimize queues
+ * and graph_compute waits for (queue_copies / build_copies / finish_copies,
+ * src/ggml-zest.cpp:261-330). */
+void zest_set_load_async(zest_npu *npu, int on);
+int zest_wait_weights(zest_npu *npu);
+
 /* The weight copy's device buffers, for callers that run the kernels
  * themselves (NULL if unknown). */
 const uint8_t *zest_weight_bfp16(const zest_npu *npu, const zest_wkey *key, int fused);

@@ -255,3 +255,33 @@ def test_host_results_cross_pcie_as_bf16_exactly(tmp_path):
         a, b = got["1"][k], got["0"][k]
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), k
         assert np.array_equal(a, O.round_bf16(a)), k
+
+
+def test_async_weight_copies_equal_synchronous_ones():
+    # with zest_set_load_async, copies from device-resident raw bytes are
+    # built on the service's load stream and the add returns at once; the
+    # first matmul waits for them on the GPU (the reference builds its copies
+    # on a background thread, src/ggml-zest.cpp:261-330)
+    N, K, T = 2048, 2560, 512
+    raws = [O.quantize(O.Q4_K, O.weights_f32(N, K, 100 + i)) for i in range(4)]
+    devs = [torch.from_numpy(r).cuda() for r in raws]
+    keys = [Z.Npu.key(d.data_ptr(), O.Q4_K, K, N) for d in devs]
+    x = dev(O.activations(T, K, 7))
+    torch.cuda.synchronize()
+    outs = {}
+    for mode in ("async", "sync"):
+        npu = Z.Npu(0)
+        npu.set_out16(False)
+        npu.set_load_async(mode == "async")
+        for k, d in zip(keys, devs):
+            npu.add_weight(k, d.data_ptr(), on_device=True)
+        ys = [torch.empty((T, N), dtype=torch.float32, device="cuda") for _ in keys]
+        for k, y in zip(keys, ys):
+            npu.mul_mat(k, x.data_ptr(), T, y.data_ptr(), on_device=True)
+        w_ptr, n_pad = npu.weight_bf16(keys[-1])  # waits for the copy on the host
+        assert w_ptr and n_pad == N
+        npu.wait_weights()
+        outs[mode] = [host(y) for y in ys]
+        npu.close()
+    for a, b in zip(outs["async"], outs["sync"]):
+        assert np.array_equal(a, b)
