@@ -72,7 +72,12 @@ void host_pool::run(int64_t n, int64_t min_piece, const std::function<void(int64
     }
     job j{ &fn, &next_, n, step, pieces };
     {
-        std::lock_guard<std::mutex> lk(mu_);
+        // A worker that woke late for the last job may still hold it; the
+        // piece counter is shared, so it must let go before the counter
+        // starts again for this job (else it could take one of this job's
+        // pieces and drop it as out of its own range).
+        std::unique_lock<std::mutex> lk(mu_);
+        idle_.wait(lk, [&] { return busy_ == 0; });
         next_ = 0;
         cur_ = j;
         finished_ = 0;
