@@ -133,6 +133,65 @@ int zest_gemm(const uint16_t *a_bf16, int64_t lda, const uint16_t *b_bf16, int64
 // the matmul service
 // ---------------------------------------------------------------------------
 
+// One call's device and host buffers and events. Slot 0 serves the
+// synchronous calls; slots 1..ZEST_SLOTS the calls zest_submit_group starts
+// and zest_wait_group finishes, several of which may be in flight at once
+// (their copies in, kernels and copies out queue on the service's three
+// streams in submission order, so one call's copy in overlaps another's copy
+// out).
+struct call_slot {
+    static constexpr int MAX_CHUNKS = 16;
+    float *x_dev = nullptr, *y_dev = nullptr;
+    size_t x_cap = 0, y_cap = 0;
+    // bf16-rounded results cross PCIe as bf16 (y16_dev -> pinned y16_host)
+    // and host threads widen them into the caller's f32
+    uint16_t *y16_dev = nullptr, *y16_host = nullptr;
+    size_t y16_cap = 0, y16_host_cap = 0;
+    unsigned *err_dev = nullptr, *err_host = nullptr;
+    cudaEvent_t start = nullptr, k_done = nullptr, o_done = nullptr;
+    cudaEvent_t in_ev[MAX_CHUNKS] = {}, done_ev[MAX_CHUNKS] = {};  // ordering only
+    cudaEvent_t copied_ev[MAX_CHUNKS] = {};                          // a chunk's results are in host memory
+    cudaEvent_t t_pack[MAX_CHUNKS] = {}, t_gemm[MAX_CHUNKS] = {}, t_end[MAX_CHUNKS] = {};
+    // the call in flight, from its submission until it is finished
+    bool busy = false, on_device = false;
+    int n = 0, nch = 0;
+    int64_t T = 0, rows = 0;
+    int64_t n_out[4] = {};
+    float *y[4] = {};
+    bool w16[4] = {};
+    size_t y16_off[4] = {};
+
+    cudaError_t create() {
+        cudaError_t e = cudaSuccess;
+        for (cudaEvent_t *ev : { &start, &k_done, &o_done })
+            if (e == cudaSuccess) e = cudaEventCreate(ev);
+        for (int c = 0; c < MAX_CHUNKS && e == cudaSuccess; c++) {
+            e = cudaEventCreateWithFlags(&in_ev[c], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done_ev[c], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&copied_ev[c], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreate(&t_pack[c]);
+            if (e == cudaSuccess) e = cudaEventCreate(&t_gemm[c]);
+            if (e == cudaSuccess) e = cudaEventCreate(&t_end[c]);
+        }
+        if (e == cudaSuccess) e = cudaMalloc(&err_dev, sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMallocHost(&err_host, sizeof(unsigned));
+        return e;
+    }
+    void destroy() {
+        cudaFree(x_dev);
+        cudaFree(y_dev);
+        cudaFree(y16_dev);
+        if (y16_host) cudaFreeHost(y16_host);
+        cudaFree(err_dev);
+        if (err_host) cudaFreeHost(err_host);
+        for (cudaEvent_t e : { start, k_done, o_done })
+            if (e) cudaEventDestroy(e);
+        for (int c = 0; c < MAX_CHUNKS; c++)
+            for (cudaEvent_t e : { in_ev[c], done_ev[c], copied_ev[c], t_pack[c], t_gemm[c], t_end[c] })
+                if (e) cudaEventDestroy(e);
+    }
+};
+
 struct zest_npu {
     struct weight {
         uint8_t *bytes = nullptr;   // bfp16 B operand, reference layout
@@ -145,7 +204,7 @@ struct zest_npu {
 
     // a host-buffer call is cut into at most MAX_CHUNKS row chunks whose input
     // copies (st_in), kernels (st) and output copies (st_out) overlap
-    static constexpr int MAX_CHUNKS = 16;
+    static constexpr int MAX_CHUNKS = call_slot::MAX_CHUNKS;
     int device = 0;
     cudaStream_t st = nullptr, st_in = nullptr, st_out = nullptr;
     // weight copies from device-resident raw bytes are built on st_load
@@ -154,20 +213,15 @@ struct zest_npu {
     bool async_load = false;
     bool out16 = true;
     std::map<key_t, weight> weights;
-    // per-call workspace; grows only
-    float *x_dev = nullptr, *y_dev = nullptr;
+    // the packed input, shared by every call: its writers and readers all run
+    // on st, in order; grows only
     uint16_t *a_bf16 = nullptr;
-    size_t x_cap = 0, y_cap = 0, a_cap = 0;
-    // host-buffer calls: bf16-rounded results cross PCIe as bf16 (y16_dev ->
-    // pinned y16_host) and host threads widen them into the caller's f32
-    uint16_t *y16_dev = nullptr, *y16_host = nullptr;
-    size_t y16_cap = 0, y16_host_cap = 0;
+    size_t a_cap = 0;
+    // per-call buffers and events: slot 0 for the synchronous calls, the
+    // others for zest_submit_group / zest_wait_group
+    call_slot slots[1 + ZEST_SLOTS];
     std::unique_ptr<host_pool> pool;
-    unsigned *err_dev = nullptr, *err_host = nullptr;
-    cudaEvent_t ev[5] = {};
-    cudaEvent_t in_ev[MAX_CHUNKS] = {}, done_ev[MAX_CHUNKS] = {}, out_ev = nullptr;  // ordering only
-    cudaEvent_t copied_ev[MAX_CHUNKS] = {};  // a chunk's results are in host memory
-    cudaEvent_t t_pack[MAX_CHUNKS] = {}, t_gemm[MAX_CHUNKS] = {}, t_end[MAX_CHUNKS] = {};
+    cudaEvent_t ev[2] = {};  // weight-copy timing
     zest_times times = {};
     // whether GGML_XDNA_FAIL_AFTER / _NAN_AFTER apply: not to the start-up
     // self-test, which the reference runs outside its injection points too
@@ -184,19 +238,10 @@ struct zest_npu {
             cudaFree(kv.second.bf16);
             if (kv.second.ready) cudaEventDestroy(kv.second.ready);
         }
-        cudaFree(x_dev);
-        cudaFree(y_dev);
         cudaFree(a_bf16);
-        cudaFree(y16_dev);
-        if (y16_host) cudaFreeHost(y16_host);
-        cudaFree(err_dev);
-        if (err_host) cudaFreeHost(err_host);
+        for (call_slot &cs : slots) cs.destroy();
         for (cudaEvent_t e : ev)
             if (e) cudaEventDestroy(e);
-        for (int c = 0; c < MAX_CHUNKS; c++)
-            for (cudaEvent_t e : { in_ev[c], done_ev[c], copied_ev[c], t_pack[c], t_gemm[c], t_end[c] })
-                if (e) cudaEventDestroy(e);
-        if (out_ev) cudaEventDestroy(out_ev);
         if (st) cudaStreamDestroy(st);
         if (st_in) cudaStreamDestroy(st_in);
         if (st_out) cudaStreamDestroy(st_out);
@@ -429,6 +474,174 @@ static std::string self_test(int device) {
     return why;
 }
 
+// Queues one group call in `cs`: up to 4 weights sharing the input x.
+// Device buffers: one pass. Host buffers: row chunks (multiples of the
+// 128-row tile) whose copies in (st_in), kernels (st) and copies out (st_out)
+// overlap one another, and the copies of the calls in other slots.
+static int submit_call(zest_npu *npu, call_slot &cs, int n, const zest_wkey *keys, const int *fused, const float *x,
+                       int64_t T, float *const *y, int on_device, const char *what) {
+    if (!keys || n <= 0 || n > 4) return set_error((std::string(what) + ": not 1 to 4 weights").c_str());
+    const zest_npu::weight *w[4];
+    for (int i = 0; i < n; i++) {
+        w[i] = npu->find(&keys[i], fused ? fused[i] : 0);
+        if (!w[i]) return set_error((std::string(what) + ": weight not added").c_str());
+        if (w[i]->K != w[0]->K) return set_error((std::string(what) + ": a group's weights differ in K").c_str());
+    }
+    cs.n = 0;
+    cs.nch = 0;
+    if (T <= 0) {
+        cs.busy = true;  // nothing to do; the wait returns at once
+        return 0;
+    }
+    if (cudaSetDevice(npu->device) != cudaSuccess) return set_error((std::string(what) + ": cannot select the device").c_str());
+    if (npu->inject && injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
+    cudaStream_t st = npu->st;
+    for (int i = 0; i < n; i++)
+        if (w[i]->ready) cudaStreamWaitEvent(st, w[i]->ready, 0);  // its copy is built (load stream)
+    const int64_t K = w[0]->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
+    const size_t x_bytes = (size_t) (T * K) * 4;
+    size_t y_off[4], y_total = 0;
+    for (int i = 0; i < n; i++) {
+        y_off[i] = y_total;
+        y_total += (size_t) (T * w[i]->n_out) * 4;
+    }
+    // (a buffer that must grow is freed first, which waits for the device)
+    if (!grow((void **) &npu->a_bf16, &npu->a_cap, (size_t) (m_pad * K) * 2) ||
+        (!on_device && (!grow((void **) &cs.x_dev, &cs.x_cap, x_bytes) || !grow((void **) &cs.y_dev, &cs.y_cap, y_total))))
+        return set_error((std::string(what) + ": out of GPU memory for the call's buffers").c_str());
+    const float *xd = on_device ? x : cs.x_dev;
+    float *yd[4];
+    for (int i = 0; i < n; i++) yd[i] = on_device ? y[i] : (float *) ((char *) cs.y_dev + y_off[i]);
+    const bool nan = npu->inject && injected_nan();
+    const int64_t rows = on_device ? T : chunk_rows(T);
+    const int nch = (int) ((T + rows - 1) / rows);
+    // Host buffers: results that hold bf16 values cross PCIe as bf16 and are
+    // widened on the host, chunk by chunk as their copies land.
+    size_t y16_total = 0;
+    for (int i = 0; i < n; i++) {
+        cs.w16[i] = !on_device && wire16(w[i]->mode);
+        if (cs.w16[i]) {
+            cs.y16_off[i] = y16_total;
+            y16_total += (size_t) (T * w[i]->n_out);
+        }
+    }
+    if (y16_total) {
+        if (!grow((void **) &cs.y16_dev, &cs.y16_cap, y16_total * 2) ||
+            !grow_pinned((void **) &cs.y16_host, &cs.y16_host_cap, y16_total * 2))
+            return set_error((std::string(what) + ": out of memory for the bf16 copies of the results").c_str());
+        if (!npu->pool) npu->pool.reset(new host_pool(host_threads()));
+    }
+    cudaEventRecord(cs.start, st);
+    cudaMemsetAsync(cs.err_dev, 0, sizeof(unsigned), st);
+    int rc = 0;
+    for (int c = 0; c < nch && !rc; c++) {
+        const int64_t r0 = c * rows, m = std::min(rows, T - r0);
+        if (!on_device) {
+            cudaMemcpyAsync(cs.x_dev + r0 * K, x + r0 * K, (size_t) (m * K) * 4, cudaMemcpyHostToDevice, npu->st_in);
+            cudaEventRecord(cs.in_ev[c], npu->st_in);
+            cudaStreamWaitEvent(st, cs.in_ev[c], 0);
+        }
+        cudaEventRecord(cs.t_pack[c], st);
+        rc = launch_pack_activations(xd + r0 * K, m, K, K, (m + TILE_M - 1) / TILE_M * TILE_M, nullptr,
+                                     npu->a_bf16 + r0 * K, K, st);
+        cudaEventRecord(cs.t_gemm[c], st);
+        gemm_seg segs[4];
+        for (int i = 0; i < n; i++)
+            segs[i] = { w[i]->bf16, K, w[i]->n_pad, w[i]->n_out, w[i]->n_out, w[i]->mode, yd[i] + r0 * w[i]->n_out };
+        if (!rc) rc = launch_gemm_group(npu->a_bf16 + r0 * K, K, m, K, n, segs, cs.err_dev, st);
+        if (!rc && nan) {
+            for (int i = 0; i < n; i++) {
+                cudaMemsetAsync(segs[i].c, 0xff, (size_t) (m * w[i]->n_out) * 4, st);
+                check_finite_kernel<<<148, 256, 0, st>>>(segs[i].c, m * w[i]->n_out, cs.err_dev);
+            }
+        }
+        if (!rc)
+            for (int i = 0; i < n; i++)
+                if (cs.w16[i])
+                    narrow_bf16_kernel<<<148, 256, 0, st>>>(segs[i].c, m * w[i]->n_out,
+                                                             cs.y16_dev + cs.y16_off[i] + r0 * w[i]->n_out);
+        cudaEventRecord(cs.t_end[c], st);
+        if (!on_device) {
+            cudaEventRecord(cs.done_ev[c], st);
+            cudaStreamWaitEvent(npu->st_out, cs.done_ev[c], 0);
+            for (int i = 0; i < n; i++) {
+                const size_t at = cs.y16_off[i] + (size_t) (r0 * w[i]->n_out), cnt = (size_t) (m * w[i]->n_out);
+                if (cs.w16[i])
+                    cudaMemcpyAsync(cs.y16_host + at, cs.y16_dev + at, cnt * 2, cudaMemcpyDeviceToHost, npu->st_out);
+                else
+                    cudaMemcpyAsync(y[i] + r0 * w[i]->n_out, segs[i].c, cnt * 4, cudaMemcpyDeviceToHost, npu->st_out);
+            }
+            cudaEventRecord(cs.copied_ev[c], npu->st_out);
+        }
+    }
+    cudaMemcpyAsync(cs.err_host, cs.err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
+    cudaEventRecord(cs.k_done, st);
+    cudaEventRecord(cs.o_done, on_device ? st : npu->st_out);
+    if (rc) {
+        cudaStreamSynchronize(st);
+        cudaStreamSynchronize(npu->st_in);
+        cudaStreamSynchronize(npu->st_out);
+        return rc;
+    }
+    cs.busy = true;
+    cs.on_device = on_device != 0;
+    cs.n = n;
+    cs.nch = nch;
+    cs.T = T;
+    cs.rows = rows;
+    for (int i = 0; i < n; i++) {
+        cs.n_out[i] = w[i]->n_out;
+        cs.y[i] = y[i];
+    }
+    return 0;
+}
+
+// Finishes the call queued in `cs`: widens its bf16 results into the
+// caller's f32 rows as each chunk's copy lands, waits for its kernels and
+// copies, and reads its error word. The call's results are then in y.
+static int finish_call(zest_npu *npu, call_slot &cs, const char *what) {
+    cs.busy = false;
+    if (cs.n == 0) return 0;
+    if (cudaSetDevice(npu->device) != cudaSuccess) return set_error((std::string(what) + ": cannot select the device").c_str());
+    int rc = 0;
+    bool any16 = false;
+    for (int i = 0; i < cs.n; i++) any16 = any16 || cs.w16[i];
+    for (int c = 0; c < cs.nch && any16 && !rc; c++) {
+        const cudaError_t ce = cudaEventSynchronize(cs.copied_ev[c]);
+        if (ce != cudaSuccess) {
+            rc = cuda_fail(what, ce);
+            break;
+        }
+        const int64_t r0 = c * cs.rows, m = std::min(cs.rows, cs.T - r0);
+        for (int i = 0; i < cs.n; i++) {
+            if (!cs.w16[i]) continue;
+            const uint16_t *src = cs.y16_host + cs.y16_off[i] + r0 * cs.n_out[i];
+            float *dst = cs.y[i] + r0 * cs.n_out[i];
+            npu->pool->run(m * cs.n_out[i], 1 << 16,
+                           [src, dst](int64_t lo, int64_t hi) { widen_bf16(src + lo, dst + lo, hi - lo); });
+        }
+    }
+    cudaError_t e = cudaEventSynchronize(cs.k_done);
+    if (e == cudaSuccess) e = cudaEventSynchronize(cs.o_done);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail(what, e);
+    float total = 0, busy = 0;
+    cudaEventElapsedTime(&total, cs.start, cs.o_done);
+    for (int c = 0; c < cs.nch; c++) {
+        float a = 0, b = 0;
+        cudaEventElapsedTime(&a, cs.t_pack[c], cs.t_gemm[c]);
+        cudaEventElapsedTime(&b, cs.t_gemm[c], cs.t_end[c]);
+        npu->times.encode_ms += a;
+        npu->times.gemm_ms += b;
+        busy += a + b;
+    }
+    npu->times.copy_ms += std::max(0.0f, total - busy);  // the copies the kernels did not hide
+    npu->times.calls += cs.n;
+    if (*cs.err_host & ERR_TIMEOUT) return set_error("a GPU kernel's bounded wait ran out");
+    if (*cs.err_host & ERR_NOT_FINITE) return set_error("the GPU's results held NaN or infinity");
+    return 0;
+}
+
 }  // namespace zest
 
 extern "C" {
@@ -454,17 +667,8 @@ zest_npu *zest_open(int device) {
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&npu->st_load, cudaStreamNonBlocking);
     for (cudaEvent_t &ev : npu->ev)
         if (e == cudaSuccess) e = cudaEventCreate(&ev);
-    for (int c = 0; c < zest_npu::MAX_CHUNKS && e == cudaSuccess; c++) {
-        e = cudaEventCreateWithFlags(&npu->in_ev[c], cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&npu->done_ev[c], cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&npu->copied_ev[c], cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreate(&npu->t_pack[c]);
-        if (e == cudaSuccess) e = cudaEventCreate(&npu->t_gemm[c]);
-        if (e == cudaSuccess) e = cudaEventCreate(&npu->t_end[c]);
-    }
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&npu->out_ev, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaMalloc(&npu->err_dev, sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMallocHost(&npu->err_host, sizeof(unsigned));
+    for (call_slot &cs : npu->slots)
+        if (e == cudaSuccess) e = cs.create();
     if (e != cudaSuccess) {
         cuda_fail("zest_open", e);
         delete npu;
@@ -544,146 +748,26 @@ void *zest_stream(zest_npu *npu) { return npu ? (void *) npu->st : nullptr; }
 
 int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *fused, const float *x, int64_t T,
                        float *const *y, int on_device) {
-    if (!npu || !keys || n <= 0 || n > 4) return set_error("zest_mul_mat: no service, or not 1 to 4 weights");
-    const zest_npu::weight *w[4];
-    for (int i = 0; i < n; i++) {
-        w[i] = npu->find(&keys[i], fused ? fused[i] : 0);
-        if (!w[i]) return set_error("zest_mul_mat: weight not added");
-        if (w[i]->K != w[0]->K) return set_error("zest_mul_mat: a group's weights differ in K");
-    }
-    if (T <= 0) return 0;
-    if (cudaSetDevice(npu->device) != cudaSuccess) return set_error("zest_mul_mat: cannot select the device");
-    if (npu->inject && injected_failure()) return set_error("an injected failure (GGML_XDNA_FAIL_AFTER)");
-    for (int i = 0; i < n; i++)
-        if (w[i]->ready) cudaStreamWaitEvent(npu->st, w[i]->ready, 0);  // its copy is built (load stream)
-    const int64_t K = w[0]->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
-    const size_t x_bytes = (size_t) (T * K) * 4;
-    size_t y_off[4], y_total = 0;
-    for (int i = 0; i < n; i++) {
-        y_off[i] = y_total;
-        y_total += (size_t) (T * w[i]->n_out) * 4;
-    }
-    if (!grow((void **) &npu->a_bf16, &npu->a_cap, (size_t) (m_pad * K) * 2) ||
-        (!on_device && (!grow((void **) &npu->x_dev, &npu->x_cap, x_bytes) ||
-                        !grow((void **) &npu->y_dev, &npu->y_cap, y_total))))
-        return set_error("zest_mul_mat: out of GPU memory for the call's buffers");
-    cudaStream_t st = npu->st;
-    const float *xd = on_device ? x : npu->x_dev;
-    float *yd[4];
-    for (int i = 0; i < n; i++) yd[i] = on_device ? y[i] : (float *) ((char *) npu->y_dev + y_off[i]);
-    const bool nan = npu->inject && injected_nan();
-    // Device buffers: one chunk. Host buffers: row chunks (multiples of the
-    // 128-row tile) whose copies in and out overlap the other chunks' kernels.
-    const int64_t rows = on_device ? T : chunk_rows(T);
-    const int nch = (int) ((T + rows - 1) / rows);
-    // Host buffers: results that hold bf16 values cross PCIe as bf16 and are
-    // widened on the host, chunk by chunk as their copies land.
-    bool w16[4] = {};
-    size_t y16_off[4] = {}, y16_total = 0;
-    for (int i = 0; i < n; i++) {
-        w16[i] = !on_device && wire16(w[i]->mode);
-        if (w16[i]) {
-            y16_off[i] = y16_total;
-            y16_total += (size_t) (T * w[i]->n_out);
-        }
-    }
-    if (y16_total) {
-        if (!grow((void **) &npu->y16_dev, &npu->y16_cap, y16_total * 2) ||
-            !grow_pinned((void **) &npu->y16_host, &npu->y16_host_cap, y16_total * 2))
-            return set_error("zest_mul_mat: out of memory for the bf16 copies of the results");
-        if (!npu->pool) npu->pool.reset(new host_pool(host_threads()));
-    }
-    cudaEventRecord(npu->ev[0], st);
-    cudaMemsetAsync(npu->err_dev, 0, sizeof(unsigned), st);
-    cudaStreamWaitEvent(npu->st_in, npu->ev[0], 0);
-    cudaStreamWaitEvent(npu->st_out, npu->ev[0], 0);
-    int rc = 0;
-    for (int c = 0; c < nch && !rc; c++) {
-        const int64_t r0 = c * rows, m = std::min(rows, T - r0);
-        if (!on_device) {
-            cudaMemcpyAsync(npu->x_dev + r0 * K, x + r0 * K, (size_t) (m * K) * 4, cudaMemcpyHostToDevice,
-                            npu->st_in);
-            cudaEventRecord(npu->in_ev[c], npu->st_in);
-            cudaStreamWaitEvent(st, npu->in_ev[c], 0);
-        }
-        cudaEventRecord(npu->t_pack[c], st);
-        rc = launch_pack_activations(xd + r0 * K, m, K, K, (m + TILE_M - 1) / TILE_M * TILE_M, nullptr,
-                                     npu->a_bf16 + r0 * K, K, st);
-        cudaEventRecord(npu->t_gemm[c], st);
-        gemm_seg segs[4];
-        for (int i = 0; i < n; i++)
-            segs[i] = { w[i]->bf16, K, w[i]->n_pad, w[i]->n_out, w[i]->n_out, w[i]->mode, yd[i] + r0 * w[i]->n_out };
-        if (!rc) rc = launch_gemm_group(npu->a_bf16 + r0 * K, K, m, K, n, segs, npu->err_dev, st);
-        if (!rc && nan) {
-            for (int i = 0; i < n; i++) {
-                cudaMemsetAsync(segs[i].c, 0xff, (size_t) (m * w[i]->n_out) * 4, st);
-                check_finite_kernel<<<148, 256, 0, st>>>(segs[i].c, m * w[i]->n_out, npu->err_dev);
-            }
-        }
-        if (!rc)
-            for (int i = 0; i < n; i++)
-                if (w16[i])
-                    narrow_bf16_kernel<<<148, 256, 0, st>>>(segs[i].c, m * w[i]->n_out,
-                                                             npu->y16_dev + y16_off[i] + r0 * w[i]->n_out);
-        cudaEventRecord(npu->t_end[c], st);
-        if (!on_device) {
-            cudaEventRecord(npu->done_ev[c], st);
-            cudaStreamWaitEvent(npu->st_out, npu->done_ev[c], 0);
-            for (int i = 0; i < n; i++) {
-                const size_t at = y16_off[i] + (size_t) (r0 * w[i]->n_out), cnt = (size_t) (m * w[i]->n_out);
-                if (w16[i])
-                    cudaMemcpyAsync(npu->y16_host + at, npu->y16_dev + at, cnt * 2, cudaMemcpyDeviceToHost,
-                                    npu->st_out);
-                else
-                    cudaMemcpyAsync(y[i] + r0 * w[i]->n_out, segs[i].c, cnt * 4, cudaMemcpyDeviceToHost,
-                                    npu->st_out);
-            }
-            cudaEventRecord(npu->copied_ev[c], npu->st_out);
-        }
-    }
-    // the bf16 results widened into the caller's f32 buffers as each chunk's
-    // copy lands (the later chunks' copies continue meanwhile)
-    for (int c = 0; c < nch && y16_total && !rc; c++) {
-        const cudaError_t ce = cudaEventSynchronize(npu->copied_ev[c]);
-        if (ce != cudaSuccess) {
-            rc = cuda_fail("zest_mul_mat", ce);
-            break;
-        }
-        const int64_t r0 = c * rows, m = std::min(rows, T - r0);
-        for (int i = 0; i < n; i++) {
-            if (!w16[i]) continue;
-            const uint16_t *src = npu->y16_host + y16_off[i] + r0 * w[i]->n_out;
-            float *dst = y[i] + r0 * w[i]->n_out;
-            npu->pool->run(m * w[i]->n_out, 1 << 16,
-                           [src, dst](int64_t lo, int64_t hi) { widen_bf16(src + lo, dst + lo, hi - lo); });
-        }
-    }
-    cudaMemcpyAsync(npu->err_host, npu->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
-    cudaEventRecord(npu->out_ev, npu->st_out);
-    cudaStreamWaitEvent(st, npu->out_ev, 0);
-    cudaEventRecord(npu->ev[4], st);
-    const cudaError_t e = cudaStreamSynchronize(st);
-    if (rc) {
-        cudaStreamSynchronize(npu->st_in);
-        cudaStreamSynchronize(npu->st_out);
-        return rc;
-    }
-    if (e != cudaSuccess) return cuda_fail("zest_mul_mat", e);
-    float total = 0, busy = 0;
-    cudaEventElapsedTime(&total, npu->ev[0], npu->ev[4]);
-    for (int c = 0; c < nch; c++) {
-        float a = 0, b = 0;
-        cudaEventElapsedTime(&a, npu->t_pack[c], npu->t_gemm[c]);
-        cudaEventElapsedTime(&b, npu->t_gemm[c], npu->t_end[c]);
-        npu->times.encode_ms += a;
-        npu->times.gemm_ms += b;
-        busy += a + b;
-    }
-    npu->times.copy_ms += std::max(0.0f, total - busy);  // the copies the kernels did not hide
-    npu->times.calls += n;
-    if (*npu->err_host & ERR_TIMEOUT) return set_error("a GPU kernel's bounded wait ran out");
-    if (*npu->err_host & ERR_NOT_FINITE) return set_error("the GPU's results held NaN or infinity");
-    return 0;
+    if (!npu) return set_error("zest_mul_mat: no service, or not 1 to 4 weights");
+    int rc = submit_call(npu, npu->slots[0], n, keys, fused, x, T, y, on_device, "zest_mul_mat");
+    return rc ? rc : finish_call(npu, npu->slots[0], "zest_mul_mat");
+}
+
+int zest_submit_group(zest_npu *npu, int slot, int n, const zest_wkey *keys, const int *fused, const float *x,
+                      int64_t T, float *const *y, int on_device) {
+    if (!npu) return set_error("zest_submit_group: no service");
+    if (slot < 0 || slot >= ZEST_SLOTS) return set_error("zest_submit_group: no such slot");
+    call_slot &cs = npu->slots[1 + slot];
+    if (cs.busy) return set_error("zest_submit_group: the slot's last call is not finished (zest_wait_group)");
+    return submit_call(npu, cs, n, keys, fused, x, T, y, on_device, "zest_submit_group");
+}
+
+int zest_wait_group(zest_npu *npu, int slot) {
+    if (!npu) return set_error("zest_wait_group: no service");
+    if (slot < 0 || slot >= ZEST_SLOTS) return set_error("zest_wait_group: no such slot");
+    call_slot &cs = npu->slots[1 + slot];
+    if (!cs.busy) return set_error("zest_wait_group: nothing submitted in the slot");
+    return finish_call(npu, cs, "zest_wait_group");
 }
 
 int zest_mul_mat_group_ex(zest_npu *npu, int n, const zest_wkey *keys, const int *fused, const float *x,
@@ -704,9 +788,10 @@ int zest_mul_mat_group_ex(zest_npu *npu, int n, const zest_wkey *keys, const int
         if (w[i]->ready) cudaStreamWaitEvent(npu->st, w[i]->ready, 0);  // its copy is built (load stream)
     const int64_t K = w[0]->K, m_pad = (T + TILE_M - 1) / TILE_M * TILE_M;
     cudaStream_t st = npu->st;
+    call_slot &cs = npu->slots[0];
     const bool nan = npu->inject && injected_nan();
-    cudaEventRecord(npu->t_pack[0], st);
-    cudaMemsetAsync(npu->err_dev, 0, sizeof(unsigned), st);
+    cudaEventRecord(cs.t_pack[0], st);
+    cudaMemsetAsync(cs.err_dev, 0, sizeof(unsigned), st);
     int rc = 0;
     const uint16_t *a = a_bf16;
     if (!a) {
@@ -716,7 +801,7 @@ int zest_mul_mat_group_ex(zest_npu *npu, int n, const zest_wkey *keys, const int
                               : launch_pack_activations(x, T, K, K, m_pad, nullptr, npu->a_bf16, K, st);
         a = npu->a_bf16;
     }
-    cudaEventRecord(npu->t_gemm[0], st);
+    cudaEventRecord(cs.t_gemm[0], st);
     gemm_seg segs[4];
     for (int i = 0; i < n; i++) {
         segs[i] = { w[i]->bf16, K, w[i]->n_pad, w[i]->n_out, w[i]->n_out, w[i]->mode, outs[i].y };
@@ -725,26 +810,26 @@ int zest_mul_mat_group_ex(zest_npu *npu, int n, const zest_wkey *keys, const int
         segs[i].a_next = outs[i].a_next;
         segs[i].lda_next = w[i]->n_out;
     }
-    if (!rc) rc = launch_gemm_group(a, K, T, K, n, segs, npu->err_dev, st);
+    if (!rc) rc = launch_gemm_group(a, K, T, K, n, segs, cs.err_dev, st);
     if (!rc && nan)
         for (int i = 0; i < n; i++)
             if (outs[i].y) {
                 cudaMemsetAsync(outs[i].y, 0xff, (size_t) (T * w[i]->n_out) * 4, st);
-                check_finite_kernel<<<148, 256, 0, st>>>(outs[i].y, T * w[i]->n_out, npu->err_dev);
+                check_finite_kernel<<<148, 256, 0, st>>>(outs[i].y, T * w[i]->n_out, cs.err_dev);
             }
-    cudaEventRecord(npu->t_end[0], st);
-    cudaMemcpyAsync(npu->err_host, npu->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
+    cudaEventRecord(cs.t_end[0], st);
+    cudaMemcpyAsync(cs.err_host, cs.err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
     const cudaError_t e = cudaStreamSynchronize(st);
     if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail("zest_mul_mat_group_ex", e);
     float pa = 0, gm = 0;
-    cudaEventElapsedTime(&pa, npu->t_pack[0], npu->t_gemm[0]);
-    cudaEventElapsedTime(&gm, npu->t_gemm[0], npu->t_end[0]);
+    cudaEventElapsedTime(&pa, cs.t_pack[0], cs.t_gemm[0]);
+    cudaEventElapsedTime(&gm, cs.t_gemm[0], cs.t_end[0]);
     npu->times.encode_ms += pa;
     npu->times.gemm_ms += gm;
     npu->times.calls += n;
-    if (*npu->err_host & ERR_TIMEOUT) return set_error("a GPU kernel's bounded wait ran out");
-    if (*npu->err_host & ERR_NOT_FINITE) return set_error("the GPU's results held NaN or infinity");
+    if (*cs.err_host & ERR_TIMEOUT) return set_error("a GPU kernel's bounded wait ran out");
+    if (*cs.err_host & ERR_NOT_FINITE) return set_error("the GPU's results held NaN or infinity");
     return 0;
 }
 

@@ -22,6 +22,7 @@ ERR_NOT_FINITE, ERR_TIMEOUT = 1, 2
 GLU_REGLU, GLU_GEGLU, GLU_SWIGLU, GLU_GEGLU_ERF, GLU_GEGLU_QUICK = 0, 1, 2, 4, 5
 ROPE_NORMAL, ROPE_NEOX = 0, 2
 BLOCK_BYTES = 9
+SLOTS = 4  # ZEST_SLOTS: group calls in flight at once (zest_submit_group)
 # (values per quant block, bytes per quant block)
 QUANT = {TYPE_F32: (1, 4), TYPE_F16: (1, 2), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144),
          TYPE_Q6_K: (256, 210), TYPE_IQ3_S: (256, 110)}
@@ -109,6 +110,8 @@ def lib() -> ctypes.CDLL:
         "zest_wait_weights": (_int, [_vp]),
         "zest_mul_mat": (_int, [_vp, ctypes.POINTER(WKey), _int, _vp, _i64, _vp, _int]),
         "zest_mul_mat_group": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, _i64, _vpp, _int]),
+        "zest_submit_group": (_int, [_vp, _int, _int, ctypes.POINTER(WKey), _intp, _vp, _i64, _vpp, _int]),
+        "zest_wait_group": (_int, [_vp, _int]),
         "zest_mul_mat_group_ex": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, ctypes.c_float, _vp, _vp, _vp,
                                          _i64, ctypes.POINTER(MmOut)]),
         "zest_stream": (_vp, [_vp]),
@@ -132,7 +135,8 @@ def exported_symbols() -> list[str]:
                         "zest_add_weight_values",
                         "zest_out_width", "zest_weight_bfp16", "zest_weight_bf16", "zest_set_load_async",
                         "zest_wait_weights", "zest_mul_mat",
-                        "zest_mul_mat_group", "zest_mul_mat_group_ex", "zest_stream", "zest_take_times")]
+                        "zest_mul_mat_group", "zest_submit_group", "zest_wait_group", "zest_mul_mat_group_ex",
+                        "zest_stream", "zest_take_times")]
 
 
 def _check(rc: int, what: str) -> None:
@@ -325,6 +329,18 @@ class Npu:
         _check(lib().zest_mul_mat_group(self.h, n, (WKey * n)(*keys), (_int * n)(*[int(f) for f in fused]),
                                         ctypes.c_void_p(x_ptr), T, (_vp * n)(*y_ptrs), int(on_device)),
                "zest_mul_mat_group")
+
+    def submit_group(self, slot: int, keys, x_ptr: int, T: int, y_ptrs, on_device: bool, fused=None):
+        """zest_mul_mat_group queued in `slot` (0 .. SLOTS-1); finish it with wait_group(slot).
+        The arrays behind x_ptr and y_ptrs must outlive the wait."""
+        n = len(keys)
+        fused = fused or [False] * n
+        _check(lib().zest_submit_group(self.h, slot, n, (WKey * n)(*keys), (_int * n)(*[int(f) for f in fused]),
+                                       ctypes.c_void_p(x_ptr), T, (_vp * n)(*y_ptrs), int(on_device)),
+               "zest_submit_group")
+
+    def wait_group(self, slot: int):
+        _check(lib().zest_wait_group(self.h, slot), "zest_wait_group")
 
     def mul_mat_group_ex(self, keys, outs, T: int, x_ptr: int = 0, a_ptr: int = 0, norm_eps: float = -1.0,
                          norm_w_ptr: int = 0, x_normed_ptr: int = 0, fused=None):

@@ -342,6 +342,24 @@ int zest_mul_mat(zest_npu *npu, const zest_wkey *key, int fused, const float *x,
 int zest_mul_mat_group(zest_npu *npu, int n, const zest_wkey *keys, const int *fused, const float *x, int64_t T,
                        float *const *y, int on_device);
 
+/* Group calls in flight at once: zest_submit_group queues the call
+ * zest_mul_mat_group makes, in slot `slot` (0 .. ZEST_SLOTS-1), and returns
+ * without waiting; zest_wait_group(slot) finishes it (host buffers: widens
+ * the bf16 results into y as their copies land) and returns its status, the
+ * results then in y. The calls of all slots queue on the service's streams in
+ * submission order, so with host buffers one call's copy in overlaps another's
+ * copy out and the host's widening: PCIe's two directions are busy at once.
+ * x and y must stay valid, and x unchanged, until the wait returns; a slot
+ * takes its next call only after its wait. One thread at a time calls into a
+ * service; wait for every submitted call before zest_close.
+ * Replaces: xdna_npu::reserve / begin / encode_row / submit / wait /
+ * decode_row with one group in flight per stream (src/xdna-npu.h:79-101),
+ * as xdna_exec_piece runs several streams in turn (src/xdna-exec.cpp:589-640). */
+#define ZEST_SLOTS 4
+int zest_submit_group(zest_npu *npu, int slot, int n, const zest_wkey *keys, const int *fused, const float *x,
+                      int64_t T, float *const *y, int on_device);
+int zest_wait_group(zest_npu *npu, int slot);
+
 /* Where one weight's result of zest_mul_mat_group_ex goes. */
 typedef struct {
     float *y;               /* [T][out_width]; may be NULL for a fused gate/up weight that gives a_next */

@@ -106,4 +106,6 @@ def test_service_refuses_without_a_service():
     refused(L.zest_mul_mat(None, None, 0, None, 10, None, 1), "no service or key")
     refused(L.zest_mul_mat_group(None, 1, ctypes.byref(key), None, None, 10, None, 1), "not 1 to 4")
     refused(L.zest_take_times(None, None), "no service")
+    refused(L.zest_submit_group(None, 0, 1, ctypes.byref(key), None, None, 10, None, 0), "no service")
+    refused(L.zest_wait_group(None, 0), "no service")
     refused(L.zest_load_iq3s_grid(None), "no table")

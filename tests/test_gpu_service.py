@@ -285,3 +285,67 @@ def test_async_weight_copies_equal_synchronous_ones():
         npu.close()
     for a, b in zip(outs["async"], outs["sync"]):
         assert np.array_equal(a, b)
+
+
+def test_submitted_groups_equal_synchronous_calls():
+    # group calls in flight in every slot at once (their copies in and out
+    # overlapping on PCIe), then each slot reused after its wait: the same
+    # results, bit for bit, as the same calls made one at a time
+    npu = Z.Npu(0)  # bf16-rounded results: they cross PCIe as bf16
+    K, T, F = 512, 2600, 300  # 512-row chunks, the last one ragged
+    Ns = (768, 256, 512)
+    raws = [O.quantize(O.Q8_0, O.weights_f32(N, K, 100 + N)) for N in Ns]
+    keys = [Z.Npu.key(r.ctypes.data, O.Q8_0, K, N) for r, N in zip(raws, Ns)]
+    for k, r in zip(keys, raws):
+        npu.add_weight(k, r.ctypes.data, on_device=False)
+    g, u = (O.quantize(O.Q4_K, O.weights_f32(F, K, s)) for s in (110, 111))
+    gkey = Z.Npu.key(g.ctypes.data, O.Q4_K, K, F)
+    npu.add_fused(gkey, g.ctypes.data, u.ctypes.data, on_device=False)
+    # (keys, fused, widths, input seed, pinned): five groups on four slots
+    groups = [([keys[0], keys[1]], [False, False], [768, 256], 120, True),
+              ([gkey], [True], [F], 121, True),
+              ([keys[2]], [False], [512], 122, False),
+              ([keys[0], gkey, keys[2]], [False, True, False], [768, F, 512], 123, True),
+              ([keys[1]], [False], [256], 124, True)]
+
+    def buffers(pinned, seed, widths):
+        x = torch.from_numpy(O.activations(T, K, seed))
+        ys = [torch.full((T, w), float("nan"), dtype=torch.float32) for w in widths]
+        if pinned:
+            x, ys = x.pin_memory(), [y.pin_memory() for y in ys]
+        return x, ys
+
+    want = []
+    for ks, fu, widths, seed, pinned in groups:
+        x, ys = buffers(pinned, seed, widths)
+        npu.mul_mat_group(ks, x.data_ptr(), T, [y.data_ptr() for y in ys], False, fu)
+        want.append([y.numpy().copy() for y in ys])
+    bufs = [buffers(p, s, w) for _, _, w, s, p in groups]
+    for rnd in range(2):  # twice: every slot takes a second call after its wait
+        for y in (y for _, ys in bufs for y in ys):
+            y.fill_(float("nan"))
+        slot_of = {}
+        for i, (ks, fu, _, _, _) in enumerate(groups):
+            slot = i % Z.SLOTS
+            if any(s == slot for s in slot_of.values()):
+                j = next(j for j, s in slot_of.items() if s == slot)
+                npu.wait_group(slot)
+                del slot_of[j]
+            x, ys = bufs[i]
+            npu.submit_group(slot, ks, x.data_ptr(), T, [y.data_ptr() for y in ys], False, fu)
+            slot_of[i] = slot
+        for i, slot in slot_of.items():
+            npu.wait_group(slot)
+        for i in range(len(groups)):
+            for got, exp in zip(bufs[i][1], want[i]):
+                assert np.array_equal(got.numpy().view(np.uint32), exp.view(np.uint32)), (rnd, i)
+    x, ys = bufs[0]
+    with pytest.raises(Z.ZestError, match="nothing submitted"):
+        npu.wait_group(0)
+    npu.submit_group(0, groups[0][0], x.data_ptr(), T, [y.data_ptr() for y in ys], False, groups[0][1])
+    with pytest.raises(Z.ZestError, match="not finished"):
+        npu.submit_group(0, groups[0][0], x.data_ptr(), T, [y.data_ptr() for y in ys], False, groups[0][1])
+    npu.wait_group(0)
+    with pytest.raises(Z.ZestError, match="no such slot"):
+        npu.wait_group(Z.SLOTS)
+    npu.close()
