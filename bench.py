@@ -375,8 +375,9 @@ def layer_config(w: dict, workload: str, world: int, mode) -> dict:
         par = "1 GPU" if world == 1 else f"tokens{world} (each GPU its own {M}-token chunk, no collective)"
     elif mode == "nshard":
         par = (f"n-shard{world}: every GPU a slab of each weight's rows (whole 128-row granules), the output "
-               "slabs all-gathered over NCCL as bf16 (exact: the results are bf16-rounded) into ggml's "
-               "row-major f32 [M][N] on every GPU, each gather overlapping the next launch")
+               "slabs all-gathered into ggml's row-major f32 [M][N] on every GPU: by the GEMM epilogue through "
+               "an NVLink multicast address as the tiles finish, or over NCCL (bf16 on the wire) where a GPU "
+               "has no multicast (the line's 'gather' says which)")
     else:
         par = f"n-shard{world}, no gather: every GPU a slab of each weight's rows, the output slabs left in place"
     wbytes = sum((slab_width(N, world) if nshard else N) * K * 2 for _, N, K, _ in w["proj"])
@@ -393,11 +394,17 @@ class LayerStep:
     input one K2 pack, then one grouped K3 launch per input (q+k+v, o,
     gate+up, down), weights converted beforehand (K1) as the reference
     converts them at load. nshard: this rank's N-slab of every weight; with
-    gather, each launch's output slabs all-gathered (bf16 on the wire) on a
+    gather, every rank gets the whole [M][N] output of every weight: by
+    default each launch's epilogue stores its slab's tiles through an NVLink
+    multicast address into every rank's copy (multimem.st; the NVSwitch does
+    the all-gather as the tiles finish, and a one-float all-reduce ends the
+    step as the group's fence), else (gather_how "nccl", or no multicast on
+    some rank) the slabs are all-gathered over NCCL, bf16 on the wire, on a
     side stream while the next launch runs."""
 
-    def __init__(self, w: dict, raws: dict, world: int, rank: int, nshard: bool, gather: bool, Z, torch):
-        from zest_b200.shard import shard_rows, slab_width
+    def __init__(self, w: dict, raws: dict, world: int, rank: int, nshard: bool, gather: bool, Z, torch,
+                 gather_how: str = "multicast"):
+        from zest_b200.shard import any_rank, shard_rows, slab_width
         self.w, self.world, self.nshard, self.gather, self.Z, self.torch = w, world, nshard, gather, Z, torch
         M, qt = w["M"], w["qtype"]
         self.bh, self.slabs = {}, {}
@@ -424,6 +431,26 @@ class LayerStep:
                     for name, *_ in w["proj"]}
         self.full = {name: torch.empty((M, N), dtype=torch.float32, device="cuda")
                      for name, N, _, _ in w["proj"]} if gather else {}
+        # the whole outputs in symmetric memory: bound to an NVLink multicast
+        # object (multicast), or reached through every peer's pointer (peer)
+        self.mc, self.mc_why, self.how = {}, None, gather_how if gather else "none"
+        if gather and gather_how in ("multicast", "peer"):
+            import torch.distributed as dist
+            try:
+                import torch.distributed._symmetric_memory as symm_mem
+                for name, N, _, _ in w["proj"]:
+                    t = symm_mem.empty((M, N), dtype=torch.float32, device="cuda")
+                    hdl = symm_mem.rendezvous(t, dist.group.WORLD)
+                    if gather_how == "multicast" and not hdl.multicast_ptr:
+                        raise RuntimeError("no multicast support")
+                    self.mc[name] = (t, hdl, int(hdl.multicast_ptr or 0), [int(p) for p in hdl.buffer_ptrs])
+            except Exception as e:  # every rank falls back to NCCL below
+                self.mc, self.mc_why = {}, f"{type(e).__name__}: {e}"
+            if any_rank(not self.mc):
+                self.mc_why = self.mc_why or "symmetric memory unavailable on another rank"
+                self.mc = {}
+                self.how = "nccl"
+            self.tick = torch.zeros(1, device="cuda")
         self.err = torch.zeros(1, dtype=torch.int32, device="cuda")
         self.stream = torch.cuda.current_stream()
         self.comm = torch.cuda.Stream() if gather else None
@@ -439,6 +466,57 @@ class LayerStep:
                                (ctypes.c_void_p * n)(*[self.out[nm].data_ptr() for nm, _, _ in members]),
                                (ctypes.c_int64 * n)(*[self.out[nm].shape[1] for nm, _, _ in members]), members))
         self.launches = len(self.kinds) + len(self.groups)
+        # multicast gather: each group's segments write their slab into every rank's whole output
+        self.msegs, self.peer_arrays = [], []
+        if self.mc:
+            for kind, members in self.groups:
+                segs = []
+                for nm, _, K in members:
+                    t, _, mcp, ptrs = self.mc[nm]
+                    N, off = t.shape[1], 4 * self.slabs[nm][0]
+                    if self.how == "multicast":
+                        segs.append(Z.GemmSeg(self.bh[nm].data_ptr(), K, self.slabs[nm][1], Z.MODE_BF16, None, N,
+                                              None, 0, None, 0, mcp + off, 1))
+                    else:
+                        peers = (ctypes.c_void_p * (world - 1))(*[ptrs[j] + off for j in range(world) if j != rank])
+                        self.peer_arrays.append(peers)
+                        segs.append(Z.GemmSeg(self.bh[nm].data_ptr(), K, self.slabs[nm][1], Z.MODE_BF16,
+                                              t.data_ptr() + off, N, None, 0, None, 0, None, 0,
+                                              ctypes.cast(peers, ctypes.POINTER(ctypes.c_void_p)), world - 1))
+                self.msegs.append((Z.GemmSeg * len(segs))(*segs))
+
+    def gather_desc(self) -> str:
+        if not self.gather:
+            return "none"
+        if self.mc and self.how == "multicast":
+            return "multimem.st of each launch's tiles into every rank's whole output (NVLink multicast)"
+        if self.mc:
+            return "TMA stores of each launch's tiles into every rank's whole output (peer pointers over NVLink)"
+        return "NCCL all-gather of the slabs, bf16 on the wire" + (f" (multicast: {self.mc_why})" if self.mc_why else "")
+
+    def check_multicast(self) -> float:
+        """The multicast outputs against the NCCL all-gather of the same slabs
+        computed into local buffers: the largest difference over this rank's
+        outputs (0 when they agree bit for bit). Collective."""
+        import torch.distributed as dist
+        from zest_b200.shard import gather_slabs
+        torch, Z, L = self.torch, self.Z, self.Z.lib()
+        self.step()
+        dist.all_reduce(self.tick)
+        torch.cuda.synchronize()
+        M = self.w["M"]
+        worst = 0.0
+        for i, (kind, bp, ldb, ns, modes, cp, ldc, members) in enumerate(self.gargs):
+            K = self.kinds[kind]
+            rc = L.zest_gemm_group(ctypes.c_void_p(self.ah[kind].data_ptr()), K, M, K, len(members), bp, ldb, ns,
+                                   modes, cp, ldc, ctypes.c_void_p(self.err.data_ptr()), self.sp)
+            if rc:
+                raise Z.ZestError(L.zest_last_error().decode())
+            for name, N, _ in members:
+                ref = torch.empty((M, N), dtype=torch.float32, device="cuda")
+                gather_slabs(self.out[name], ref, self.world, N)
+                worst = max(worst, float((ref - self.mc[name][0]).abs().max().item()))
+        return worst
 
     def step(self, events=None):
         from zest_b200.shard import gather_slabs
@@ -453,19 +531,26 @@ class LayerStep:
             K = self.kinds[kind]
             if events is not None:
                 events[i][0].record(self.stream)
-            rc = L.zest_gemm_group(ctypes.c_void_p(self.ah[kind].data_ptr()), K, M, K, len(members), bp, ldb, ns,
-                                   modes, cp, ldc, ctypes.c_void_p(self.err.data_ptr()), self.sp)
+            if self.mc:
+                rc = L.zest_gemm_segs(ctypes.c_void_p(self.ah[kind].data_ptr()), K, M, K, len(members), self.msegs[i],
+                                      ctypes.c_void_p(self.err.data_ptr()), self.sp)
+            else:
+                rc = L.zest_gemm_group(ctypes.c_void_p(self.ah[kind].data_ptr()), K, M, K, len(members), bp, ldb,
+                                       ns, modes, cp, ldc, ctypes.c_void_p(self.err.data_ptr()), self.sp)
             if events is not None:
                 events[i][1].record(self.stream)
             if rc:
                 raise Z.ZestError(L.zest_last_error().decode())
-            if self.gather:
+            if self.gather and not self.mc:
                 # the gather of this launch's slabs overlaps the next launch
                 self.comm.wait_stream(self.stream)
                 with torch.cuda.stream(self.comm):
                     for name, N, _ in members:
                         gather_slabs(self.out[name], self.full[name], self.world, N, wire=torch.bfloat16)
-        if self.gather:
+        if self.mc:
+            import torch.distributed as dist
+            dist.all_reduce(self.tick)  # every rank's tiles are in every copy before the step ends
+        elif self.gather:
             self.stream.wait_stream(self.comm)
 
     def timed(self, steps: int, warmup: int, local: int, clocked: bool = True):
@@ -531,11 +616,17 @@ def run_ours(args, w: dict) -> None:
     gather = nshard and mode == "nshard"
     raws = {name: weight_raw(qt, name, N, K, threads) for name, N, K, _ in w["proj"]}
 
-    layer = LayerStep(w, raws, world, rank, nshard, gather, Z, torch)
+    layer = LayerStep(w, raws, world, rank, nshard, gather, Z, torch, args.gather)
     ms, gemm_ms, clocks = layer.timed(args.steps, args.warmup, local)
     ms_max = max_over_ranks(ms, world, torch)
     groups, slabs = layer.groups, layer.slabs
     launches = layer.launches
+    gather_desc = layer.gather_desc()
+    if layer.mc:
+        from zest_b200.shard import any_rank
+        worst = layer.check_multicast()
+        if any_rank(not worst == 0.0):
+            raise Z.ZestError(f"multicast gather differs from NCCL's by {worst} (this rank)")
     del layer
     torch.cuda.empty_cache()
 
@@ -612,6 +703,8 @@ def run_ours(args, w: dict) -> None:
             "gpu_launches": args.steps * launches,
             "clocks": clocks,
         }
+        if nshard:
+            line["gather"] = gather_desc
         if tokens_leg:
             line["tokens_mode"] = tokens_leg
         if e2e:
@@ -1450,6 +1543,10 @@ def main() -> None:
                     help="N>1: N-slabs of every weight with (nshard, the default) or without the NCCL all-gather "
                          "of the output slabs, each GPU its own token chunk (tokens, no collective), or the layer "
                          "as one tensor-parallel block (tp: o/down K-sharded, one all-reduce per row chunk)")
+    ap.add_argument("--gather", choices=["peer", "multicast", "nccl"], default="peer",
+                    help="nshard: the output all-gather from the GEMM epilogue, by TMA stores into every peer's "
+                         "copy (default) or multimem.st through NVLink multicast, or by NCCL (also where a rank "
+                         "has no symmetric memory)")
     ap.add_argument("--tp-chunks", type=int, default=1, help="tp with NCCL: row chunks whose all-reduce overlaps the next")
     ap.add_argument("--tp-reduce", choices=["multicast", "nccl"], default="nccl",
                     help="tp: K-sharded partials summed by NCCL, or in the GEMM epilogue through NVLink multicast "

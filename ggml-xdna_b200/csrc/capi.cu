@@ -873,6 +873,9 @@ int zest_gemm_segs(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, in
         g[i].a_next = z.a_next;
         g[i].lda_next = z.lda_next;
         g[i].c_mc = z.c_multicast;
+        g[i].mc_store = z.multicast_store;
+        g[i].c_peers = z.c_peers;
+        g[i].n_peers = z.n_peers;
     }
     return launch_gemm_group(a_bf16, lda, M, K, n, g, err, (cudaStream_t) stream);
 }

@@ -83,6 +83,8 @@ struct gemm_params {
     uint16_t *a_next;    // SwiGLU: the result's bfp16-rounded bf16 copy, the next GEMM's A, or null
     int64_t lda_next;
     float *c_mc;         // or null: the results added (multimem.red) into a multicast buffer [M][ldc]
+    int mc_store;        // with c_mc: the results stored (multimem.st) into every copy instead
+    int n_peers;         // pair kernel with TMA stores: each tile also stored into this many peers' copies
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
@@ -210,12 +212,16 @@ __device__ __forceinline__ uint32_t store_chunk(const gemm_params &p, const uint
         if (col0 + 32 <= p.n_out && (p.ldc % 4) == 0 && ((uintptr_t) dst & 15) == 0) {
             bad |= any_not_finite(o);
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) multimem_red_add_v4(dst + i, o[i], o[i + 1], o[i + 2], o[i + 3]);
+            for (int i = 0; i < 32; i += 4) {
+                if (p.mc_store) multimem_st_v4(dst + i, o[i], o[i + 1], o[i + 2], o[i + 3]);
+                else multimem_red_add_v4(dst + i, o[i], o[i + 1], o[i + 2], o[i + 3]);
+            }
         } else {
 #pragma unroll
             for (int i = 0; i < 32; i++)
                 if (col0 + i < p.n_out) {
-                    multimem_red_add(dst + i, o[i]);
+                    if (p.mc_store) multimem_st(dst + i, o[i]);
+                    else multimem_red_add(dst + i, o[i]);
                     bad |= not_finite(o[i]);
                 }
         }
@@ -448,8 +454,13 @@ struct pair_cfg {
 // src/xdna-npu.cpp:476-531).
 constexpr int MAX_SEG = 4;
 
+// Up to MAX_PEERS other GPUs' copies of each output, stored into by the
+// epilogue's TMA beside the local one (an N-shard's all-gather).
+constexpr int MAX_PEERS = 7;
+
 struct pair_maps {
     CUtensorMap b[MAX_SEG], c[MAX_SEG];
+    CUtensorMap peer[MAX_SEG][MAX_PEERS];
 };
 
 struct pair_params {
@@ -867,11 +878,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         if (grow < p.M) {
                             float *dst = p.c_mc + grow * p.ldc + gcol;
                             if (gcol + 4 <= p.n_out && ((uintptr_t) dst & 15) == 0) {
-                                multimem_red_add_v4(dst, v.x, v.y, v.z, v.w);
+                                if (p.mc_store) multimem_st_v4(dst, v.x, v.y, v.z, v.w);
+                                else multimem_red_add_v4(dst, v.x, v.y, v.z, v.w);
                             } else {
                                 const float e[4] = { v.x, v.y, v.z, v.w };
                                 for (int i = 0; i < 4; i++)
-                                    if (gcol + i < p.n_out) multimem_red_add(dst + i, e[i]);
+                                    if (gcol + i < p.n_out) {
+                                        if (p.mc_store) multimem_st(dst + i, e[i]);
+                                        else multimem_red_add(dst + i, e[i]);
+                                    }
                             }
                         }
                     }
@@ -882,6 +897,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 __syncwarp();
                 if (lane == 0) {
                     tma_store_2d_hint(&maps.c[seg], buf, (int32_t) col0, (int32_t) row0, out_pol);
+                    for (int r = 0; r < p.n_peers; r++)
+                        tma_store_2d_hint(&maps.peer[seg][r], buf, (int32_t) col0, (int32_t) row0, out_pol);
                     bulk_commit_group();
                     stored = true;
                 }
@@ -906,7 +923,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (stored) bulk_wait_all();  // every store has landed before the block exits
         bool mc = false;
-        for (int sg = 0; sg < pp.nseg; sg++) mc = mc || pp.seg[sg].c_mc != nullptr;
+        for (int sg = 0; sg < pp.nseg; sg++) mc = mc || pp.seg[sg].c_mc != nullptr || pp.seg[sg].n_peers > 0;
+        if (mc) fence_proxy_async_global();  // the peers' copies: TMA's writes ordered before the fence below
         if (mc) asm volatile("fence.acq_rel.sys;" ::: "memory");  // the reductions are performed before we exit
         if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(pp.err, ERR_NOT_FINITE);
     }
@@ -1121,9 +1139,21 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
         p.a_next = g.a_next;
         p.lda_next = g.lda_next;
         p.c_mc = g.c_mc;
+        p.mc_store = g.mc_store;
         // TMA stores need 16-byte aligned rows; SwiGLU halves the width and keeps direct stores
         p.tma_store = g.mode != MODE_SWIGLU && g.c && g.ldc % 4 == 0 && ((uintptr_t) g.c & 15) == 0 &&
                       make_tmap_out(&maps.c[s], g.c, M, g.n_out, g.ldc);
+        p.n_peers = 0;
+        if (g.n_peers > 0) {
+            if (!p.tma_store || g.n_peers > MAX_PEERS || !g.c_peers)
+                return set_error("gemm: peer copies need a TMA-stored output (fp32 or bf16, 16-byte aligned rows) "
+                                 "and at most 7 peers");
+            for (int r = 0; r < g.n_peers; r++)
+                if (!g.c_peers[r] || ((uintptr_t) g.c_peers[r] & 15) ||
+                    !make_tmap_out(&maps.peer[s][r], g.c_peers[r], M, g.n_out, g.ldc))
+                    return set_error("gemm: cannot build the TMA descriptor of a peer's copy");
+            p.n_peers = g.n_peers;
+        }
         pp.tile0[s] = tiles_n;
         tiles_n += (int) ((g.N + BN_T - 1) / BN_T);
     }
@@ -1203,6 +1233,7 @@ int launch_single(const CUtensorMap &ta, int64_t M, int64_t K, const gemm_seg &g
     p.a_next = g.a_next;
     p.lda_next = g.lda_next;
     p.c_mc = g.c_mc;
+    p.mc_store = g.mc_store;
     p.num_m = (int) ((M + BM - 1) / BM);
     p.num_n = (int) ((g.N + BN - 1) / BN);
     p.num_k = (int) ((K + BK - 1) / BK);
@@ -1260,6 +1291,8 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
     CUtensorMap ta;
     if (!make_tmap(&ta, a_bf16, M, K, lda, BM)) return set_error("gemm: cannot build the TMA descriptors");
     if (!gp.pair) {
+        for (int s = 0; s < nseg; s++)
+            if (segs[s].n_peers > 0) return set_error("gemm: peer copies need more than 128 rows (the pair kernel)");
         for (int s = 0; s < nseg; s++)
             if (launch_single(ta, M, K, segs[s], err_flag, st)) return -1;
         return 0;

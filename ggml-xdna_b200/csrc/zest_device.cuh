@@ -301,6 +301,18 @@ __device__ __forceinline__ void multimem_red_add_v4(float *mc, float a, float b,
                  : "memory");
 }
 
+// Stores to the address in every GPU bound to the multicast object (the
+// NVSwitch replicates the write). Relaxed, system scope.
+__device__ __forceinline__ void multimem_st_v4(float *mc, float a, float b, float c, float d) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ void multimem_st(float *mc, float a) {
+    asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc), "f"(a) : "memory");
+}
+
 __device__ __forceinline__ void multimem_red_add(float *mc, float a) {
     asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(mc), "f"(a) : "memory");
 }
@@ -524,6 +536,12 @@ __device__ __forceinline__ void bulk_wait_read() {
 
 // Until every committed store group has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Orders this thread's async-proxy (TMA) and generic-proxy accesses to
+// global memory, e.g. completed TMA stores before a system-scope fence.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major bf16 tile written by TMA
 // with 128-byte swizzle: rows of 128 B (64 values), 8-row atoms of 1 KB.

@@ -51,6 +51,9 @@ struct gemm_seg {
     uint16_t *a_next = nullptr;
     int64_t lda_next = 0;
     float *c_mc = nullptr;       // multicast address: results added into every GPU's copy (NVSwitch reduction)
+    int mc_store = 0;            // with c_mc: stored into every copy instead (an N-shard's all-gather)
+    float *const *c_peers = nullptr;  // the tiles also stored into these (other GPUs' buffers laid out as c)
+    int n_peers = 0;
 };
 
 // How K3 runs one launch: the kernel, its tiles, the order the persistent

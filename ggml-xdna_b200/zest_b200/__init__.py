@@ -43,7 +43,8 @@ class WKey(ctypes.Structure):
 class GemmSeg(ctypes.Structure):
     """zest_gemm_seg: one weight of zest_gemm_segs with its fused epilogue."""
     _fields_ = [("b", _vp), ("ldb", _i64), ("N", _i64), ("mode", _int), ("c", _vp), ("ldc", _i64),
-                ("residual", _vp), ("ldr", _i64), ("a_next", _vp), ("lda_next", _i64), ("c_multicast", _vp)]
+                ("residual", _vp), ("ldr", _i64), ("a_next", _vp), ("lda_next", _i64), ("c_multicast", _vp),
+                ("multicast_store", _int), ("c_peers", _vpp), ("n_peers", _int)]
 
 
 class GemmPlan(ctypes.Structure):

@@ -142,7 +142,20 @@ typedef struct {
                              copies through the NVSwitch (multimem.red), so when every rank's launch has
                              finished each copy holds the sum of the ranks' partial products. The
                              caller zeroes the copies and fences the group before and after */
+    int multicast_store;  /* with c_multicast: 1 stores the results into every copy instead of adding
+                             them (multimem.st): an N-sharded launch writes its slab of output columns
+                             into every GPU's whole [M][N] output (c_multicast points at the slab's
+                             first column), the all-gather done by the NVSwitch as the tiles finish.
+                             The caller fences the group after the launch, before the copies are read */
+    float *const *c_peers; /* NULL, or n_peers pointers, each into another GPU's buffer laid out as c
+                              (mapped into this process, e.g. peer pointers of symmetric memory): the
+                              epilogue stores every tile there too, by TMA, as it stores it into c. An
+                              N-sharded launch's all-gather: c and c_peers point at the slab's first
+                              column of every GPU's whole [M][N] output. The caller fences the group
+                              after the launch, before the copies are read. Plain stores: no multicast */
+    int n_peers;          /* 0 .. ZEST_MAX_PEERS */
 } zest_gemm_seg;
+#define ZEST_MAX_PEERS 7
 
 /* zest_gemm_group with fused epilogues: per weight a residual ADD, or for a
  * fused gate/up weight the down projection's packed input instead of (or

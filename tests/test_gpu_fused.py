@@ -164,3 +164,36 @@ def test_gemm_segs_rejects_bad_epilogues():
            Z.GemmSeg(bh.data_ptr(), 64, 512, Z.MODE_F32, None, 0, None, 0, None, 0)]
     for sg in bad:
         assert L.zest_gemm_segs(p(ah), 64, 256, 64, 1, segs(sg), p(err), sp()) != 0
+
+
+def test_gemm_peer_copies_equal_the_output():
+    # an N-shard's all-gather from the epilogue: each tile TMA-stored into up
+    # to 7 further buffers laid out as c (here buffers of this GPU standing in
+    # for the peers' copies), at the slab's column offset in a wider output;
+    # every copy holds the output's bits, and columns outside the slab stay
+    M, N, K, W, off = 900, 768, 512, 1280, 256  # a 768-column slab at column 256 of a 1280-wide output
+    ah, bh = operands(M, N, K, 9)
+    outs = [torch.full((M, W), 7.0, device="cuda") for _ in range(8)]
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    peers = (ctypes.c_void_p * 7)(*[o.data_ptr() + 4 * off for o in outs[1:]])
+    _alive.append(peers)
+    s = segs(Z.GemmSeg(bh.data_ptr(), K, N, Z.MODE_BF16, outs[0].data_ptr() + 4 * off, W, None, 0, None, 0, None, 0,
+                       ctypes.cast(peers, ctypes.POINTER(ctypes.c_void_p)), 7))
+    call("zest_gemm_segs", p(ah), K, M, K, 1, s, p(err))
+    plain = host(Z.gemm(ah, bh, M, N, Z.MODE_BF16))
+    for o in outs:
+        h = host(o)
+        assert np.array_equal(h[:, off:off + N], plain)
+        assert (h[:, :off] == 7.0).all() and (h[:, off + N:] == 7.0).all()
+    assert int(err.item()) == 0
+    # what the epilogue cannot do is refused: peers of a one-CTA launch (M <= 128)
+    # or of an output without TMA stores (rows not 16-byte aligned)
+    L = Z.lib()
+    s = segs(Z.GemmSeg(bh.data_ptr(), K, N, Z.MODE_BF16, outs[0].data_ptr() + 4 * off, W, None, 0, None, 0, None, 0,
+                       ctypes.cast(peers, ctypes.POINTER(ctypes.c_void_p)), 7))
+    assert L.zest_gemm_segs(p(ah), K, 100, K, 1, s, p(err), sp()) != 0
+    assert b"more than 128 rows" in L.zest_last_error()
+    s = segs(Z.GemmSeg(bh.data_ptr(), K, N, Z.MODE_BF16, outs[0].data_ptr() + 4 * off + 4, W, None, 0, None, 0, None,
+                       0, ctypes.cast(peers, ctypes.POINTER(ctypes.c_void_p)), 7))
+    assert L.zest_gemm_segs(p(ah), K, M, K, 1, s, p(err), sp()) != 0
+    assert b"peer copies need" in L.zest_last_error()
