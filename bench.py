@@ -434,12 +434,13 @@ class LayerStep:
         # the whole outputs in symmetric memory: bound to an NVLink multicast
         # object (multicast), or reached through every peer's pointer (peer)
         self.mc, self.mc_why, self.how = {}, None, gather_how if gather else "none"
-        if gather and gather_how in ("multicast", "peer"):
+        if gather and gather_how in ("multicast", "peer", "peer16"):
             import torch.distributed as dist
             try:
                 import torch.distributed._symmetric_memory as symm_mem
                 for name, N, _, _ in w["proj"]:
-                    t = symm_mem.empty((M, N), dtype=torch.float32, device="cuda")
+                    t = symm_mem.empty((M, N), dtype=torch.bfloat16 if gather_how == "peer16" else torch.float32,
+                                       device="cuda")
                     hdl = symm_mem.rendezvous(t, dist.group.WORLD)
                     if gather_how == "multicast" and not hdl.multicast_ptr:
                         raise RuntimeError("no multicast support")
@@ -474,7 +475,13 @@ class LayerStep:
                 for nm, _, K in members:
                     t, _, mcp, ptrs = self.mc[nm]
                     N, off = t.shape[1], 4 * self.slabs[nm][0]
-                    if self.how == "multicast":
+                    if self.how == "peer16":
+                        c16 = (ctypes.c_void_p * world)(*[ptrs[j] + off // 2 for j in range(world)])
+                        self.peer_arrays.append(c16)
+                        segs.append(Z.GemmSeg(self.bh[nm].data_ptr(), K, self.slabs[nm][1], Z.MODE_BF16, None, 0,
+                                              None, 0, None, 0, None, 0, None, 0,
+                                              ctypes.cast(c16, ctypes.POINTER(ctypes.c_void_p)), world, N))
+                    elif self.how == "multicast":
                         segs.append(Z.GemmSeg(self.bh[nm].data_ptr(), K, self.slabs[nm][1], Z.MODE_BF16, None, N,
                                               None, 0, None, 0, mcp + off, 1))
                     else:
@@ -488,6 +495,9 @@ class LayerStep:
     def gather_desc(self) -> str:
         if not self.gather:
             return "none"
+        if self.mc and self.how == "peer16":
+            return ("TMA stores of each launch's tiles in bf16 into every rank's whole bf16 output (peer pointers "
+                    "over NVLink), widened to f32 on every rank after each launch's fence")
         if self.mc and self.how == "multicast":
             return "multimem.st of each launch's tiles into every rank's whole output (NVLink multicast)"
         if self.mc:
@@ -515,7 +525,8 @@ class LayerStep:
             for name, N, _ in members:
                 ref = torch.empty((M, N), dtype=torch.float32, device="cuda")
                 gather_slabs(self.out[name], ref, self.world, N)
-                worst = max(worst, float((ref - self.mc[name][0]).abs().max().item()))
+                got = self.full[name] if self.how == "peer16" else self.mc[name][0]
+                worst = max(worst, float((ref - got).abs().max().item()))
         return worst
 
     def step(self, events=None):
@@ -541,13 +552,29 @@ class LayerStep:
                 events[i][1].record(self.stream)
             if rc:
                 raise Z.ZestError(L.zest_last_error().decode())
-            if self.gather and not self.mc:
+            if self.how == "peer16":
+                # every rank's tiles of this launch are in every bf16 copy once
+                # the fence completes; the widening overlaps the next launch
+                import torch.distributed as dist
+                self.comm.wait_stream(self.stream)
+                with torch.cuda.stream(self.comm):
+                    dist.all_reduce(self.tick)
+                    cs = ctypes.c_void_p(self.comm.cuda_stream)
+                    for name, N, _ in members:
+                        if L.zest_widen_bf16(ctypes.c_void_p(self.mc[name][0].data_ptr()), M * N,
+                                             ctypes.c_void_p(self.full[name].data_ptr()), cs):
+                            raise Z.ZestError(L.zest_last_error().decode())
+            elif self.gather and not self.mc:
                 # the gather of this launch's slabs overlaps the next launch
                 self.comm.wait_stream(self.stream)
                 with torch.cuda.stream(self.comm):
                     for name, N, _ in members:
                         gather_slabs(self.out[name], self.full[name], self.world, N, wire=torch.bfloat16)
-        if self.mc:
+        if self.how == "peer16":
+            import torch.distributed as dist
+            self.stream.wait_stream(self.comm)
+            dist.all_reduce(self.tick)  # every rank has widened its copies before the next step writes them
+        elif self.mc:
             import torch.distributed as dist
             dist.all_reduce(self.tick)  # every rank's tiles are in every copy before the step ends
         elif self.gather:
@@ -1543,7 +1570,7 @@ def main() -> None:
                     help="N>1: N-slabs of every weight with (nshard, the default) or without the NCCL all-gather "
                          "of the output slabs, each GPU its own token chunk (tokens, no collective), or the layer "
                          "as one tensor-parallel block (tp: o/down K-sharded, one all-reduce per row chunk)")
-    ap.add_argument("--gather", choices=["peer", "multicast", "nccl"], default="peer",
+    ap.add_argument("--gather", choices=["peer", "peer16", "multicast", "nccl"], default="peer",
                     help="nshard: the output all-gather from the GEMM epilogue, by TMA stores into every peer's "
                          "copy (default) or multimem.st through NVLink multicast, or by NCCL (also where a rank "
                          "has no symmetric memory)")

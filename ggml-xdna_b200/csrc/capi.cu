@@ -876,6 +876,9 @@ int zest_gemm_segs(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K, in
         g[i].mc_store = z.multicast_store;
         g[i].c_peers = z.c_peers;
         g[i].n_peers = z.n_peers;
+        g[i].c16 = z.c16;
+        g[i].n_c16 = z.n_c16;
+        g[i].ldc16 = z.ldc16;
     }
     return launch_gemm_group(a_bf16, lda, M, K, n, g, err, (cudaStream_t) stream);
 }

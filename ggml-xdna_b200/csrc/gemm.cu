@@ -85,6 +85,7 @@ struct gemm_params {
     float *c_mc;         // or null: the results added (multimem.red) into a multicast buffer [M][ldc]
     int mc_store;        // with c_mc: the results stored (multimem.st) into every copy instead
     int n_peers;         // pair kernel with TMA stores: each tile also stored into this many peers' copies
+    int n_c16;           // pair kernel: each tile stored in bf16 into this many copies (bf16 mode)
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
@@ -461,6 +462,7 @@ constexpr int MAX_PEERS = 7;
 struct pair_maps {
     CUtensorMap b[MAX_SEG], c[MAX_SEG];
     CUtensorMap peer[MAX_SEG][MAX_PEERS];
+    CUtensorMap c16[MAX_SEG][MAX_PEERS + 1];  // bf16 copies: 32 x 32 boxes, 64-byte swizzle
 };
 
 struct pair_params {
@@ -831,8 +833,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 const int64_t col0 = (int64_t) nb * P_BN + ch * 32;
                 if (col0 >= p.N) continue;
-                if (!p.tma_store && !p.c_mc) {
+                if (!p.tma_store && !p.c_mc && !p.n_c16) {
                     bad |= store_chunk(p, r, row, col0);
+                    continue;
+                }
+                if (p.n_c16) {
+                    // the chunk in bf16 (bf16 mode: the rounded values are
+                    // bf16 exactly): 32 rows x 64 bytes, 64-byte swizzle,
+                    // TMA-stored into every copy
+                    uint8_t *buf = epi + (q * NBUF + (ch % NBUF)) * 4096;
+                    if (lane == 0) bulk_wait_read<NBUF - 1>();  // the store NBUF chunks ago has read this buffer
+                    __syncwarp();
+                    float o[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __uint_as_float(r[i]);
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) bf16_round2(o[i], o[i + 1]);
+                    bad |= any_not_finite(o);
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            w[k] = __byte_perm(__float_as_uint(o[8 * u + 2 * k]), __float_as_uint(o[8 * u + 2 * k + 1]),
+                                               0x7632);
+                        *reinterpret_cast<uint4 *>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) =
+                            make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        for (int r2 = 0; r2 < p.n_c16; r2++)
+                            tma_store_2d_hint(&maps.c16[seg][r2], buf, (int32_t) col0, (int32_t) row0, out_pol);
+                        bulk_commit_group();
+                        stored = true;
+                    }
                     continue;
                 }
                 // this warp's 32 rows x 32 columns through a 128-byte-swizzled
@@ -923,7 +958,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (stored) bulk_wait_all();  // every store has landed before the block exits
         bool mc = false;
-        for (int sg = 0; sg < pp.nseg; sg++) mc = mc || pp.seg[sg].c_mc != nullptr || pp.seg[sg].n_peers > 0;
+        for (int sg = 0; sg < pp.nseg; sg++)
+            mc = mc || pp.seg[sg].c_mc != nullptr || pp.seg[sg].n_peers > 0 || pp.seg[sg].n_c16 > 0;
         if (mc) fence_proxy_async_global();  // the peers' copies: TMA's writes ordered before the fence below
         if (mc) asm volatile("fence.acq_rel.sys;" ::: "memory");  // the reductions are performed before we exit
         if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(pp.err, ERR_NOT_FINITE);
@@ -974,6 +1010,20 @@ bool make_tmap_out(CUtensorMap *m, void *base, int64_t rows, int64_t cols, int64
     cuuint32_t estr[2] = { 1, 1 };
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+// A bf16 output [rows][ld] as 32 x 32 tiles, 64-byte swizzle, for the
+// epilogue's bf16 copies.
+bool make_tmap_out16(CUtensorMap *m, void *base, int64_t rows, int64_t cols, int64_t ld) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = { (cuuint64_t) cols, (cuuint64_t) rows };
+    cuuint64_t strides[1] = { (cuuint64_t) ld * 2 };
+    cuuint32_t box[2] = { 32, 32 };
+    cuuint32_t estr[2] = { 1, 1 };
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
            CUDA_SUCCESS;
 }
 
@@ -1154,6 +1204,18 @@ int launch_pair_group(const CUtensorMap &ta, int64_t M, int64_t K, int nseg, con
                     return set_error("gemm: cannot build the TMA descriptor of a peer's copy");
             p.n_peers = g.n_peers;
         }
+        p.n_c16 = 0;
+        if (g.n_c16 > 0) {
+            if (g.mode != MODE_BF16 || g.c || g.c_mc || g.resid || g.n_peers || g.n_c16 > MAX_PEERS + 1 || !g.c16 ||
+                g.ldc16 < g.n_out || g.ldc16 % 8)
+                return set_error("gemm: bf16 copies take a bf16-mode output alone (no f32 output, residual or "
+                                 "peers), at most 8 copies, rows of ldc16 >= the width, a multiple of 8");
+            for (int r = 0; r < g.n_c16; r++)
+                if (!g.c16[r] || ((uintptr_t) g.c16[r] & 15) ||
+                    !make_tmap_out16(&maps.c16[s][r], g.c16[r], M, g.n_out, g.ldc16))
+                    return set_error("gemm: cannot build the TMA descriptor of a bf16 copy");
+            p.n_c16 = g.n_c16;
+        }
         pp.tile0[s] = tiles_n;
         tiles_n += (int) ((g.N + BN_T - 1) / BN_T);
     }
@@ -1220,6 +1282,7 @@ int launch_single(const CUtensorMap &ta, int64_t M, int64_t K, const gemm_seg &g
     CUtensorMap tb;
     if (!make_tmap(&tb, g.b, g.N, K, g.ldb, BN)) return set_error("gemm: cannot build the TMA descriptors");
     gemm_params p;
+    memset(&p, 0, sizeof p);
     p.M = M;
     p.N = g.N;
     p.K = K;
@@ -1274,7 +1337,7 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
             return set_error("gemm: bad output mode");
         const int64_t width = g.mode == MODE_SWIGLU ? g.N / 2 : g.N;
         if (g.n_out <= 0 || g.n_out > width) g.n_out = width;
-        if (!g.c && !g.a_next && !g.c_mc) return set_error("gemm: no output");
+        if (!g.c && !g.a_next && !g.c_mc && !g.n_c16) return set_error("gemm: no output");
         if (g.c_mc && (g.c || g.mode == MODE_SWIGLU || g.resid || g.a_next || g.ldc < g.n_out))
             return set_error("gemm: a multicast output takes fp32 or bf16 results alone, rows of ldc >= the width");
         if (g.c && g.ldc < g.n_out) return set_error("gemm: ldc smaller than the output width");
@@ -1292,7 +1355,8 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
     if (!make_tmap(&ta, a_bf16, M, K, lda, BM)) return set_error("gemm: cannot build the TMA descriptors");
     if (!gp.pair) {
         for (int s = 0; s < nseg; s++)
-            if (segs[s].n_peers > 0) return set_error("gemm: peer copies need more than 128 rows (the pair kernel)");
+            if (segs[s].n_peers > 0 || segs[s].n_c16 > 0)
+                return set_error("gemm: peer and bf16 copies need more than 128 rows (the pair kernel)");
         for (int s = 0; s < nseg; s++)
             if (launch_single(ta, M, K, segs[s], err_flag, st)) return -1;
         return 0;

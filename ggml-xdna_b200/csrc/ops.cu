@@ -9,6 +9,7 @@
 #include "zest_device.cuh"
 #include "zest_internal.h"
 
+#include <algorithm>
 #include <cmath>
 
 namespace zest {
@@ -123,6 +124,22 @@ __global__ void rope_kernel(const float *__restrict__ x, int64_t T, int64_t head
 
 using namespace zest;
 
+// bf16 -> f32, exact: 8 values a thread (one 16-byte load, two 16-byte
+// stores), grid-stride; the ragged tail one value a thread.
+__global__ void widen_bf16_kernel(const uint16_t *__restrict__ src, int64_t n, float *__restrict__ dst) {
+    const int64_t n8 = n / 8;
+    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n8; i += (int64_t) gridDim.x * blockDim.x) {
+        const uint4 h = reinterpret_cast<const uint4 *>(src)[i];
+        float4 *d = reinterpret_cast<float4 *>(dst) + 2 * i;
+        d[0] = make_float4(__uint_as_float(h.x << 16), __uint_as_float(h.x & 0xffff0000u), __uint_as_float(h.y << 16),
+                           __uint_as_float(h.y & 0xffff0000u));
+        d[1] = make_float4(__uint_as_float(h.z << 16), __uint_as_float(h.z & 0xffff0000u), __uint_as_float(h.w << 16),
+                           __uint_as_float(h.w & 0xffff0000u));
+    }
+    const int64_t t = 8 * n8 + blockIdx.x * (int64_t) blockDim.x + threadIdx.x;
+    if (t < n) dst[t] = __uint_as_float((uint32_t) src[t] << 16);
+}
+
 extern "C" {
 
 int zest_rms_norm(const float *x, int64_t rows, int64_t d, float eps, float *y, void *stream) {
@@ -145,6 +162,14 @@ int zest_add(const float *x, const float *b, int bias_row, int64_t rows, int64_t
     if (bias_row) binary_kernel<2><<<blocks_for(n, 256), 256, 0, (cudaStream_t) stream>>>(x, b, n, d, y);
     else binary_kernel<1><<<blocks_for(n, 256), 256, 0, (cudaStream_t) stream>>>(x, b, n, d, y);
     return check_launch("zest_add");
+}
+
+int zest_widen_bf16(const uint16_t *src, int64_t n, float *dst, void *stream) {
+    if (n <= 0) return 0;
+    if (!src || !dst || ((uintptr_t) src & 15) || ((uintptr_t) dst & 15))
+        return set_error("zest_widen_bf16: src and dst must be 16-byte aligned");
+    widen_bf16_kernel<<<blocks_for(std::max<int64_t>(1, n / 8), 256), 256, 0, (cudaStream_t) stream>>>(src, n, dst);
+    return check_launch("zest_widen_bf16");
 }
 
 int zest_scale(const float *x, int64_t n, float s, float bias, float *y, void *stream) {

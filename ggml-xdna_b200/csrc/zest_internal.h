@@ -54,6 +54,9 @@ struct gemm_seg {
     int mc_store = 0;            // with c_mc: stored into every copy instead (an N-shard's all-gather)
     float *const *c_peers = nullptr;  // the tiles also stored into these (other GPUs' buffers laid out as c)
     int n_peers = 0;
+    uint16_t *const *c16 = nullptr;   // bf16 copies of the tiles (bf16 mode): [M][ldc16] each
+    int n_c16 = 0;
+    int64_t ldc16 = 0;
 };
 
 // How K3 runs one launch: the kernel, its tiles, the order the persistent

@@ -44,7 +44,8 @@ class GemmSeg(ctypes.Structure):
     """zest_gemm_seg: one weight of zest_gemm_segs with its fused epilogue."""
     _fields_ = [("b", _vp), ("ldb", _i64), ("N", _i64), ("mode", _int), ("c", _vp), ("ldc", _i64),
                 ("residual", _vp), ("ldr", _i64), ("a_next", _vp), ("lda_next", _i64), ("c_multicast", _vp),
-                ("multicast_store", _int), ("c_peers", _vpp), ("n_peers", _int)]
+                ("multicast_store", _int), ("c_peers", _vpp), ("n_peers", _int),
+                ("c16", _vpp), ("n_c16", _int), ("ldc16", _i64)]
 
 
 class GemmPlan(ctypes.Structure):
@@ -111,6 +112,7 @@ def lib() -> ctypes.CDLL:
         "zest_wait_weights": (_int, [_vp]),
         "zest_mul_mat": (_int, [_vp, ctypes.POINTER(WKey), _int, _vp, _i64, _vp, _int]),
         "zest_mul_mat_group": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, _i64, _vpp, _int]),
+        "zest_widen_bf16": (_int, [_vp, _i64, _vp, _vp]),
         "zest_submit_group": (_int, [_vp, _int, _int, ctypes.POINTER(WKey), _intp, _vp, _i64, _vpp, _int]),
         "zest_wait_group": (_int, [_vp, _int]),
         "zest_mul_mat_group_ex": (_int, [_vp, _int, ctypes.POINTER(WKey), _intp, _vp, ctypes.c_float, _vp, _vp, _vp,
@@ -130,7 +132,7 @@ def exported_symbols() -> list[str]:
                         "zest_convert_weight", "zest_convert_gate_up", "zest_gemm", "zest_gemm_group",
                         "zest_gemm_segs", "zest_plan_gemm", "zest_mul_mat_noalloc",
                         "zest_rms_norm", "zest_mul_row", "zest_add", "zest_scale", "zest_glu", "zest_rope_table",
-                        "zest_rope", "zest_pack_rms_norm", "zest_norm_rope",
+                        "zest_rope", "zest_pack_rms_norm", "zest_norm_rope", "zest_widen_bf16",
                         "zest_usable", "zest_open",
                         "zest_close", "zest_set_out16", "zest_has_weight", "zest_add_weight", "zest_add_fused",
                         "zest_add_weight_values",

@@ -154,8 +154,23 @@ typedef struct {
                               column of every GPU's whole [M][N] output. The caller fences the group
                               after the launch, before the copies are read. Plain stores: no multicast */
     int n_peers;          /* 0 .. ZEST_MAX_PEERS */
+    uint16_t *const *c16; /* NULL, or (ZEST_MODE_BF16 only, whose results are bf16 values) n_c16 buffers
+                             [M][ldc16] of bf16, this GPU's or other GPUs' (mapped into this process):
+                             the epilogue TMA-stores every tile there in bf16, half the bytes of f32.
+                             c may then be NULL. An N-sharded launch's all-gather at half the link
+                             bytes: each pointer at the slab's first column of a GPU's whole bf16
+                             output, which zest_widen_bf16 turns into ggml's f32 after the group's
+                             fence. Plain stores: no multicast */
+    int n_c16;            /* 0 .. ZEST_MAX_PEERS + 1 */
+    int64_t ldc16;        /* a multiple of 8 */
 } zest_gemm_seg;
 #define ZEST_MAX_PEERS 7
+
+/* dst[i] = the f32 value of the bf16 src[i] (exact), i < n: gathered bf16
+ * results back into ggml's f32. src and dst 16-byte aligned.
+ * Replaces: the f32 rows the reference's read-back writes (bfp16_c16_row,
+ * src/npu/bfp16_pack.cpp:213-229) from the NPU's bf16 output. */
+int zest_widen_bf16(const uint16_t *src, int64_t n, float *dst, void *stream);
 
 /* zest_gemm_group with fused epilogues: per weight a residual ADD, or for a
  * fused gate/up weight the down projection's packed input instead of (or

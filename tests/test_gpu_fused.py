@@ -197,3 +197,39 @@ def test_gemm_peer_copies_equal_the_output():
                        0, ctypes.cast(peers, ctypes.POINTER(ctypes.c_void_p)), 7))
     assert L.zest_gemm_segs(p(ah), K, M, K, 1, s, p(err), sp()) != 0
     assert b"peer copies need" in L.zest_last_error()
+
+
+def test_gemm_bf16_copies_widen_to_the_output():
+    # the N-shard's half-bytes all-gather: each tile TMA-stored in bf16 into up
+    # to 8 buffers (here this GPU's, standing in for every GPU's whole bf16
+    # output) at the slab's column offset; widened back to f32 they hold the
+    # bf16-mode output's bits, and the columns outside the slab stay
+    M, N, K, W, off = 900, 768, 512, 1280, 256
+    ah, bh = operands(M, N, K, 11)
+    fill = torch.tensor([7.0], dtype=torch.bfloat16).view(torch.int16).item()
+    c16 = [torch.full((M, W), fill, dtype=torch.int16, device="cuda") for _ in range(8)]
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ptrs = (ctypes.c_void_p * 8)(*[c.data_ptr() + 2 * off for c in c16])
+    _alive.append(ptrs)
+    cp = ctypes.cast(ptrs, ctypes.POINTER(ctypes.c_void_p))
+    s = segs(Z.GemmSeg(bh.data_ptr(), K, N, Z.MODE_BF16, None, 0, None, 0, None, 0, None, 0, None, 0, cp, 8, W))
+    call("zest_gemm_segs", p(ah), K, M, K, 1, s, p(err))
+    plain = host(Z.gemm(ah, bh, M, N, Z.MODE_BF16))
+    for c in c16:
+        wide = torch.empty((M, W), device="cuda")
+        call("zest_widen_bf16", p(c), M * W, p(wide))
+        h = host(wide)
+        assert np.array_equal(h[:, off:off + N].view(np.uint32), plain.view(np.uint32))
+        assert (h[:, :off] == 7.0).all() and (h[:, off + N:] == 7.0).all()
+    assert int(err.item()) == 0
+    # a ragged length widens exactly too
+    x = torch.randn(1003, device="cuda").to(torch.bfloat16)
+    y = torch.empty(1003, device="cuda")
+    call("zest_widen_bf16", p(x), 1003, p(y))
+    assert torch.equal(y, x.float())
+    # bf16 copies of fp32-mode results, or beside an f32 output, are refused
+    L = Z.lib()
+    for mode, c in ((Z.MODE_F32, None), (Z.MODE_BF16, c16[0].data_ptr())):
+        s = segs(Z.GemmSeg(bh.data_ptr(), K, N, mode, c, W, None, 0, None, 0, None, 0, None, 0, cp, 8, W))
+        assert L.zest_gemm_segs(p(ah), K, M, K, 1, s, p(err), sp()) != 0
+        assert b"bf16 copies take" in L.zest_last_error()
