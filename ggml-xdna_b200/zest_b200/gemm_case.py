@@ -22,6 +22,9 @@ SHAPES = {
     "C5 m2048 gu": (2048, [10752, 10752], 2048), "C5 m2048 down": (2048, [2048], 10752),
     "C4 m2048 qkv": (2048, [6144, 1024, 1024], 5120), "C4 m2048 gu": (2048, [17408, 17408], 5120),
     "C4 m2048 down": (2048, [5120], 17408),
+    # not a config's launch: one k-block, so the epilogue is nearly all of the
+    # launch (8192 x 8192 f32 out), for profiling the epilogue alone
+    "K64 probe": (8192, [8192], 64),
 }
 
 
