@@ -403,7 +403,7 @@ class LayerStep:
     side stream while the next launch runs."""
 
     def __init__(self, w: dict, raws: dict, world: int, rank: int, nshard: bool, gather: bool, Z, torch,
-                 gather_how: str = "multicast"):
+                 gather_how: str = "peer16"):
         from zest_b200.shard import any_rank, shard_rows, slab_width
         self.w, self.world, self.nshard, self.gather, self.Z, self.torch = w, world, nshard, gather, Z, torch
         M, qt = w["M"], w["qtype"]
@@ -1570,10 +1570,10 @@ def main() -> None:
                     help="N>1: N-slabs of every weight with (nshard, the default) or without the NCCL all-gather "
                          "of the output slabs, each GPU its own token chunk (tokens, no collective), or the layer "
                          "as one tensor-parallel block (tp: o/down K-sharded, one all-reduce per row chunk)")
-    ap.add_argument("--gather", choices=["peer", "peer16", "multicast", "nccl"], default="peer",
-                    help="nshard: the output all-gather from the GEMM epilogue, by TMA stores into every peer's "
-                         "copy (default) or multimem.st through NVLink multicast, or by NCCL (also where a rank "
-                         "has no symmetric memory)")
+    ap.add_argument("--gather", choices=["peer16", "peer", "multicast", "nccl"], default="peer16",
+                    help="nshard: the output all-gather from the GEMM epilogue, by TMA stores into every GPU's "
+                         "copy in bf16 then widened (peer16, the default) or in f32 (peer), or by multimem.st "
+                         "through NVLink multicast, or by NCCL (also where a rank has no symmetric memory)")
     ap.add_argument("--tp-chunks", type=int, default=1, help="tp with NCCL: row chunks whose all-reduce overlaps the next")
     ap.add_argument("--tp-reduce", choices=["multicast", "nccl"], default="nccl",
                     help="tp: K-sharded partials summed by NCCL, or in the GEMM epilogue through NVLink multicast "
