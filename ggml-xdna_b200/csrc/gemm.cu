@@ -1346,6 +1346,22 @@ int launch_gemm_group(const uint16_t *a_bf16, int64_t lda, int64_t M, int64_t K,
         if (g.a_next && (g.mode != MODE_SWIGLU || g.n_out % 8 || g.lda_next < g.n_out || g.lda_next % 8 ||
                          ((uintptr_t) g.a_next & 15)))
             return set_error("gemm: the next operand needs SwiGLU, a width of 8s and 16-byte aligned rows");
+        if (g.n_peers < 0 || g.n_peers > MAX_PEERS || (g.n_peers && !g.c_peers))
+            return set_error("gemm: 0 to 7 peer copies, given by pointer");
+        if (g.n_peers && (g.mode == MODE_SWIGLU || !g.c || g.ldc % 4 || ((uintptr_t) g.c & 15)))
+            return set_error("gemm: peer copies need a TMA-stored output (fp32 or bf16, 16-byte aligned rows) "
+                             "and at most 7 peers");
+        for (int r = 0; r < g.n_peers; r++)
+            if (!g.c_peers[r] || ((uintptr_t) g.c_peers[r] & 15))
+                return set_error("gemm: a peer's copy must be 16-byte aligned");
+        if (g.n_c16 < 0 || g.n_c16 > MAX_PEERS + 1 ||
+            (g.n_c16 && (g.mode != MODE_BF16 || g.c || g.c_mc || g.resid || g.n_peers || !g.c16 ||
+                         g.ldc16 < g.n_out || g.ldc16 % 8)))
+            return set_error("gemm: bf16 copies take a bf16-mode output alone (no f32 output, residual or "
+                             "peers), at most 8 copies, rows of ldc16 >= the width, a multiple of 8");
+        for (int r = 0; r < g.n_c16; r++)
+            if (!g.c16[r] || ((uintptr_t) g.c16[r] & 15))
+                return set_error("gemm: a bf16 copy must be 16-byte aligned");
     }
     int64_t Ns[MAX_SEG];
     for (int s = 0; s < nseg; s++) Ns[s] = segs[s].N;

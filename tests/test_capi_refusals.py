@@ -109,3 +109,34 @@ def test_service_refuses_without_a_service():
     refused(L.zest_submit_group(None, 0, 1, ctypes.byref(key), None, None, 10, None, 0), "no service")
     refused(L.zest_wait_group(None, 0), "no service")
     refused(L.zest_load_iq3s_grid(None), "no table")
+
+
+def ptrs(*vals):
+    arr = (vp * len(vals))(*vals)
+    ptrs._alive.append(arr)
+    return ctypes.cast(arr, ctypes.POINTER(vp))
+
+
+ptrs._alive = []
+
+
+def test_epilogue_copies_refuse_what_the_epilogue_cannot_store():
+    # peer copies (an N-shard's all-gather in f32): a TMA-stored output, 0..7 aligned peers
+    refused(segs(seg(c_peers=ptrs(P), n_peers=8)), "0 to 7 peer copies")
+    refused(segs(seg(c_peers=None, n_peers=1)), "0 to 7 peer copies")
+    refused(segs(seg(c=None, c_multicast=P, c_peers=ptrs(P), n_peers=1)), "peer copies need")
+    refused(segs(seg(ldc=513, c_peers=ptrs(P), n_peers=1)), "peer copies need")
+    refused(segs(seg(c_peers=ptrs(ODD), n_peers=1)), "16-byte aligned")
+    # bf16 copies (the all-gather in bf16): bf16-mode results alone, 1..8 aligned copies
+    refused(segs(seg(c=None, c16=ptrs(P), n_c16=1, ldc16=512, mode=Z.MODE_F32)), "bf16 copies take")
+    refused(segs(seg(c16=ptrs(P), n_c16=1, ldc16=512)), "bf16 copies take")  # beside an f32 output
+    refused(segs(seg(c=None, c16=ptrs(*[P] * 9), n_c16=9, ldc16=512)), "bf16 copies take")
+    refused(segs(seg(c=None, c16=ptrs(P), n_c16=1, ldc16=500)), "bf16 copies take")
+    refused(segs(seg(c=None, c16=ptrs(ODD), n_c16=1, ldc16=512)), "16-byte aligned")
+
+
+def test_widen_refuses_unaligned_buffers():
+    L = Z.lib()
+    refused(L.zest_widen_bf16(vp(ODD), 100, vp(P), None), "16-byte aligned")
+    refused(L.zest_widen_bf16(vp(P), 100, vp(ODD), None), "16-byte aligned")
+    assert L.zest_widen_bf16(vp(ODD), 0, vp(ODD), None) == 0  # nothing to do
