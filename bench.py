@@ -504,10 +504,11 @@ class LayerStep:
             return "TMA stores of each launch's tiles into every rank's whole output (peer pointers over NVLink)"
         return "NCCL all-gather of the slabs, bf16 on the wire" + (f" (multicast: {self.mc_why})" if self.mc_why else "")
 
-    def check_multicast(self) -> float:
-        """The multicast outputs against the NCCL all-gather of the same slabs
-        computed into local buffers: the largest difference over this rank's
-        outputs (0 when they agree bit for bit). Collective."""
+    def check_gather(self) -> float:
+        """The outputs gathered by the GEMM epilogue (multicast, peer or bf16
+        peer stores) against the NCCL all-gather of the same slabs computed
+        into local buffers: the largest difference over this rank's outputs
+        (0 when they agree bit for bit). Collective."""
         import torch.distributed as dist
         from zest_b200.shard import gather_slabs
         torch, Z, L = self.torch, self.Z, self.Z.lib()
@@ -651,9 +652,9 @@ def run_ours(args, w: dict) -> None:
     gather_desc = layer.gather_desc()
     if layer.mc:
         from zest_b200.shard import any_rank
-        worst = layer.check_multicast()
+        worst = layer.check_gather()
         if any_rank(not worst == 0.0):
-            raise Z.ZestError(f"multicast gather differs from NCCL's by {worst} (this rank)")
+            raise Z.ZestError(f"the epilogue's gather differs from NCCL's by {worst} (this rank)")
     del layer
     torch.cuda.empty_cache()
 
