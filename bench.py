@@ -748,6 +748,10 @@ def e2e_run(args, w: dict, raws: dict, Z, torch) -> dict:
     """The same step through the C ABI's matmul service, host (pinned) inputs
     and outputs, host<->device copies inside the timed region."""
     M = w["M"]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 and "GGML_ZEST_HOST_THREADS" not in os.environ:
+        # the ranks share the host's cores: each service's widening pool takes its share
+        os.environ["GGML_ZEST_HOST_THREADS"] = str(max(1, (os.cpu_count() or 1) // world))
     npu = Z.Npu(torch.cuda.current_device())
     keys = {}
     for name, N, K, _ in w["proj"]:
